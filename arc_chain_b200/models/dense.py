@@ -1,0 +1,193 @@
+"""Device-resident dense INT8 decoder weights (Llama-style MHA/GQA).
+
+Fusions done once at load time (exact: they only concatenate output rows):
+* ``wqkv`` = [wq; wk; wv] rows, one GEMM for the three projections
+  (cached_integer_model.rs:1425-1427 runs them on the same normed input);
+* ``wgu``  = [gate; up] rows (1491-1492);
+Each matrix keeps its own per-row i64 scales, so every output element is
+computed exactly as the reference's ``matmul_i8_into`` computes it.
+
+Tensor-parallel sharding (``tp_rank``/``tp_size``) is Megatron-style: q/k/v
+and gate/up are split by output rows (whole heads / whole FFN rows), wo and
+down by input columns, the LM head by vocab rows.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import numpy as np
+import torch
+
+from arc_chain_b200.formats import gen
+from arc_chain_b200.formats.arc_int8 import Int8Model, LAYER_MATS
+from arc_chain_b200.models.config import ModelConfig
+from arc_chain_b200.ops import int_ops as ops
+
+
+@dataclass
+class Linear:
+    w: torch.Tensor          # int8 [M, K]
+    s: torch.Tensor          # int64 [M]
+    tmap: ops.TensorMap = None
+
+    @property
+    def M(self):
+        return self.w.shape[0]
+
+    @property
+    def K(self):
+        return self.w.shape[1]
+
+    def build_map(self):
+        self.tmap = ops.TensorMap(self.w, ops.BM)
+        return self
+
+
+@dataclass
+class DenseLayer:
+    qkv: Linear
+    wo: Linear
+    gu: Linear
+    down: Linear
+    attn_norm: torch.Tensor
+    ffn_norm: torch.Tensor
+
+
+@dataclass
+class DenseModel:
+    cfg: ModelConfig
+    attn_scale: int
+    emb: torch.Tensor
+    emb_s: torch.Tensor
+    lm: Linear
+    final_norm: torch.Tensor
+    rope_cos: torch.Tensor
+    rope_sin: torch.Tensor
+    layers: List[DenseLayer]
+    tp_rank: int = 0
+    tp_size: int = 1
+    vocab_offset: int = 0
+    weight_hash: Optional[bytes] = None
+
+    @property
+    def n_heads_local(self):
+        return self.cfg.n_heads // self.tp_size
+
+    @property
+    def n_kv_local(self):
+        return self.cfg.n_kv_heads // self.tp_size
+
+    @property
+    def d_ff_local(self):
+        return self.cfg.d_ff // self.tp_size
+
+    @property
+    def vocab_local(self):
+        return self.lm.M
+
+
+def _shard_rows(a, rank, size):
+    n = a.shape[0] // size
+    return a[rank * n:(rank + 1) * n]
+
+
+def _shard_cols(a, rank, size):
+    n = a.shape[1] // size
+    return a[:, rank * n:(rank + 1) * n]
+
+
+def _vocab_range(V, rank, size):
+    per = (V + size - 1) // size
+    lo = min(V, rank * per)
+    return lo, min(V, lo + per)
+
+
+def check_tp(cfg: ModelConfig, tp: int):
+    if cfg.n_heads % tp or cfg.n_kv_heads % tp or cfg.d_ff % tp:
+        raise ValueError(f"{cfg.name}: heads {cfg.n_heads}/{cfg.n_kv_heads} and d_ff {cfg.d_ff} must divide by tp={tp}")
+    if (cfg.d_ff // tp) % 16 or (cfg.d_model // tp) % 16:
+        raise ValueError("sharded K must stay a multiple of 16 bytes (TMA row stride)")
+
+
+def from_host(m: Int8Model, device, tp_rank: int = 0, tp_size: int = 1) -> DenseModel:
+    """Upload an Int8Model (numpy) to the device, sharded for TP."""
+    c = m.cfg
+    check_tp(c, tp_size)
+    dev = torch.device(device)
+    T = lambda a, dt=None: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    dh = c.d_head
+    layers = []
+    for L in m.layers:
+        r, s_ = tp_rank, tp_size
+        wq, wk, wv = (_shard_rows(L[n], r, s_) for n in ("wq", "wk", "wv"))
+        sq, sk, sv = (_shard_rows(L[n + "_s"], r, s_) for n in ("wq", "wk", "wv"))
+        qkv = Linear(T(np.concatenate([wq, wk, wv])), T(np.concatenate([sq, sk, sv])))
+        wo = Linear(T(_shard_cols(L["wo"], r, s_)), T(L["wo_s"]))
+        gu = Linear(T(np.concatenate([_shard_rows(L["gate"], r, s_), _shard_rows(L["up"], r, s_)])),
+                    T(np.concatenate([_shard_rows(L["gate_s"], r, s_), _shard_rows(L["up_s"], r, s_)])))
+        down = Linear(T(_shard_cols(L["down"], r, s_)), T(L["down_s"]))
+        layers.append(DenseLayer(qkv.build_map(), wo.build_map(), gu.build_map(), down.build_map(),
+                                 T(L["attn_norm"]), T(L["ffn_norm"])))
+    lo, hi = _vocab_range(c.vocab, tp_rank, tp_size)
+    lm = Linear(T(m.out[lo:hi]), T(m.out_s[lo:hi])).build_map()
+    return DenseModel(c, int(m.attn_scale), T(m.emb), T(m.emb_s), lm, T(m.final_norm), T(m.rope_cos),
+                      T(m.rope_sin), layers, tp_rank, tp_size, lo)
+
+
+def random_device(cfg: ModelConfig, device, seed: int = 0, tp_rank: int = 0, tp_size: int = 1) -> DenseModel:
+    """Seeded random-init model generated directly on the device (identical
+    values to :func:`arc_chain_b200.formats.gen.random_model`)."""
+    check_tp(cfg, tp_size)
+    dev = torch.device(device)
+    d, dkv, dff, V = cfg.d_model, cfg.d_kv, cfg.d_ff, cfg.vocab
+    r, s_ = tp_rank, tp_size
+
+    def mat_rows(tid, rows, cols, lo, hi, out=None):
+        """rows [lo, hi) of the seeded matrix `tid` (data, scales)."""
+        full = torch.empty(rows * cols, dtype=torch.int8, device=dev) if out is None else out
+        ops.rng_i8(seed, tid << 2, full)
+        full = full.view(rows, cols)
+        sc = gen.row_scales(seed, (tid << 2) | 1, rows, gen.scale_base(cols))
+        return full[lo:hi], torch.from_numpy(sc[lo:hi]).to(dev)
+
+    def rows_of(tid, rows, cols):
+        n = rows // s_
+        w, sc = mat_rows(tid, rows, cols, r * n, (r + 1) * n)
+        return w.contiguous(), sc
+
+    def cols_of(tid, rows, cols):
+        w, sc = mat_rows(tid, rows, cols, 0, rows)
+        n = cols // s_
+        return w[:, r * n:(r + 1) * n].contiguous(), sc
+
+    layers = []
+    for l in range(cfg.n_layers):
+        tid = lambda j: gen.layer_tensor_id(l, j)
+        wq, sq = rows_of(tid(0), d, d)
+        wk, sk = rows_of(tid(1), dkv, d)
+        wv, sv = rows_of(tid(2), dkv, d)
+        qkv = Linear(torch.cat([wq, wk, wv]), torch.cat([sq, sk, sv]))
+        del wq, wk, wv
+        wo, so = cols_of(tid(3), d, d)
+        wg, sg = rows_of(tid(4), dff, d)
+        wu, su = rows_of(tid(5), dff, d)
+        gu = Linear(torch.cat([wg, wu]), torch.cat([sg, su]))
+        del wg, wu
+        wd, sd = cols_of(tid(6), d, dff)
+        an = torch.from_numpy(gen.gamma(seed, (tid(7) << 2) | 1, d)).to(dev)
+        fn = torch.from_numpy(gen.gamma(seed, (tid(8) << 2) | 1, d)).to(dev)
+        layers.append(DenseLayer(qkv.build_map(), Linear(wo, so).build_map(), gu.build_map(),
+                                 Linear(wd, sd).build_map(), an, fn))
+    emb = torch.empty(V * d, dtype=torch.int8, device=dev)
+    ops.rng_i8(seed, 0 << 2, emb)
+    emb = emb.view(V, d)
+    emb_s = torch.from_numpy(gen.row_scales(seed, (0 << 2) | 1, V, gen.EMB_SCALE_BASE)).to(dev)
+    lo, hi = _vocab_range(V, r, s_)
+    lw, ls = mat_rows(1, V, d, lo, hi)
+    lm = Linear(lw.contiguous(), ls).build_map()
+    fnorm = torch.from_numpy(gen.gamma(seed, (2 << 2) | 1, d)).to(dev)
+    rc, rs = gen.rope_tables(cfg.d_head, cfg.max_seq, cfg.rope_theta)
+    torch.cuda.synchronize(dev)
+    return DenseModel(cfg, cfg.resolved_attn_scale(), emb, emb_s, lm, fnorm, torch.from_numpy(rc).to(dev),
+                      torch.from_numpy(rs).to(dev), layers, tp_rank, tp_size, lo)

@@ -1,0 +1,59 @@
+"""Loader for the in-tree sm_100a kernel library (``libarcb_cuda.so``).
+
+There is no fallback: on a machine with a GPU, a missing or unloadable
+library raises.  Kernels launch on the caller's current torch CUDA stream, so
+they compose with torch ops and are captured by CUDA graphs.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+_LIB = None
+_LOCK = threading.Lock()
+
+vp, i32, i64, u64 = C.c_void_p, C.c_int, C.c_int64, C.c_uint64
+
+_SIGS = {
+    "arcb_tmap_i8": (i32, [vp, vp, i64, i64, i32]),
+    "arcb_gemm_bn": (i32, [i32]),
+    "arcb_gemm_i8": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp]),
+    "arcb_embed": (i32, [vp, vp, vp, i32, i32, i32, vp, vp, i32, vp]),
+    "arcb_rmsnorm_limbs": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, vp]),
+    "arcb_finalize": (i32, [vp, i32, i32, vp, vp, vp, i32, i32, vp]),
+    "arcb_finalize_qkv": (i32, [vp, i32, vp, vp, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp, vp, i32, vp, vp]),
+    "arcb_finalize_swiglu": (i32, [vp, i32, i32, vp, vp, vp, vp, vp, vp]),
+    "arcb_attn_decode": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, i32, i64, i32, vp, vp, vp, i32, vp, vp]),
+    "arcb_sample": (i32, [vp, i32, i32, vp, i32, vp, vp, vp, i32, vp, vp, vp, vp, i32, vp]),
+    "arcb_rng_i8": (i32, [u64, u64, vp, i64, vp]),
+}
+
+
+def lib():
+    global _LIB
+    with _LOCK:
+        if _LIB is None:
+            from arc_chain_b200 import _build
+
+            path = os.path.join(_build.LIBDIR, "libarcb_cuda.so")
+            if not os.path.exists(path) or _build._stale(path, _build.cuda_sources() + _build._headers()):
+                path = _build.build_cuda()
+            L = C.CDLL(path)
+            for name, (res, args) in _SIGS.items():
+                f = getattr(L, name)
+                f.restype = res
+                f.argtypes = args
+            _LIB = L
+    return _LIB
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with CUDA error {rc}")
+
+
+def loaded_path() -> str:
+    from arc_chain_b200 import _build
+
+    return os.path.join(_build.LIBDIR, "libarcb_cuda.so")

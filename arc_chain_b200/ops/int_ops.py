@@ -1,0 +1,141 @@
+"""torch-facing wrappers of the sm_100a kernels (one call = one kernel launch).
+
+Every wrapper launches on ``torch.cuda.current_stream()`` and counts its
+launch in :data:`LAUNCHES` so benchmarks can report how many of this
+library's kernels ran in a timed region.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import Optional
+
+import torch
+
+from arc_chain_b200.ops._lib import check, lib
+
+LAUNCHES = [0]
+BM, BK = 128, 128
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _s():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _count():
+    LAUNCHES[0] += 1
+
+
+class TensorMap:
+    """A CUtensorMap (128 bytes, 64-byte aligned host memory) over a 2-D int8
+    tensor [rows, cols], box = {128 bytes of K, box_rows}, 128-byte swizzle."""
+
+    def __init__(self, t: torch.Tensor, box_rows: int):
+        assert t.dtype == torch.int8 and t.dim() == 2 and t.is_contiguous()
+        self._raw = C.create_string_buffer(128 + 64)
+        self.addr = (C.addressof(self._raw) + 63) & ~63
+        self.tensor = t
+        self.rows, self.cols = t.shape
+        self.box_rows = box_rows
+        rc = lib().arcb_tmap_i8(self.addr, t.data_ptr(), self.rows, self.cols, box_rows)
+        if rc != 0:
+            raise RuntimeError(f"cuTensorMapEncodeTiled failed ({rc}) for {tuple(t.shape)} box {box_rows}")
+
+
+def gemm_bn(B: int) -> int:
+    return lib().arcb_gemm_bn(B)
+
+
+def _stages(bn: int) -> int:
+    return 4 if bn >= 256 else (6 if bn >= 128 else 8)
+
+
+def gemm_smem(bn: int) -> int:
+    return 1024 + _stages(bn) * (BM * BK + bn * BK) + (2 * _stages(bn) + 2) * 8 + 16
+
+
+_SMS = [None]
+
+
+def num_sms() -> int:
+    if _SMS[0] is None:
+        _SMS[0] = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return _SMS[0]
+
+
+def choose_ksplit(M: int, K: int, bn: int, n_tiles: int = 1) -> int:
+    """Split-K factor minimising (waves x chunks per CTA) over the SMs."""
+    mt = (M + BM - 1) // BM * n_tiles
+    nch = (K + BK - 1) // BK
+    occ = max(1, (232448 - 1024) // (gemm_smem(bn) + 1024))
+    slots = num_sms() * occ
+    best, best_t = 1, None
+    for ks in range(1, nch + 1):
+        cps = (nch + ks - 1) // ks
+        ks_eff = (nch + cps - 1) // cps
+        waves = (mt * ks_eff + slots - 1) // slots
+        t = waves * (cps + 1.5)  # +1.5 chunks of fixed per-CTA cost
+        if best_t is None or t < best_t - 1e-9:
+            best, best_t = ks_eff, t
+    return best
+
+
+def gemm_i8(wmap: TensorMap, xmap: TensorMap, M: int, K: int, B: int, ksplit: int, lmax: torch.Tensor,
+            P: torch.Tensor, err: torch.Tensor) -> None:
+    _count()
+    check(lib().arcb_gemm_i8(wmap.addr, xmap.addr, M, K, B, xmap.box_rows, ksplit, _p(lmax), _p(P), _p(err), _s()),
+          "gemm_i8")
+
+
+def embed(tokens, emb, emb_s, V, d, B, h, counters):
+    _count()
+    check(lib().arcb_embed(_p(tokens), _p(emb), _p(emb_s), V, d, B, _p(h), _p(counters), counters.numel(), _s()),
+          "embed")
+
+
+def rmsnorm_limbs(h, gamma, d, B, X, lmax, y_out=None):
+    _count()
+    check(lib().arcb_rmsnorm_limbs(_p(h), _p(gamma), gamma.numel(), d, B, _p(X), _p(lmax), _p(y_out), _s()),
+          "rmsnorm_limbs")
+
+
+def finalize(P, M, B, lmax, scales, out, ldo, mode):
+    _count()
+    check(lib().arcb_finalize(_p(P), M, B, _p(lmax), _p(scales), _p(out), ldo, mode, _s()), "finalize")
+
+
+def finalize_qkv(P, B, lmax, scales, n_heads, n_kv, dh, q_out, Kc, Vc, pt, pos, rcos, rsin, max_seq, err):
+    _count()
+    check(lib().arcb_finalize_qkv(_p(P), B, _p(lmax), _p(scales), n_heads, n_kv, dh, _p(q_out), _p(Kc), _p(Vc),
+                                  _p(pt), pt.shape[1], _p(pos), _p(rcos), _p(rsin), max_seq, _p(err), _s()),
+          "finalize_qkv")
+
+
+def finalize_swiglu(P, dff, B, lmax, scales, X, lmax_out, y_out=None):
+    _count()
+    check(lib().arcb_finalize_swiglu(_p(P), dff, B, _p(lmax), _p(scales), _p(X), _p(lmax_out), _p(y_out), _s()),
+          "finalize_swiglu")
+
+
+def attn_decode(q, Kc, Vc, pt, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax, max_T, err, o_out=None):
+    _count()
+    check(lib().arcb_attn_decode(_p(q), _p(Kc), _p(Vc), _p(pt), pt.shape[1], _p(pos), n_heads, n_kv, dh,
+                                 int(attn_scale), B, _p(X), _p(lmax), _p(o_out), max_T, _p(err), _s()),
+          "attn_decode")
+
+
+def sample(logits, V, n, hist, count, gen, tokens_next, pos_inc=None, done=None, eos=None, lrow=None):
+    _count()
+    n_eos = 0 if eos is None else eos.numel()
+    check(lib().arcb_sample(_p(logits), logits.shape[1], V, _p(lrow), n, _p(hist), _p(count), _p(gen),
+                            gen.shape[1], _p(tokens_next), _p(pos_inc), _p(done), _p(eos), n_eos, _s()),
+          "sample")
+
+
+def rng_i8(seed: int, stream: int, out: torch.Tensor) -> None:
+    _count()
+    check(lib().arcb_rng_i8(seed, stream, _p(out), out.numel(), _s()), "rng_i8")

@@ -1,0 +1,256 @@
+"""Decode engine for dense INT8 decoders on B200.
+
+One forward over a batch of *slots* (a slot = one token at one position of
+one request) runs:
+
+    embed -> per layer [RMSNorm+limbs -> QKV GEMM -> finalize+RoPE+KV append
+    -> paged attention (+limbs) -> W_o GEMM -> (TP reduce) -> residual
+    -> RMSNorm+limbs -> gate/up GEMM -> SwiGLU+limbs -> down GEMM
+    -> (TP reduce) -> residual] -> final RMSNorm -> LM head -> (TP gather)
+    -> repetition penalty + argmax
+
+Every output element equals the reference CPU engine's
+(crates/arc-inference/src/cached_integer_model.rs:1381-1516): all reductions
+are exact integer sums, so batching, prefill of many positions at once, split-K
+and tensor-parallel partial sums leave results bit-identical.
+
+``generate`` reproduces the reference's generate loop (1518-1557): BOS=1,
+prompt, then the last prompt token is fed again at step 0, compounding
+repetition penalty over the newest 64 ids, argmax with lowest-index ties, EOS
+kept in the output, output hash = BLAKE3 of the LE u32 ids.  The prompt is
+prefilled in one batched forward (its logits are discarded by the reference,
+so the LM head is skipped there).  Decode steps replay one CUDA graph.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from arc_chain_b200.models.dense import DenseModel
+from arc_chain_b200.ops import int_ops as ops
+from arc_chain_b200.runtime.kv_paged import PAGE, PagedKV
+from arc_chain_b200.utils.hashing import blake3
+import numpy as np
+
+I32, I64, I8 = torch.int32, torch.int64, torch.int8
+
+
+class Comm:
+    """Tensor-parallel hooks; the single-GPU instance does nothing."""
+
+    size = 1
+    rank = 0
+
+    def reduce_partials(self, P: torch.Tensor, rows: int, M: int, lmax: torch.Tensor) -> None:
+        pass
+
+    def gather_logits(self, local: torch.Tensor, full: torch.Tensor, B: int, vocab_offset: int) -> None:
+        pass
+
+    @property
+    def n_launches(self) -> int:
+        return 0
+
+
+class StepBuffers:
+    """Device buffers for a forward over up to B slots."""
+
+    def __init__(self, model: DenseModel, B: int, max_pages: int, gen_cap: int = 0):
+        c = model.cfg
+        dev = model.emb.device
+        self.B = B
+        d, dh = c.d_model, c.d_head
+        dl = model.n_heads_local * dh
+        dffl = model.d_ff_local
+        self.tokens = torch.zeros(B, dtype=I32, device=dev)
+        self.pos = torch.zeros(B, dtype=I32, device=dev)
+        self.pt = torch.zeros(B, max_pages, dtype=I32, device=dev)
+        self.h = torch.zeros(B, d, dtype=I64, device=dev)
+        self.q = torch.zeros(B, dl, dtype=I64, device=dev)
+        self.bn = ops.gemm_bn(B)
+        rows = max(8 * B, self.bn)  # the TMA box never exceeds the tensor
+        self.Xd = torch.zeros(rows, d, dtype=I8, device=dev)
+        self.Xo = torch.zeros(rows, dl, dtype=I8, device=dev)
+        self.Xf = torch.zeros(rows, dffl, dtype=I8, device=dev)
+        self.mXd = ops.TensorMap(self.Xd, self.bn)
+        self.mXo = ops.TensorMap(self.Xo, self.bn)
+        self.mXf = ops.TensorMap(self.Xf, self.bn)
+        L0 = model.layers[0]
+        mmax = max(L0.qkv.M, d, L0.gu.M, model.vocab_local)
+        self.P = torch.zeros(8 * B * mmax, dtype=I32, device=dev)
+        self.cnt = torch.zeros(4 * c.n_layers + 4, dtype=I32, device=dev)
+        self.err = torch.zeros(1, dtype=I32, device=dev)
+        self.logits_local = torch.zeros(B, model.vocab_local, dtype=I64, device=dev)
+        self.logits = self.logits_local if model.tp_size == 1 else torch.zeros(B, c.vocab, dtype=I64, device=dev)
+        # sampling state (one sampled slot per row)
+        self.hist = torch.zeros(B, 64, dtype=I32, device=dev)
+        self.count = torch.zeros(B, dtype=I32, device=dev)
+        self.gen = torch.zeros(B, max(1, gen_cap), dtype=I32, device=dev)
+        self.done = torch.zeros(B, dtype=I32, device=dev)
+        self.eos = torch.zeros(8, dtype=I32, device=dev)
+        self.n_eos = 0
+        # split-K per GEMM for this B
+        self.ks = {
+            "qkv": ops.choose_ksplit(L0.qkv.M, L0.qkv.K, self.bn),
+            "wo": ops.choose_ksplit(L0.wo.M, L0.wo.K, self.bn),
+            "gu": ops.choose_ksplit(L0.gu.M, L0.gu.K, self.bn),
+            "down": ops.choose_ksplit(L0.down.M, L0.down.K, self.bn),
+            "lm": ops.choose_ksplit(model.lm.M, model.lm.K, self.bn),
+        }
+
+
+class Engine:
+    def __init__(self, model: DenseModel, n_pages: Optional[int] = None, max_seq: Optional[int] = None,
+                 comm: Optional[Comm] = None, kv_bytes: Optional[int] = None):
+        self.m = model
+        c = model.cfg
+        self.comm = comm or Comm()
+        self.max_seq = max_seq or c.max_seq
+        self.max_pages = (self.max_seq + PAGE - 1) // PAGE
+        if n_pages is None:
+            per = PagedKV.bytes_per_page(c.n_layers, model.n_kv_local, c.d_head)
+            budget = kv_bytes if kv_bytes is not None else 4 * self.max_pages * per
+            n_pages = max(self.max_pages, budget // per)
+        self.kv = PagedKV(c.n_layers, n_pages, model.n_kv_local, c.d_head, model.emb.device, self.max_pages)
+        self._bufs: Dict[Tuple[int, int], StepBuffers] = {}
+        self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        self._rid = 0
+
+    # ------------------------------------------------------------------ buffers
+    def buffers(self, B: int, gen_cap: int = 0) -> StepBuffers:
+        key = (B, gen_cap)
+        if key not in self._bufs:
+            self._bufs[key] = StepBuffers(self.m, B, self.max_pages, gen_cap)
+        return self._bufs[key]
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, bb: StepBuffers, B: int, with_logits: bool = True) -> None:
+        """One forward over slots 0..B-1 of `bb` (tokens/pos/pt already set)."""
+        m, c, cm = self.m, self.m.cfg, self.comm
+        d, dh = c.d_model, c.d_head
+        nh, nkv = m.n_heads_local, m.n_kv_local
+        dl, dffl = nh * dh, m.d_ff_local
+        assert B == bb.B, "a StepBuffers instance serves exactly B slots (tensor maps are sized for it)"
+        ops.embed(bb.tokens, m.emb, m.emb_s, c.vocab, d, B, bb.h, bb.cnt)
+        for l, Ly in enumerate(m.layers):
+            c0, c1, c2, c3 = (bb.cnt[4 * l + i:4 * l + i + 1] for i in range(4))
+            ops.rmsnorm_limbs(bb.h, Ly.attn_norm, d, B, bb.Xd, c0)
+            ops.gemm_i8(Ly.qkv.tmap, bb.mXd, Ly.qkv.M, Ly.qkv.K, B, bb.ks["qkv"], c0, bb.P, bb.err)
+            ops.finalize_qkv(bb.P, B, c0, Ly.qkv.s, nh, nkv, dh, bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos,
+                             m.rope_cos, m.rope_sin, self.max_seq, bb.err)
+            ops.attn_decode(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo,
+                            c1, self.max_seq, bb.err)
+            ops.gemm_i8(Ly.wo.tmap, bb.mXo, Ly.wo.M, Ly.wo.K, B, bb.ks["wo"], c1, bb.P, bb.err)
+            cm.reduce_partials(bb.P, 8 * B, d, c1)
+            ops.finalize(bb.P, d, B, c1, Ly.wo.s, bb.h, d, 1)
+            ops.rmsnorm_limbs(bb.h, Ly.ffn_norm, d, B, bb.Xd, c2)
+            ops.gemm_i8(Ly.gu.tmap, bb.mXd, Ly.gu.M, Ly.gu.K, B, bb.ks["gu"], c2, bb.P, bb.err)
+            ops.finalize_swiglu(bb.P, dffl, B, c2, Ly.gu.s, bb.Xf, c3)
+            ops.gemm_i8(Ly.down.tmap, bb.mXf, Ly.down.M, Ly.down.K, B, bb.ks["down"], c3, bb.P, bb.err)
+            cm.reduce_partials(bb.P, 8 * B, d, c3)
+            ops.finalize(bb.P, d, B, c3, Ly.down.s, bb.h, d, 1)
+        if with_logits:
+            cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
+            ops.rmsnorm_limbs(bb.h, m.final_norm, d, B, bb.Xd, cf)
+            ops.gemm_i8(m.lm.tmap, bb.mXd, m.lm.M, m.lm.K, B, bb.ks["lm"], cf, bb.P, bb.err)
+            ops.finalize(bb.P, m.lm.M, B, cf, m.lm.s, bb.logits_local, m.lm.M, 0)
+            cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset)
+
+    def decode_step(self, bb: StepBuffers) -> None:
+        """forward + sample for every slot; slots advance in place."""
+        self.forward(bb, bb.B, True)
+        ops.sample(bb.logits, self.m.cfg.vocab, bb.B, bb.hist, bb.count, bb.gen, bb.tokens, pos_inc=bb.pos,
+                   done=bb.done, eos=bb.eos[:max(1, bb.n_eos)] if bb.n_eos else None)
+
+    def capture(self, bb: StepBuffers) -> torch.cuda.CUDAGraph:
+        """Capture one decode step of `bb` into a CUDA graph (after a warm-up
+        step has run eagerly, so kernel attributes are already set)."""
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self.decode_step(bb)
+        torch.cuda.current_stream().wait_stream(s)
+        return g
+
+    # ------------------------------------------------------------------ requests
+    def new_request(self, n_tokens: int) -> int:
+        rid = self._rid
+        self._rid += 1
+        self.kv.reserve(rid, n_tokens)
+        return rid
+
+    def prefill(self, rid: int, tokens: Sequence[int], start_pos: int = 0, chunk: int = 1024) -> None:
+        """Write KV for `tokens` at positions start_pos.. (logits discarded)."""
+        row = torch.tensor(self.kv.table_row(rid), dtype=I32)
+        for s in range(0, len(tokens), chunk):
+            part = list(tokens[s:s + chunk])
+            B = len(part)
+            bb = self.buffers(B)
+            bb.tokens.copy_(torch.tensor(part, dtype=I32))
+            bb.pos.copy_(torch.arange(start_pos + s, start_pos + s + B, dtype=I32))
+            bb.pt.copy_(row.unsqueeze(0).expand(B, -1))
+            self.forward(bb, B, with_logits=False)
+
+    def generate(self, prompt: Sequence[int], max_tokens: int, eos: Sequence[int] = (),
+                 use_graph: bool = True) -> Tuple[List[int], bytes]:
+        """Single-stream greedy generate, bit-identical to the reference."""
+        prompt = [int(t) for t in prompt]
+        n = len(prompt)
+        rid = self.new_request(1 + n + max_tokens)
+        try:
+            self.prefill(rid, [1] + prompt)
+            toks = self._decode_loop(rid, prompt[-1] if n else 0, n + 1, max_tokens, eos, use_graph)
+        finally:
+            self.kv.release(rid)
+        return toks, blake3(np.asarray(toks, dtype="<u4").tobytes())
+
+    def _decode_loop(self, rid, first_tok, first_pos, max_tokens, eos, use_graph) -> List[int]:
+        bb = self.buffers(1, gen_cap=max(1, max_tokens))
+        self._reset_sampling(bb, [rid], [first_tok], [first_pos], eos)
+        if max_tokens <= 0:
+            return []
+        if use_graph:
+            g = self._graph_for(bb)
+            for _ in range(max_tokens):
+                g.replay()
+        else:
+            for _ in range(max_tokens):
+                self.decode_step(bb)
+        cnt = int(bb.count[0].item())
+        return [int(t) for t in bb.gen[0, :cnt].tolist()]
+
+    def _reset_sampling(self, bb: StepBuffers, rids, first_toks, first_pos, eos) -> None:
+        B = bb.B
+        bb.tokens.copy_(torch.tensor(first_toks, dtype=I32))
+        bb.pos.copy_(torch.tensor(first_pos, dtype=I32))
+        bb.pt.copy_(torch.tensor([self.kv.table_row(r) for r in rids], dtype=I32))
+        bb.hist.zero_()
+        bb.count.zero_()
+        bb.done.zero_()
+        eos = list(eos)[:8]
+        bb.n_eos = len(eos)
+        if eos:
+            bb.eos[:len(eos)].copy_(torch.tensor(eos, dtype=I32))
+
+    def _graph_for(self, bb: StepBuffers) -> torch.cuda.CUDAGraph:
+        key = (id(bb), bb.n_eos)
+        if key not in self._graphs:
+            # warm-up: one eager step on a scratch copy of the state, then restore
+            saved = [t.clone() for t in (bb.tokens, bb.pos, bb.hist, bb.count, bb.done, bb.gen)]
+            self.decode_step(bb)
+            torch.cuda.synchronize()
+            for t, s in zip((bb.tokens, bb.pos, bb.hist, bb.count, bb.done, bb.gen), saved):
+                t.copy_(s)
+            self._graphs[key] = self.capture(bb)
+        return self._graphs[key]
+
+    def check_errors(self) -> int:
+        e = 0
+        for bb in self._bufs.values():
+            e |= int(bb.err.item())
+        return e

@@ -1,0 +1,470 @@
+// Decode-step kernels around the limb GEMM (K3-K7): embedding, RMSNorm with
+// fused limb split, GEMM finalize (limb recombination + per-row scale) fused
+// with residual add / RoPE + paged KV append / SwiGLU + limb split, exact
+// paged decode attention, and repetition penalty + argmax.
+//
+// Integer semantics follow the reference CPU engine bit for bit
+// (crates/arc-inference/src/cached_integer_model.rs: RMSNorm 985-1000, RoPE
+// 1002-1012, SiLU 1016-1027, attention 1448-1481, penalty/argmax 1537-1548;
+// crates/arc-inference/src/integer_lut.rs for exp/softmax/isqrt).
+//
+// Conventions:
+//  * a "slot" is one token of the step's batch (B slots); a slot has a
+//    position pos[b] and a page-table row pt[b * pt_stride + page].
+//  * limb planes: X + l * B * K + b * K + k, l = 0..7 (signed radix-256
+//    digits); lmax is the per-operand max limb count, raised by atomicMax.
+//  * P: GEMM partials [8 * B, M] int32, row l * B + b; finalize zeroes what
+//    it reads so the next GEMM can accumulate into it.
+//  * KV cache (per layer): [page][kv_head][16][d_head] int64.
+#include <climits>
+
+#include "common.cuh"
+#include "lut.cuh"
+
+using namespace q16;
+
+namespace {
+
+constexpr int PAGE = 16;
+
+__device__ __forceinline__ int block_max_int(int v, int* sh) {
+  v = __reduce_max_sync(0xffffffffu, v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    int x = l < (int)(blockDim.x >> 5) ? sh[l] : INT_MIN;
+    x = __reduce_max_sync(0xffffffffu, x);
+    if (l == 0) sh[0] = x;
+  }
+  __syncthreads();
+  int r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
+  return v;
+}
+
+__device__ __forceinline__ int64_t warp_max_i64(int64_t v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    int64_t o = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, m);
+    v = o > v ? o : v;
+  }
+  return v;
+}
+
+// Block reduction helpers over 64-bit values (shared scratch of 32 slots).
+__device__ __forceinline__ uint64_t block_sum_u64(uint64_t v, uint64_t* sh) {
+  v = warp_sum_u64(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    uint64_t x = l < (int)(blockDim.x >> 5) ? sh[l] : 0;
+    x = warp_sum_u64(x);
+    if (l == 0) sh[0] = x;
+  }
+  __syncthreads();
+  uint64_t r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ int64_t block_max_i64(int64_t v, int64_t* sh) {
+  v = warp_max_i64(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    int64_t x = l < (int)(blockDim.x >> 5) ? sh[l] : INT64_MIN;
+    x = warp_max_i64(x);
+    if (l == 0) sh[0] = x;
+  }
+  __syncthreads();
+  int64_t r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ void store_limbs(int8_t* X, size_t plane_stride, size_t off, int64_t v, int& need) {
+  int8_t d[8];
+  int n = limb_split8(v, d);
+  need = n > need ? n : need;
+#pragma unroll
+  for (int l = 0; l < 8; ++l) X[l * plane_stride + off] = d[l];
+}
+
+// Recombine one output element from its limb partials and zero them.
+__device__ __forceinline__ int64_t fin_elem(int* P, int M, int B, int L, int b, int m, int64_t s) {
+  uint64_t acc = 0;
+  for (int l = 0; l < L; ++l) {
+    int* p = P + (size_t)(l * B + b) * M + m;
+    acc += (uint64_t)(int64_t)(*p) << (8 * l);
+    *p = 0;
+  }
+  return mulshr((int64_t)acc, s);
+}
+
+// ------------------------------------------------------------------ embed
+// h[b] = emb_i8[min(tok, V-1)] * scale (cached_integer_model.rs:1397-1400, 1821-1830)
+__global__ void k_embed(const int* __restrict__ tokens, const int8_t* __restrict__ emb,
+                        const int64_t* __restrict__ emb_s, int V, int d, int64_t* __restrict__ h,
+                        int* __restrict__ counters, int ncounters) {
+  const int b = blockIdx.y;
+  int tok = tokens[b];
+  int idx = tok < 0 ? 0 : (tok >= V ? V - 1 : tok);
+  if (tok < 0) idx = V - 1;  // u32 ids >= 2^31 clamp to V-1 as in the reference
+  const int64_t s = emb_s[idx];
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < d; j += gridDim.x * blockDim.x)
+    h[(size_t)b * d + j] = wmul((int64_t)emb[(size_t)idx * d + j], s);
+  if (blockIdx.x == 0 && blockIdx.y == 0)
+    for (int c = threadIdx.x; c < ncounters; c += blockDim.x) counters[c] = 0;
+}
+
+// ------------------------------------------------------------------ RMSNorm + limbs
+__global__ void k_rmsnorm_limbs(const int64_t* __restrict__ h, const int64_t* __restrict__ gamma,
+                                int ngamma, int d, int B, int8_t* __restrict__ X, int* __restrict__ lmax,
+                                int64_t* __restrict__ y_out) {
+  __shared__ uint64_t sh[32];
+  __shared__ int shi[32];
+  const int b = blockIdx.x;
+  const int64_t* x = h + (size_t)b * d;
+  uint64_t ss = 0;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) ss += (uint64_t)(wmul(x[j], x[j]) >> FRAC_BITS);
+  ss = block_sum_u64(ss, sh);
+  const int64_t inv = rms_inv((int64_t)ss, d);
+  int need = 0;
+  const size_t ps = (size_t)B * d;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    const int64_t y = rms_apply(x[j], inv, j < ngamma ? gamma[j] : ONE);
+    if (y_out) y_out[(size_t)b * d + j] = y;
+    if (X) store_limbs(X, ps, (size_t)b * d + j, y, need);
+  }
+  need = block_max_int(need, shi);
+  if (threadIdx.x == 0 && lmax) atomicMax(lmax, need);
+}
+
+// ------------------------------------------------------------------ finalize
+// mode 0: out[b*ldo+m] = v ; mode 1: out[b*ldo+m] += v (residual)
+__global__ void k_finalize(int* __restrict__ P, int M, int B, const int* __restrict__ lmax,
+                           const int64_t* __restrict__ scales, int64_t* __restrict__ out, int ldo, int mode) {
+  const int b = blockIdx.y;
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  const int64_t v = fin_elem(P, M, B, *lmax, b, m, scales[m]);
+  int64_t* o = out + (size_t)b * ldo + m;
+  *o = mode == 1 ? wadd(*o, v) : v;
+}
+
+// QKV finalize + RoPE on q and k heads + paged KV append (1418-1444).
+// Rows of the fused weight: [0, d) q, [d, d + dkv) k, [d + dkv, d + 2dkv) v.
+__global__ void k_finalize_qkv(int* __restrict__ P, int B, const int* __restrict__ lmax,
+                               const int64_t* __restrict__ scales, int n_heads, int n_kv, int dh,
+                               int64_t* __restrict__ q_out, int64_t* __restrict__ Kc,
+                               int64_t* __restrict__ Vc, const int* __restrict__ pt, int pt_stride,
+                               const int* __restrict__ pos, const int64_t* __restrict__ rcos,
+                               const int64_t* __restrict__ rsin, int max_seq, int* __restrict__ err) {
+  const int b = blockIdx.y;
+  const int half = dh / 2;
+  const int d = n_heads * dh, dkv = n_kv * dh;
+  const int M = d + 2 * dkv;
+  const int nq = d / 2, nk = dkv / 2;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq + nk + dkv) return;
+  const int L = *lmax;
+  const int p = pos[b];
+  if (p < 0 || p >= max_seq) {
+    set_error(err, ARCB_ERR_SEQ_OVERFLOW);
+    return;
+  }
+  const int page = pt[(size_t)b * pt_stride + p / PAGE];
+  const int slot = p % PAGE;
+  if (i < nq + nk) {
+    const bool is_q = i < nq;
+    const int ii = is_q ? i : i - nq;
+    const int head = ii / half, e = ii % half;
+    const int r0 = (is_q ? 0 : d) + head * dh + e, r1 = r0 + half;
+    int64_t x0 = fin_elem(P, M, B, L, b, r0, scales[r0]);
+    int64_t x1 = fin_elem(P, M, B, L, b, r1, scales[r1]);
+    rope_pair(x0, x1, rcos[(size_t)p * half + e], rsin[(size_t)p * half + e]);
+    if (is_q) {
+      q_out[(size_t)b * d + head * dh + e] = x0;
+      q_out[(size_t)b * d + head * dh + e + half] = x1;
+    } else {
+      int64_t* kr = Kc + (((size_t)page * n_kv + head) * PAGE + slot) * dh;
+      kr[e] = x0;
+      kr[e + half] = x1;
+    }
+  } else {
+    const int j = i - nq - nk;
+    const int r = d + dkv + j;
+    const int64_t v = fin_elem(P, M, B, L, b, r, scales[r]);
+    const int head = j / dh, e = j % dh;
+    Vc[(((size_t)page * n_kv + head) * PAGE + slot) * dh + e] = v;
+  }
+}
+
+// gate/up finalize + SwiGLU + limb split for W_down (1496-1498).
+// Rows: [0, dff) gate, [dff, 2dff) up.
+__global__ void k_finalize_swiglu(int* __restrict__ P, int dff, int B, const int* __restrict__ lmax,
+                                  const int64_t* __restrict__ scales, int8_t* __restrict__ X,
+                                  int* __restrict__ lmax_out, int64_t* __restrict__ y_out) {
+  __shared__ int shi[32];
+  const int b = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const int M = 2 * dff;
+  int need = 0;
+  if (j < dff) {
+    const int L = *lmax;
+    const int64_t g = fin_elem(P, M, B, L, b, j, scales[j]);
+    const int64_t u = fin_elem(P, M, B, L, b, dff + j, scales[dff + j]);
+    const int64_t y = swiglu(g, u, c_exp_lut.v);
+    if (y_out) y_out[(size_t)b * dff + j] = y;
+    store_limbs(X, (size_t)B * dff, (size_t)b * dff + j, y, need);
+  }
+  need = block_max_int(need, shi);
+  if (threadIdx.x == 0) atomicMax(lmax_out, need);
+}
+
+// ------------------------------------------------------------------ attention
+// One CTA per (q head, slot).  Exact integer attention over positions
+// 0..pos[b] (1448-1476): wrapping i64 dots, score ((dot>>16)*scale)>>16,
+// softmax_i64 (integer_lut.rs:78-100) with a single max and a single sum (no
+// online rescaling, which would change the rounding), then
+// o = sum_j (w_j * v_j) >> 16 per term.  The output is written straight
+// into the limb planes of the W_o GEMM operand.
+__global__ void k_attn_decode(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
+                              const int64_t* __restrict__ Vc, const int* __restrict__ pt, int pt_stride,
+                              const int* __restrict__ pos, int n_heads, int n_kv, int dh,
+                              int64_t attn_scale, int B, int8_t* __restrict__ X, int* __restrict__ lmax,
+                              int64_t* __restrict__ o_out, int max_T, int* __restrict__ err) {
+  extern __shared__ int64_t sm[];
+  __shared__ uint64_t shu[32];
+  __shared__ int shi[32];
+  int64_t* qs = sm;
+  int64_t* sc = sm + dh;
+  const int hq = blockIdx.x, b = blockIdx.y;
+  const int T = pos[b] + 1;
+  if (T > max_T || T < 1) {
+    if (threadIdx.x == 0) set_error(err, ARCB_ERR_SEQ_OVERFLOW);
+    return;
+  }
+  const int kvh = hq * n_kv / n_heads;
+  const int d = n_heads * dh;
+  for (int e = threadIdx.x; e < dh; e += blockDim.x) qs[e] = q[(size_t)b * d + hq * dh + e];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int* ptb = pt + (size_t)b * pt_stride;
+  for (int j = warp; j < T; j += nw) {
+    const int64_t* kr = Kc + (((size_t)ptb[j / PAGE] * n_kv + kvh) * PAGE + (j % PAGE)) * dh;
+    uint64_t acc = 0;
+    for (int e = lane; e < dh; e += 32) acc += (uint64_t)qs[e] * (uint64_t)kr[e];
+    acc = warp_sum_u64(acc);
+    if (lane == 0) sc[j] = attn_score((int64_t)acc, attn_scale);
+  }
+  __syncthreads();
+  if (T == 1) {
+    if (threadIdx.x == 0) sc[0] = ONE;
+  } else {
+    int64_t mx = INT64_MIN;
+    for (int j = threadIdx.x; j < T; j += blockDim.x) mx = sc[j] > mx ? sc[j] : mx;
+    mx = block_max_i64(mx, (int64_t*)shu);
+    uint64_t sum = 0;
+    for (int j = threadIdx.x; j < T; j += blockDim.x) {
+      const int64_t e = integer_exp(wsub(sc[j], mx), c_exp_lut.v);
+      sc[j] = e;
+      sum += (uint64_t)e;
+    }
+    const int64_t s = (int64_t)block_sum_u64(sum, shu);
+    for (int j = threadIdx.x; j < T; j += blockDim.x) sc[j] = s == 0 ? ONE / T : wmul(sc[j], ONE) / s;
+  }
+  __syncthreads();
+  int need = 0;
+  for (int e = threadIdx.x; e < dh; e += blockDim.x) {
+    uint64_t o = 0;
+    for (int j = 0; j < T; ++j) {
+      const int64_t v = Vc[(((size_t)ptb[j / PAGE] * n_kv + kvh) * PAGE + (j % PAGE)) * dh + e];
+      o += (uint64_t)mulshr(sc[j], v);
+    }
+    const size_t off = (size_t)b * d + hq * dh + e;
+    if (o_out) o_out[off] = (int64_t)o;
+    if (X) store_limbs(X, (size_t)B * d, off, (int64_t)o, need);
+  }
+  need = block_max_int(need, shi);
+  if (threadIdx.x == 0 && lmax) atomicMax(lmax, need);
+}
+
+// ------------------------------------------------------------------ sampling
+// Repetition penalty over the newest min(count, 64) generated ids (compounding,
+// newest first), then argmax with lowest-index ties (1533-1548).  Per sampled
+// slot s: logits row lrow[s]; hist ring [S, 64]; writes the next token into
+// tokens_next[s], appends it to gen[s, count] (cap gen_cap) and the ring, and
+// advances pos_inc[s] when given.  done[s] latches on an EOS id.
+__global__ void k_sample(int64_t* __restrict__ logits, int ldl, int V, const int* __restrict__ lrow,
+                         int* __restrict__ hist, int* __restrict__ count, int* __restrict__ gen, int gen_cap,
+                         int* __restrict__ tokens_next, int* __restrict__ pos_inc, int* __restrict__ done,
+                         const int* __restrict__ eos, int n_eos) {
+  __shared__ int64_t sv[32];
+  __shared__ int si[32];
+  const int s = blockIdx.x;
+  if (done && done[s]) return;
+  int64_t* lg = logits + (size_t)(lrow ? lrow[s] : s) * ldl;
+  const int cnt = count[s];
+  if (threadIdx.x == 0) {
+    const int n = cnt < 64 ? cnt : 64;
+    for (int k = 0; k < n; ++k) {
+      const int t = hist[s * 64 + ((cnt - 1 - k) & 63)];
+      if (t >= 0 && t < V) lg[t] = penalize(lg[t]);
+    }
+  }
+  __syncthreads();
+  int64_t bv = INT64_MIN;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const int64_t v = lg[i];
+    if (v > bv) {
+      bv = v;
+      bi = i;
+    }
+  }
+  // warp reduce (value desc, index asc)
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const int64_t ov = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)bv, m);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    bv = l < nw ? sv[l] : INT64_MIN;
+    bi = l < nw ? si[l] : 0x7fffffff;
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      const int64_t ov = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)bv, m);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (l == 0) {
+      if (bi == 0x7fffffff) bi = 0;  // V == 0 guard; argmax_i64 returns 0
+      tokens_next[s] = bi;
+      if (cnt < gen_cap) gen[(size_t)s * gen_cap + cnt] = bi;
+      hist[s * 64 + (cnt & 63)] = bi;
+      count[s] = cnt + 1;
+      if (pos_inc) pos_inc[s] += 1;
+      if (done)
+        for (int e = 0; e < n_eos; ++e)
+          if (eos[e] == bi) done[s] = 1;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ seeded init
+__global__ void k_rng_i8(uint64_t key, int8_t* __restrict__ out, int64_t n);
+
+}  // namespace
+
+#include "../common/rng.h"
+
+namespace {
+__global__ void k_rng_i8(uint64_t key, int8_t* __restrict__ out, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = arcrng::weight_i8(key, (uint64_t)i);
+}
+}  // namespace
+
+// ==================================================================== C ABI
+extern "C" {
+
+static inline cudaStream_t S(void* s) { return (cudaStream_t)s; }
+
+int arcb_embed(const int* tokens, const int8_t* emb, const int64_t* emb_s, int V, int d, int B, int64_t* h,
+               int* counters, int ncounters, void* st) {
+  dim3 g((d + 255) / 256, B);
+  k_embed<<<g, 256, 0, S(st)>>>(tokens, emb, emb_s, V, d, h, counters, ncounters);
+  return (int)cudaGetLastError();
+}
+
+int arcb_rmsnorm_limbs(const int64_t* h, const int64_t* gamma, int ngamma, int d, int B, int8_t* X, int* lmax,
+                       int64_t* y_out, void* st) {
+  k_rmsnorm_limbs<<<B, 512, 0, S(st)>>>(h, gamma, ngamma, d, B, X, lmax, y_out);
+  return (int)cudaGetLastError();
+}
+
+int arcb_finalize(int* P, int M, int B, const int* lmax, const int64_t* scales, int64_t* out, int ldo, int mode,
+                  void* st) {
+  dim3 g((M + 255) / 256, B);
+  k_finalize<<<g, 256, 0, S(st)>>>(P, M, B, lmax, scales, out, ldo, mode);
+  return (int)cudaGetLastError();
+}
+
+int arcb_finalize_qkv(int* P, int B, const int* lmax, const int64_t* scales, int n_heads, int n_kv, int dh,
+                      int64_t* q_out, int64_t* Kc, int64_t* Vc, const int* pt, int pt_stride, const int* pos,
+                      const int64_t* rcos, const int64_t* rsin, int max_seq, int* err, void* st) {
+  const int d = n_heads * dh, dkv = n_kv * dh;
+  const int n = d / 2 + dkv / 2 + dkv;
+  dim3 g((n + 127) / 128, B);
+  k_finalize_qkv<<<g, 128, 0, S(st)>>>(P, B, lmax, scales, n_heads, n_kv, dh, q_out, Kc, Vc, pt, pt_stride, pos,
+                                        rcos, rsin, max_seq, err);
+  return (int)cudaGetLastError();
+}
+
+int arcb_finalize_swiglu(int* P, int dff, int B, const int* lmax, const int64_t* scales, int8_t* X,
+                         int* lmax_out, int64_t* y_out, void* st) {
+  dim3 g((dff + 255) / 256, B);
+  k_finalize_swiglu<<<g, 256, 0, S(st)>>>(P, dff, B, lmax, scales, X, lmax_out, y_out);
+  return (int)cudaGetLastError();
+}
+
+int arcb_attn_decode(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride,
+                     const int* pos, int n_heads, int n_kv, int dh, int64_t attn_scale, int B, int8_t* X,
+                     int* lmax, int64_t* o_out, int max_T, int* err, void* st) {
+  const size_t smem = (size_t)(dh + max_T) * 8;
+  static size_t attr = 0;
+  if (smem > 48 * 1024 && smem > attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    attr = smem;
+  }
+  dim3 g(n_heads, B);
+  k_attn_decode<<<g, 128, smem, S(st)>>>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax,
+                                          o_out, max_T, err);
+  return (int)cudaGetLastError();
+}
+
+int arcb_sample(int64_t* logits, int ldl, int V, const int* lrow, int S_, int* hist, int* count, int* gen,
+                int gen_cap, int* tokens_next, int* pos_inc, int* done, const int* eos, int n_eos, void* st) {
+  k_sample<<<S_, 1024, 0, S(st)>>>(logits, ldl, V, lrow, hist, count, gen, gen_cap, tokens_next, pos_inc, done,
+                                    eos, n_eos);
+  return (int)cudaGetLastError();
+}
+
+int arcb_rng_i8(uint64_t seed, uint64_t stream, int8_t* out, int64_t n, void* st) {
+  const uint64_t key = arcrng::stream_key(seed, stream);
+  int blocks = (int)((n + 255) / 256);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (blocks < 1) blocks = 1;
+  k_rng_i8<<<blocks, 256, 0, S(st)>>>(key, out, n);
+  return (int)cudaGetLastError();
+}
+
+}  // extern "C"

@@ -1,0 +1,150 @@
+"""sm_100a kernels against the CPU oracle (exact equality)."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from arc_chain_b200 import spec
+from arc_chain_b200.formats import gen
+from arc_chain_b200.models.config import preset
+from arc_chain_b200.oracle import arcref
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from arc_chain_b200.ops import int_ops
+
+    return int_ops
+
+
+def _limbs(x: np.ndarray, B: int, K: int):
+    """Host signed-digit limb planes [8*B, K] and max limb count."""
+    planes = np.zeros((8, B, K), dtype=np.int8)
+    r = x.astype(np.int64).copy()
+    need = 0
+    for l in range(8):
+        d = (r & 0xFF).astype(np.uint8).view(np.int8)
+        planes[l] = d
+        r = (r - d.astype(np.int64)) >> 8
+        if np.any(r != 0):
+            need = l + 2
+    need = min(8, need) if np.any(x != 0) else 0
+    if np.any(x != 0) and need == 0:
+        need = 1
+    return planes.reshape(8 * B, K), need
+
+
+@pytest.mark.parametrize("M,K,B,mag", [(128, 128, 1, 1 << 17), (256, 256, 3, 1 << 20), (384, 688, 2, 1 << 40),
+                                       (4096, 4096, 1, 1 << 18), (1000, 512, 5, 1 << 62), (640, 1024, 40, 1 << 17),
+                                       (256, 512, 70, 1 << 23)])
+def test_gemm_i8_exact(M, K, B, mag):
+    ops = _ops()
+    rng = np.random.default_rng(M * 7 + K + B)
+    w = rng.integers(-127, 128, size=(M, K), dtype=np.int64).astype(np.int8)
+    s = rng.integers(1, 5000, size=M).astype(np.int64)
+    x = rng.integers(-mag, mag, size=(B, K), dtype=np.int64)
+    planes, need = _limbs(x, B, K)
+    dev = torch.device("cuda")
+    W = torch.from_numpy(w).to(dev)
+    bn = ops.gemm_bn(B)
+    if planes.shape[0] < bn:
+        planes = np.concatenate([planes, np.zeros((bn - planes.shape[0], K), np.int8)])
+    X = torch.from_numpy(planes).to(dev)
+    wm, xm = ops.TensorMap(W, 128), ops.TensorMap(X, bn)
+    lmax = torch.tensor([need], dtype=torch.int32, device=dev)
+    P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    S = torch.from_numpy(s).to(dev)
+    out = torch.zeros(B, M, dtype=torch.int64, device=dev)
+    for ks in (1, 3):
+        ops.gemm_i8(wm, xm, M, K, B, ks, lmax, P, err)
+        ops.finalize(P, M, B, lmax, S, out, M, 0)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        got = out.cpu().numpy()
+        for b in range(B):
+            ref = arcref.matmul_i8(w, s, x[b])
+            np.testing.assert_array_equal(got[b], ref)
+        assert int(P.abs().max().item()) == 0  # finalize zeroed the partials
+
+
+def test_rmsnorm_limbs_exact():
+    ops = _ops()
+    rng = np.random.default_rng(1)
+    B, d = 4, 4096
+    h = rng.integers(-(1 << 22), 1 << 22, size=(B, d), dtype=np.int64)
+    g = rng.integers(60000, 70000, size=d - 7).astype(np.int64)  # shorter gamma: ONE past the end
+    dev = torch.device("cuda")
+    H = torch.from_numpy(h).to(dev)
+    G = torch.from_numpy(g).to(dev)
+    X = torch.zeros(8 * B, d, dtype=torch.int8, device=dev)
+    lm = torch.zeros(1, dtype=torch.int32, device=dev)
+    Y = torch.zeros(B, d, dtype=torch.int64, device=dev)
+    ops.rmsnorm_limbs(H, G, d, B, X, lm, Y)
+    torch.cuda.synchronize()
+    y = Y.cpu().numpy()
+    for b in range(B):
+        np.testing.assert_array_equal(y[b], arcref.rmsnorm(h[b], g))
+    planes, need = _limbs(y, B, d)
+    assert int(lm.item()) == need
+    np.testing.assert_array_equal(X.cpu().numpy(), planes)
+
+
+def _engine_for(cfg_name, seed=0):
+    from arc_chain_b200.models import dense
+    from arc_chain_b200.runtime.engine import Engine
+
+    cfg = preset(cfg_name)
+    host = gen.random_model(cfg, seed)
+    dm = dense.from_host(host, "cuda")
+    return host, Engine(dm)
+
+
+@pytest.mark.parametrize("name", ["micro", "micro_gqa"])
+def test_generate_matches_oracle(name):
+    host, eng = _engine_for(name)
+    om = arcref.Model(host)
+    prompt = gen.seeded_prompt(20, host.cfg.vocab, 1)
+    ref, rh = om.generate(prompt, 24)
+    for use_graph in (False, True):
+        got, gh = eng.generate(prompt, 24, use_graph=use_graph)
+        assert got == ref
+        assert gh == rh
+    assert eng.check_errors() == 0
+
+
+def test_generate_eos_stops():
+    host, eng = _engine_for("micro")
+    om = arcref.Model(host)
+    prompt = gen.seeded_prompt(8, host.cfg.vocab, 3)
+    ref, _ = om.generate(prompt, 12)
+    eos = [ref[4]]
+    r2, h2 = om.generate(prompt, 12, eos)
+    got, gh = eng.generate(prompt, 12, eos)
+    assert got == r2 and gh == h2 and len(got) <= 5
+
+
+def test_tiny_golden_hash():
+    """The tiny config: 32-token prompt (seed 1), 64 greedy tokens, weights seed 0."""
+    host, eng = _engine_for("tiny")
+    prompt = gen.seeded_prompt(32, 32000, 1)
+    om = arcref.Model(host)
+    ref, rh = om.generate(prompt, 64)
+    got, gh = eng.generate(prompt, 64)
+    assert got == ref and gh == rh
+
+
+def test_device_random_init_matches_host():
+    from arc_chain_b200.models import dense
+
+    cfg = preset("micro_gqa")
+    host = gen.random_model(cfg, 5)
+    dm = dense.random_device(cfg, "cuda", seed=5)
+    ref = dense.from_host(host, "cuda")
+    assert torch.equal(dm.emb, ref.emb) and torch.equal(dm.emb_s, ref.emb_s)
+    assert torch.equal(dm.lm.w, ref.lm.w) and torch.equal(dm.final_norm, ref.final_norm)
+    for a, b in zip(dm.layers, ref.layers):
+        for n in ("qkv", "wo", "gu", "down"):
+            assert torch.equal(getattr(a, n).w, getattr(b, n).w)
+            assert torch.equal(getattr(a, n).s, getattr(b, n).s)
