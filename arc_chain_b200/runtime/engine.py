@@ -209,6 +209,44 @@ class Engine:
             self.kv.release(rid)
         return toks, blake3(np.asarray(toks, dtype="<u4").tobytes())
 
+    def stream_generate(self, prompt: Sequence[int], max_tokens: int, eos: Sequence[int] = ()):
+        """Streaming generate (public API): yields each token as it is produced.
+
+        Every decode step copies that step's input (token id, position) from
+        pinned host memory to the device and reads the sampled id back into
+        pinned host memory, so the caller sees tokens one at a time."""
+        prompt = [int(t) for t in prompt]
+        n = len(prompt)
+        rid = self.new_request(1 + n + max_tokens)
+        try:
+            self.prefill(rid, [1] + prompt)
+            bb = self.buffers(1, gen_cap=max(1, max_tokens))
+            tok, pos = (prompt[-1] if n else 0), n + 1
+            self._reset_sampling(bb, [rid], [tok], [pos], eos)
+            g = self._graph_for(bb)
+            pin_in = torch.empty(2, dtype=I32, pin_memory=True)
+            pin_out = torch.empty(1, dtype=I32, pin_memory=True)
+            eos_set = set(int(e) for e in eos)
+            st = torch.cuda.current_stream()
+            for _ in range(max_tokens):
+                pin_in[0], pin_in[1] = tok, pos
+                bb.tokens.copy_(pin_in[0:1], non_blocking=True)
+                bb.pos.copy_(pin_in[1:2], non_blocking=True)
+                g.replay()
+                pin_out.copy_(bb.tokens, non_blocking=True)
+                st.synchronize()
+                tok = int(pin_out[0])
+                pos += 1
+                yield tok
+                if tok in eos_set:
+                    break
+        finally:
+            self.kv.release(rid)
+
+    # bytes moved between host and device by each stream_generate step
+    STREAM_H2D_BYTES = 8
+    STREAM_D2H_BYTES = 4
+
     def _decode_loop(self, rid, first_tok, first_pos, max_tokens, eos, use_graph) -> List[int]:
         bb = self.buffers(1, gen_cap=max(1, max_tokens))
         self._reset_sampling(bb, [rid], [first_tok], [first_pos], eos)
