@@ -91,10 +91,18 @@ def gemm_i8(wmap: TensorMap, xmap: TensorMap, M: int, K: int, B: int, ksplit: in
           "gemm_i8")
 
 
-def embed(tokens, emb, emb_s, V, d, B, h, counters):
+def embed(tokens, emb, emb_s, V, d, B, h, counters, ss):
+    """h = embedding rows; ss[0] = first norm's sum of squares; zeroes
+    counters and ss[1:] (ss is [n_norms, B] int64 viewed as u64)."""
     _count()
-    check(lib().arcb_embed(_p(tokens), _p(emb), _p(emb_s), V, d, B, _p(h), _p(counters), counters.numel(), _s()),
-          "embed")
+    check(lib().arcb_embed(_p(tokens), _p(emb), _p(emb_s), V, d, B, _p(h), _p(counters), counters.numel(), _p(ss),
+                           ss.shape[0], _s()), "embed")
+
+
+def norm_limbs(h, ss_row, gamma, d, B, X, lmax, y_out=None):
+    _count()
+    check(lib().arcb_norm_limbs(_p(h), _p(ss_row), _p(gamma), gamma.numel(), d, B, _p(X), _p(lmax), _p(y_out),
+                                _s()), "norm_limbs")
 
 
 def rmsnorm_limbs(h, gamma, d, B, X, lmax, y_out=None):
@@ -103,9 +111,9 @@ def rmsnorm_limbs(h, gamma, d, B, X, lmax, y_out=None):
           "rmsnorm_limbs")
 
 
-def finalize(P, M, B, lmax, scales, out, ldo, mode):
+def finalize(P, M, B, lmax, scales, out, ldo, mode, ss_out=None):
     _count()
-    check(lib().arcb_finalize(_p(P), M, B, _p(lmax), _p(scales), _p(out), ldo, mode, _s()), "finalize")
+    check(lib().arcb_finalize(_p(P), M, B, _p(lmax), _p(scales), _p(out), ldo, mode, _p(ss_out), _s()), "finalize")
 
 
 def finalize_qkv(P, B, lmax, scales, n_heads, n_kv, dh, q_out, Kc, Vc, pt, pos, rcos, rsin, max_seq, err):
@@ -121,10 +129,30 @@ def finalize_swiglu(P, dff, B, lmax, scales, X, lmax_out, y_out=None):
           "finalize_swiglu")
 
 
-def attn_decode(q, Kc, Vc, pt, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax, max_T, err, o_out=None):
-    _count()
+class AttnScratch:
+    """Scratch of the split-KV attention for B slots x n_heads heads."""
+
+    def __init__(self, B, n_heads, dh, max_T, device):
+        self.S = torch.zeros(B * n_heads * max_T, dtype=torch.int64, device=device)
+        self.Mx = torch.full((B * n_heads,), -(1 << 63), dtype=torch.int64, device=device)
+        self.O = torch.zeros(B * n_heads * dh, dtype=torch.int64, device=device)
+        self.cnt = torch.zeros(B * n_heads, dtype=torch.int32, device=device)
+        self.chunk = attn_chunk(B, n_heads, max_T)
+
+
+def attn_chunk(B, n_heads, max_T) -> int:
+    c = -(-max_T * n_heads * B // (4 * 148))
+    c = (c + 15) // 16 * 16
+    return max(16, min(512, c))
+
+
+def attn_decode(q, Kc, Vc, pt, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax, max_T, scratch, err, o_out=None):
+    """Two launches (scores+max, exp-sum+PV+limbs)."""
+    LAUNCHES[0] += 2
+    sc = scratch
     check(lib().arcb_attn_decode(_p(q), _p(Kc), _p(Vc), _p(pt), pt.shape[1], _p(pos), n_heads, n_kv, dh,
-                                 int(attn_scale), B, _p(X), _p(lmax), _p(o_out), max_T, _p(err), _s()),
+                                 int(attn_scale), B, sc.chunk, max_T, _p(sc.S), _p(sc.Mx), _p(sc.O), _p(sc.cnt),
+                                 _p(X), _p(lmax), _p(o_out), _p(err), _s()),
           "attn_decode")
 
 

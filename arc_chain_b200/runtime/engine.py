@@ -82,6 +82,9 @@ class StepBuffers:
         mmax = max(L0.qkv.M, d, L0.gu.M, model.vocab_local)
         self.P = torch.zeros(8 * B * mmax, dtype=I32, device=dev)
         self.cnt = torch.zeros(4 * c.n_layers + 4, dtype=I32, device=dev)
+        # per-norm sum of squares: [2 * n_layers + 1, B] (u64 bits in int64)
+        self.ss = torch.zeros(2 * c.n_layers + 1, B, dtype=I64, device=dev)
+        self.attn = ops.AttnScratch(B, model.n_heads_local, dh, max_pages * PAGE, dev)
         self.err = torch.zeros(1, dtype=I32, device=dev)
         self.logits_local = torch.zeros(B, model.vocab_local, dtype=I64, device=dev)
         self.logits = self.logits_local if model.tp_size == 1 else torch.zeros(B, c.vocab, dtype=I64, device=dev)
@@ -134,27 +137,28 @@ class Engine:
         nh, nkv = m.n_heads_local, m.n_kv_local
         dl, dffl = nh * dh, m.d_ff_local
         assert B == bb.B, "a StepBuffers instance serves exactly B slots (tensor maps are sized for it)"
-        ops.embed(bb.tokens, m.emb, m.emb_s, c.vocab, d, B, bb.h, bb.cnt)
+        ops.embed(bb.tokens, m.emb, m.emb_s, c.vocab, d, B, bb.h, bb.cnt, bb.ss)
+        ss = bb.ss
         for l, Ly in enumerate(m.layers):
             c0, c1, c2, c3 = (bb.cnt[4 * l + i:4 * l + i + 1] for i in range(4))
-            ops.rmsnorm_limbs(bb.h, Ly.attn_norm, d, B, bb.Xd, c0)
+            ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
             ops.gemm_i8(Ly.qkv.tmap, bb.mXd, Ly.qkv.M, Ly.qkv.K, B, bb.ks["qkv"], c0, bb.P, bb.err)
             ops.finalize_qkv(bb.P, B, c0, Ly.qkv.s, nh, nkv, dh, bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos,
                              m.rope_cos, m.rope_sin, self.max_seq, bb.err)
             ops.attn_decode(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo,
-                            c1, self.max_seq, bb.err)
+                            c1, self.max_pages * PAGE, bb.attn, bb.err)
             ops.gemm_i8(Ly.wo.tmap, bb.mXo, Ly.wo.M, Ly.wo.K, B, bb.ks["wo"], c1, bb.P, bb.err)
             cm.reduce_partials(bb.P, 8 * B, d, c1)
-            ops.finalize(bb.P, d, B, c1, Ly.wo.s, bb.h, d, 1)
-            ops.rmsnorm_limbs(bb.h, Ly.ffn_norm, d, B, bb.Xd, c2)
+            ops.finalize(bb.P, d, B, c1, Ly.wo.s, bb.h, d, 1, ss[2 * l + 1])
+            ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
             ops.gemm_i8(Ly.gu.tmap, bb.mXd, Ly.gu.M, Ly.gu.K, B, bb.ks["gu"], c2, bb.P, bb.err)
             ops.finalize_swiglu(bb.P, dffl, B, c2, Ly.gu.s, bb.Xf, c3)
             ops.gemm_i8(Ly.down.tmap, bb.mXf, Ly.down.M, Ly.down.K, B, bb.ks["down"], c3, bb.P, bb.err)
             cm.reduce_partials(bb.P, 8 * B, d, c3)
-            ops.finalize(bb.P, d, B, c3, Ly.down.s, bb.h, d, 1)
+            ops.finalize(bb.P, d, B, c3, Ly.down.s, bb.h, d, 1, ss[2 * l + 2])
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
-            ops.rmsnorm_limbs(bb.h, m.final_norm, d, B, bb.Xd, cf)
+            ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
             ops.gemm_i8(m.lm.tmap, bb.mXd, m.lm.M, m.lm.K, B, bb.ks["lm"], cf, bb.P, bb.err)
             ops.finalize(bb.P, m.lm.M, B, cf, m.lm.s, bb.logits_local, m.lm.M, 0)
             cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset)

@@ -1,7 +1,8 @@
 // Decode-step kernels around the limb GEMM (K3-K7): embedding, RMSNorm with
 // fused limb split, GEMM finalize (limb recombination + per-row scale) fused
-// with residual add / RoPE + paged KV append / SwiGLU + limb split, exact
-// paged decode attention, and repetition penalty + argmax.
+// with residual add + next-norm sum of squares / RoPE + paged KV append /
+// SwiGLU + limb split, exact split-KV paged decode attention, and repetition
+// penalty + argmax.
 //
 // Integer semantics follow the reference CPU engine bit for bit
 // (crates/arc-inference/src/cached_integer_model.rs: RMSNorm 985-1000, RoPE
@@ -15,6 +16,9 @@
 //    digits); lmax is the per-operand max limb count, raised by atomicMax.
 //  * P: GEMM partials [8 * B, M] int32, row l * B + b; finalize zeroes what
 //    it reads so the next GEMM can accumulate into it.
+//  * ss: per-norm sum of squares sum((x*x) >> 16) per slot, u64 wrapping.
+//    The producer of a residual stream value (embed, residual finalize) adds
+//    into it, so the norm itself is a fully parallel elementwise kernel.
 //  * KV cache (per layer): [page][kv_head][16][d_head] int64.
 #include <climits>
 
@@ -26,6 +30,21 @@ using namespace q16;
 namespace {
 
 constexpr int PAGE = 16;
+
+__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
+  return v;
+}
+
+__device__ __forceinline__ int64_t warp_max_i64(int64_t v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    int64_t o = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, m);
+    v = o > v ? o : v;
+  }
+  return v;
+}
 
 __device__ __forceinline__ int block_max_int(int v, int* sh) {
   v = __reduce_max_sync(0xffffffffu, v);
@@ -44,22 +63,6 @@ __device__ __forceinline__ int block_max_int(int v, int* sh) {
   return r;
 }
 
-__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) v += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
-  return v;
-}
-
-__device__ __forceinline__ int64_t warp_max_i64(int64_t v) {
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) {
-    int64_t o = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, m);
-    v = o > v ? o : v;
-  }
-  return v;
-}
-
-// Block reduction helpers over 64-bit values (shared scratch of 32 slots).
 __device__ __forceinline__ uint64_t block_sum_u64(uint64_t v, uint64_t* sh) {
   v = warp_sum_u64(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -113,55 +116,96 @@ __device__ __forceinline__ int64_t fin_elem(int* P, int M, int B, int L, int b, 
   return mulshr((int64_t)acc, s);
 }
 
+__device__ __forceinline__ uint64_t sq16(int64_t x) { return (uint64_t)(wmul(x, x) >> FRAC_BITS); }
+
 // ------------------------------------------------------------------ embed
-// h[b] = emb_i8[min(tok, V-1)] * scale (cached_integer_model.rs:1397-1400, 1821-1830)
+// h[b] = emb_i8[min(tok, V-1)] * scale (cached_integer_model.rs:1397-1400,
+// 1821-1830).  One CTA per slot; also writes the first norm's sum of squares
+// into ss[0][b] and zeroes the step's counters and the other ss slots.
 __global__ void k_embed(const int* __restrict__ tokens, const int8_t* __restrict__ emb,
-                        const int64_t* __restrict__ emb_s, int V, int d, int64_t* __restrict__ h,
-                        int* __restrict__ counters, int ncounters) {
-  const int b = blockIdx.y;
-  int tok = tokens[b];
-  int idx = tok < 0 ? 0 : (tok >= V ? V - 1 : tok);
-  if (tok < 0) idx = V - 1;  // u32 ids >= 2^31 clamp to V-1 as in the reference
+                        const int64_t* __restrict__ emb_s, int V, int d, int B, int64_t* __restrict__ h,
+                        int* __restrict__ counters, int ncounters, uint64_t* __restrict__ ss, int nss) {
+  __shared__ uint64_t sh[32];
+  const int b = blockIdx.x;
+  const uint32_t tok = (uint32_t)tokens[b];
+  const int idx = tok >= (uint32_t)V ? V - 1 : (int)tok;
   const int64_t s = emb_s[idx];
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < d; j += gridDim.x * blockDim.x)
-    h[(size_t)b * d + j] = wmul((int64_t)emb[(size_t)idx * d + j], s);
-  if (blockIdx.x == 0 && blockIdx.y == 0)
+  uint64_t acc = 0;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    const int64_t v = wmul((int64_t)emb[(size_t)idx * d + j], s);
+    h[(size_t)b * d + j] = v;
+    acc += sq16(v);
+  }
+  acc = block_sum_u64(acc, sh);
+  if (threadIdx.x == 0) ss[b] = acc;
+  for (int c = threadIdx.x; c < nss - 1; c += blockDim.x) ss[(size_t)(c + 1) * B + b] = 0;
+  if (b == 0)
     for (int c = threadIdx.x; c < ncounters; c += blockDim.x) counters[c] = 0;
 }
 
-// ------------------------------------------------------------------ RMSNorm + limbs
-__global__ void k_rmsnorm_limbs(const int64_t* __restrict__ h, const int64_t* __restrict__ gamma,
-                                int ngamma, int d, int B, int8_t* __restrict__ X, int* __restrict__ lmax,
+// ------------------------------------------------------------------ RMSNorm apply + limbs
+// y = (((x * isqrt(ss/n + 1)) >> 16) * gamma) >> 16, gamma = ONE past its end.
+__global__ void k_norm_limbs(const int64_t* __restrict__ h, const uint64_t* __restrict__ ss,
+                             const int64_t* __restrict__ gamma, int ngamma, int d, int B, int8_t* __restrict__ X,
+                             int* __restrict__ lmax, int64_t* __restrict__ y_out) {
+  __shared__ int shi[32];
+  const int b = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t inv = rms_inv((int64_t)ss[b], d);
+  int need = 0;
+  if (j < d) {
+    const size_t off = (size_t)b * d + j;
+    const int64_t y = rms_apply(h[off], inv, j < ngamma ? gamma[j] : ONE);
+    if (y_out) y_out[off] = y;
+    if (X) store_limbs(X, (size_t)B * d, off, y, need);
+  }
+  need = block_max_int(need, shi);
+  if (threadIdx.x == 0 && lmax) atomicMax(lmax, need);
+}
+
+// Self-contained RMSNorm (computes its own sum of squares; one CTA per slot).
+__global__ void k_rmsnorm_limbs(const int64_t* __restrict__ h, const int64_t* __restrict__ gamma, int ngamma,
+                                int d, int B, int8_t* __restrict__ X, int* __restrict__ lmax,
                                 int64_t* __restrict__ y_out) {
   __shared__ uint64_t sh[32];
   __shared__ int shi[32];
   const int b = blockIdx.x;
   const int64_t* x = h + (size_t)b * d;
   uint64_t ss = 0;
-  for (int j = threadIdx.x; j < d; j += blockDim.x) ss += (uint64_t)(wmul(x[j], x[j]) >> FRAC_BITS);
+  for (int j = threadIdx.x; j < d; j += blockDim.x) ss += sq16(x[j]);
   ss = block_sum_u64(ss, sh);
   const int64_t inv = rms_inv((int64_t)ss, d);
   int need = 0;
-  const size_t ps = (size_t)B * d;
   for (int j = threadIdx.x; j < d; j += blockDim.x) {
     const int64_t y = rms_apply(x[j], inv, j < ngamma ? gamma[j] : ONE);
     if (y_out) y_out[(size_t)b * d + j] = y;
-    if (X) store_limbs(X, ps, (size_t)b * d + j, y, need);
+    if (X) store_limbs(X, (size_t)B * d, (size_t)b * d + j, y, need);
   }
   need = block_max_int(need, shi);
   if (threadIdx.x == 0 && lmax) atomicMax(lmax, need);
 }
 
 // ------------------------------------------------------------------ finalize
-// mode 0: out[b*ldo+m] = v ; mode 1: out[b*ldo+m] += v (residual)
+// mode 0: out[b*ldo+m] = v ; mode 1: out[b*ldo+m] += v (residual) and, when
+// ss_out is given, ss_out[b] += sum over the CTA of (out*out) >> 16.
 __global__ void k_finalize(int* __restrict__ P, int M, int B, const int* __restrict__ lmax,
-                           const int64_t* __restrict__ scales, int64_t* __restrict__ out, int ldo, int mode) {
+                           const int64_t* __restrict__ scales, int64_t* __restrict__ out, int ldo, int mode,
+                           uint64_t* __restrict__ ss_out) {
+  __shared__ uint64_t sh[32];
   const int b = blockIdx.y;
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
-  if (m >= M) return;
-  const int64_t v = fin_elem(P, M, B, *lmax, b, m, scales[m]);
-  int64_t* o = out + (size_t)b * ldo + m;
-  *o = mode == 1 ? wadd(*o, v) : v;
+  uint64_t acc = 0;
+  if (m < M) {
+    const int64_t v = fin_elem(P, M, B, *lmax, b, m, scales[m]);
+    int64_t* o = out + (size_t)b * ldo + m;
+    const int64_t r = mode == 1 ? wadd(*o, v) : v;
+    *o = r;
+    acc = sq16(r);
+  }
+  if (ss_out) {
+    acc = block_sum_u64(acc, sh);
+    if (threadIdx.x == 0) atomicAdd((unsigned long long*)(ss_out + b), (unsigned long long)acc);
+  }
 }
 
 // QKV finalize + RoPE on q and k heads + paged KV append (1418-1444).
@@ -226,7 +270,7 @@ __global__ void k_finalize_swiglu(int* __restrict__ P, int dff, int B, const int
     const int L = *lmax;
     const int64_t g = fin_elem(P, M, B, L, b, j, scales[j]);
     const int64_t u = fin_elem(P, M, B, L, b, dff + j, scales[dff + j]);
-    const int64_t y = swiglu(g, u, c_exp_lut.v);
+    const int64_t y = swiglu(g, u, g_exp_lut.v);
     if (y_out) y_out[(size_t)b * dff + j] = y;
     store_limbs(X, (size_t)B * dff, (size_t)b * dff + j, y, need);
   }
@@ -235,71 +279,138 @@ __global__ void k_finalize_swiglu(int* __restrict__ P, int dff, int B, const int
 }
 
 // ------------------------------------------------------------------ attention
-// One CTA per (q head, slot).  Exact integer attention over positions
-// 0..pos[b] (1448-1476): wrapping i64 dots, score ((dot>>16)*scale)>>16,
-// softmax_i64 (integer_lut.rs:78-100) with a single max and a single sum (no
-// online rescaling, which would change the rounding), then
-// o = sum_j (w_j * v_j) >> 16 per term.  The output is written straight
-// into the limb planes of the W_o GEMM operand.
-__global__ void k_attn_decode(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
-                              const int64_t* __restrict__ Vc, const int* __restrict__ pt, int pt_stride,
-                              const int* __restrict__ pos, int n_heads, int n_kv, int dh,
-                              int64_t attn_scale, int B, int8_t* __restrict__ X, int* __restrict__ lmax,
-                              int64_t* __restrict__ o_out, int max_T, int* __restrict__ err) {
-  extern __shared__ int64_t sm[];
-  __shared__ uint64_t shu[32];
-  __shared__ int shi[32];
-  int64_t* qs = sm;
-  int64_t* sc = sm + dh;
+// Exact split-KV decode attention (1448-1476).  softmax_i64 needs the exact
+// global max and the exact global sum, and rounding happens per term, so
+// there is no online rescaling: the keys of one (slot, head) are split over
+// CTAs in three exact integer phases:
+//   A (k_attn_scores): scores s_j = ((q.k_j >> 16) * scale) >> 16 with
+//      wrapping i64 dots -> scratch S, and an atomicMax into Mx;
+//   B (k_attn_pv): every CTA recomputes e_j = exp(s_j - max) over all j and
+//      their sum (integer, order free), then for its own keys
+//      w_j = e_j * ONE / sum and sum_j (w_j * v_j) >> 16 -> u64 atomicAdd into
+//      O; the last CTA of the (slot, head) turns O into limb planes for W_o
+//      and resets O, Mx and its counter.
+// grid = (n_heads, B, n_split); split s covers keys [s*chunk, (s+1)*chunk).
+__global__ void k_attn_scores(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
+                              const int* __restrict__ pt, int pt_stride, const int* __restrict__ pos,
+                              int n_heads, int n_kv, int dh, int64_t attn_scale, int chunk, int max_T,
+                              int64_t* __restrict__ S, long long* __restrict__ Mx, int* __restrict__ err) {
+  __shared__ int64_t qs[256];
+  __shared__ int64_t shm[32];
   const int hq = blockIdx.x, b = blockIdx.y;
   const int T = pos[b] + 1;
+  const int j0 = blockIdx.z * chunk;
   if (T > max_T || T < 1) {
-    if (threadIdx.x == 0) set_error(err, ARCB_ERR_SEQ_OVERFLOW);
+    if (threadIdx.x == 0 && blockIdx.z == 0) set_error(err, ARCB_ERR_SEQ_OVERFLOW);
     return;
   }
+  if (j0 >= T) return;
+  const int j1 = min(T, j0 + chunk);
   const int kvh = hq * n_kv / n_heads;
   const int d = n_heads * dh;
   for (int e = threadIdx.x; e < dh; e += blockDim.x) qs[e] = q[(size_t)b * d + hq * dh + e];
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int* ptb = pt + (size_t)b * pt_stride;
-  for (int j = warp; j < T; j += nw) {
-    const int64_t* kr = Kc + (((size_t)ptb[j / PAGE] * n_kv + kvh) * PAGE + (j % PAGE)) * dh;
-    uint64_t acc = 0;
-    for (int e = lane; e < dh; e += 32) acc += (uint64_t)qs[e] * (uint64_t)kr[e];
-    acc = warp_sum_u64(acc);
-    if (lane == 0) sc[j] = attn_score((int64_t)acc, attn_scale);
-  }
-  __syncthreads();
-  if (T == 1) {
-    if (threadIdx.x == 0) sc[0] = ONE;
-  } else {
-    int64_t mx = INT64_MIN;
-    for (int j = threadIdx.x; j < T; j += blockDim.x) mx = sc[j] > mx ? sc[j] : mx;
-    mx = block_max_i64(mx, (int64_t*)shu);
-    uint64_t sum = 0;
-    for (int j = threadIdx.x; j < T; j += blockDim.x) {
-      const int64_t e = integer_exp(wsub(sc[j], mx), c_exp_lut.v);
-      sc[j] = e;
-      sum += (uint64_t)e;
+  int64_t* Sbh = S + ((size_t)b * n_heads + hq) * max_T;
+  int64_t mx = INT64_MIN;
+  // two keys per warp iteration for memory-level parallelism
+  for (int j = j0 + warp; j < j1; j += 2 * nw) {
+    const int ja = j, jb = j + nw;
+    const int64_t* ka = Kc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * dh;
+    const int64_t* kb = jb < j1 ? Kc + (((size_t)ptb[jb / PAGE] * n_kv + kvh) * PAGE + (jb % PAGE)) * dh : ka;
+    uint64_t aa = 0, ab = 0;
+#pragma unroll 4
+    for (int e = lane; e < dh; e += 32) {
+      const uint64_t qe = (uint64_t)qs[e];
+      aa += qe * (uint64_t)__ldg(ka + e);
+      ab += qe * (uint64_t)__ldg(kb + e);
     }
-    const int64_t s = (int64_t)block_sum_u64(sum, shu);
-    for (int j = threadIdx.x; j < T; j += blockDim.x) sc[j] = s == 0 ? ONE / T : wmul(sc[j], ONE) / s;
+    aa = warp_sum_u64(aa);
+    ab = warp_sum_u64(ab);
+    const int64_t sa = attn_score((int64_t)aa, attn_scale);
+    const int64_t sb = attn_score((int64_t)ab, attn_scale);
+    if (lane == 0) {
+      Sbh[ja] = sa;
+      if (jb < j1) Sbh[jb] = sb;
+    }
+    mx = sa > mx ? sa : mx;
+    if (jb < j1) mx = sb > mx ? sb : mx;
+  }
+  mx = block_max_i64(mx, shm);
+  if (threadIdx.x == 0) atomicMax(Mx + (size_t)b * n_heads + hq, (long long)mx);
+}
+
+__global__ void k_attn_pv(const int64_t* __restrict__ Vc, const int* __restrict__ pt, int pt_stride,
+                          const int* __restrict__ pos, int n_heads, int n_kv, int dh, int chunk, int max_T,
+                          const int64_t* __restrict__ S, long long* __restrict__ Mx,
+                          unsigned long long* __restrict__ O, int* __restrict__ cnt, int B,
+                          int8_t* __restrict__ X, int* __restrict__ lmax, int64_t* __restrict__ o_out) {
+  __shared__ int64_t lut[EXP_LUT_N];
+  __shared__ int64_t wsh[512];
+  __shared__ uint64_t shu[32];
+  __shared__ int shi[32];
+  __shared__ int last_s;
+  const int hq = blockIdx.x, b = blockIdx.y;
+  const int T = pos[b] + 1;
+  const int j0 = blockIdx.z * chunk;
+  if (T > max_T || T < 1 || j0 >= T) return;
+  const int j1 = min(T, j0 + chunk);
+  const int n_split_used = (T + chunk - 1) / chunk;
+  const int kvh = hq * n_kv / n_heads;
+  const int d = n_heads * dh;
+  const size_t bh = (size_t)b * n_heads + hq;
+  const int64_t* Sbh = S + bh * max_T;
+  for (int i = threadIdx.x; i < EXP_LUT_N; i += blockDim.x) lut[i] = g_exp_lut.v[i];
+  __syncthreads();
+  const int64_t mx = (int64_t)Mx[bh];
+  // global sum of exps (every CTA computes the same exact integer)
+  uint64_t sum = 0;
+  for (int j = threadIdx.x; j < T; j += blockDim.x) sum += (uint64_t)integer_exp(wsub(Sbh[j], mx), lut);
+  const int64_t s = (int64_t)block_sum_u64(sum, shu);
+  // weights of this CTA's keys
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+    int64_t w;
+    if (T == 1) w = ONE;
+    else if (s == 0) w = ONE / T;
+    else w = wmul(integer_exp(wsub(Sbh[j], mx), lut), ONE) / s;
+    wsh[j - j0] = w;
   }
   __syncthreads();
-  int need = 0;
+  const int* ptb = pt + (size_t)b * pt_stride;
   for (int e = threadIdx.x; e < dh; e += blockDim.x) {
     uint64_t o = 0;
-    for (int j = 0; j < T; ++j) {
-      const int64_t v = Vc[(((size_t)ptb[j / PAGE] * n_kv + kvh) * PAGE + (j % PAGE)) * dh + e];
-      o += (uint64_t)mulshr(sc[j], v);
+#pragma unroll 8
+    for (int j = j0; j < j1; ++j) {
+      const int64_t v = __ldg(Vc + (((size_t)ptb[j / PAGE] * n_kv + kvh) * PAGE + (j % PAGE)) * dh + e);
+      o += (uint64_t)mulshr(wsh[j - j0], v);
     }
+    if (n_split_used == 1) {
+      O[bh * dh + e] = o;  // sole contributor
+    } else {
+      atomicAdd(O + bh * dh + e, (unsigned long long)o);
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_s = (n_split_used == 1) || (atomicAdd(cnt + bh, 1) == n_split_used - 1);
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  int need = 0;
+  for (int e = threadIdx.x; e < dh; e += blockDim.x) {
+    const int64_t o = (int64_t)__ldcg(O + bh * dh + e);
+    O[bh * dh + e] = 0;
     const size_t off = (size_t)b * d + hq * dh + e;
-    if (o_out) o_out[off] = (int64_t)o;
-    if (X) store_limbs(X, (size_t)B * d, off, (int64_t)o, need);
+    if (o_out) o_out[off] = o;
+    if (X) store_limbs(X, (size_t)B * d, off, o, need);
   }
   need = block_max_int(need, shi);
-  if (threadIdx.x == 0 && lmax) atomicMax(lmax, need);
+  if (threadIdx.x == 0) {
+    cnt[bh] = 0;
+    Mx[bh] = LLONG_MIN;
+    if (lmax) atomicMax(lmax, need);
+  }
 }
 
 // ------------------------------------------------------------------ sampling
@@ -335,7 +446,6 @@ __global__ void k_sample(int64_t* __restrict__ logits, int ldl, int V, const int
       bi = i;
     }
   }
-  // warp reduce (value desc, index asc)
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) {
     const int64_t ov = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)bv, m);
@@ -378,9 +488,6 @@ __global__ void k_sample(int64_t* __restrict__ logits, int ldl, int V, const int
   }
 }
 
-// ------------------------------------------------------------------ seeded init
-__global__ void k_rng_i8(uint64_t key, int8_t* __restrict__ out, int64_t n);
-
 }  // namespace
 
 #include "../common/rng.h"
@@ -395,25 +502,31 @@ __global__ void k_rng_i8(uint64_t key, int8_t* __restrict__ out, int64_t n) {
 // ==================================================================== C ABI
 extern "C" {
 
-static inline cudaStream_t S(void* s) { return (cudaStream_t)s; }
+static inline cudaStream_t S_(void* s) { return (cudaStream_t)s; }
 
 int arcb_embed(const int* tokens, const int8_t* emb, const int64_t* emb_s, int V, int d, int B, int64_t* h,
-               int* counters, int ncounters, void* st) {
+               int* counters, int ncounters, uint64_t* ss, int nss, void* st) {
+  k_embed<<<B, 512, 0, S_(st)>>>(tokens, emb, emb_s, V, d, B, h, counters, ncounters, ss, nss);
+  return (int)cudaGetLastError();
+}
+
+int arcb_norm_limbs(const int64_t* h, const uint64_t* ss, const int64_t* gamma, int ngamma, int d, int B,
+                    int8_t* X, int* lmax, int64_t* y_out, void* st) {
   dim3 g((d + 255) / 256, B);
-  k_embed<<<g, 256, 0, S(st)>>>(tokens, emb, emb_s, V, d, h, counters, ncounters);
+  k_norm_limbs<<<g, 256, 0, S_(st)>>>(h, ss, gamma, ngamma, d, B, X, lmax, y_out);
   return (int)cudaGetLastError();
 }
 
 int arcb_rmsnorm_limbs(const int64_t* h, const int64_t* gamma, int ngamma, int d, int B, int8_t* X, int* lmax,
                        int64_t* y_out, void* st) {
-  k_rmsnorm_limbs<<<B, 512, 0, S(st)>>>(h, gamma, ngamma, d, B, X, lmax, y_out);
+  k_rmsnorm_limbs<<<B, 512, 0, S_(st)>>>(h, gamma, ngamma, d, B, X, lmax, y_out);
   return (int)cudaGetLastError();
 }
 
 int arcb_finalize(int* P, int M, int B, const int* lmax, const int64_t* scales, int64_t* out, int ldo, int mode,
-                  void* st) {
+                  uint64_t* ss_out, void* st) {
   dim3 g((M + 255) / 256, B);
-  k_finalize<<<g, 256, 0, S(st)>>>(P, M, B, lmax, scales, out, ldo, mode);
+  k_finalize<<<g, 256, 0, S_(st)>>>(P, M, B, lmax, scales, out, ldo, mode, ss_out);
   return (int)cudaGetLastError();
 }
 
@@ -423,37 +536,37 @@ int arcb_finalize_qkv(int* P, int B, const int* lmax, const int64_t* scales, int
   const int d = n_heads * dh, dkv = n_kv * dh;
   const int n = d / 2 + dkv / 2 + dkv;
   dim3 g((n + 127) / 128, B);
-  k_finalize_qkv<<<g, 128, 0, S(st)>>>(P, B, lmax, scales, n_heads, n_kv, dh, q_out, Kc, Vc, pt, pt_stride, pos,
-                                        rcos, rsin, max_seq, err);
+  k_finalize_qkv<<<g, 128, 0, S_(st)>>>(P, B, lmax, scales, n_heads, n_kv, dh, q_out, Kc, Vc, pt, pt_stride, pos,
+                                         rcos, rsin, max_seq, err);
   return (int)cudaGetLastError();
 }
 
 int arcb_finalize_swiglu(int* P, int dff, int B, const int* lmax, const int64_t* scales, int8_t* X,
                          int* lmax_out, int64_t* y_out, void* st) {
   dim3 g((dff + 255) / 256, B);
-  k_finalize_swiglu<<<g, 256, 0, S(st)>>>(P, dff, B, lmax, scales, X, lmax_out, y_out);
+  k_finalize_swiglu<<<g, 256, 0, S_(st)>>>(P, dff, B, lmax, scales, X, lmax_out, y_out);
   return (int)cudaGetLastError();
 }
 
+// Attention scratch: S [B, n_heads, max_T] i64, Mx [B, n_heads] (init
+// LLONG_MIN), O [B, n_heads, dh] u64 (init 0), cnt [B, n_heads] (init 0).
 int arcb_attn_decode(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride,
-                     const int* pos, int n_heads, int n_kv, int dh, int64_t attn_scale, int B, int8_t* X,
-                     int* lmax, int64_t* o_out, int max_T, int* err, void* st) {
-  const size_t smem = (size_t)(dh + max_T) * 8;
-  static size_t attr = 0;
-  if (smem > 48 * 1024 && smem > attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return (int)e;
-    attr = smem;
-  }
-  dim3 g(n_heads, B);
-  k_attn_decode<<<g, 128, smem, S(st)>>>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax,
-                                          o_out, max_T, err);
+                     const int* pos, int n_heads, int n_kv, int dh, int64_t attn_scale, int B, int chunk, int max_T,
+                     int64_t* S, long long* Mx, unsigned long long* O, int* cnt, int8_t* X, int* lmax,
+                     int64_t* o_out, int* err, void* st) {
+  if (dh > 256 || chunk > 512 || chunk < 1) return -1;
+  const int nsplit = (max_T + chunk - 1) / chunk;
+  dim3 g(n_heads, B, nsplit);
+  k_attn_scores<<<g, 128, 0, S_(st)>>>(q, Kc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, chunk, max_T, S,
+                                        Mx, err);
+  k_attn_pv<<<g, 128, 0, S_(st)>>>(Vc, pt, pt_stride, pos, n_heads, n_kv, dh, chunk, max_T, S, Mx, O, cnt, B, X,
+                                    lmax, o_out);
   return (int)cudaGetLastError();
 }
 
-int arcb_sample(int64_t* logits, int ldl, int V, const int* lrow, int S_, int* hist, int* count, int* gen,
+int arcb_sample(int64_t* logits, int ldl, int V, const int* lrow, int S, int* hist, int* count, int* gen,
                 int gen_cap, int* tokens_next, int* pos_inc, int* done, const int* eos, int n_eos, void* st) {
-  k_sample<<<S_, 1024, 0, S(st)>>>(logits, ldl, V, lrow, hist, count, gen, gen_cap, tokens_next, pos_inc, done,
+  k_sample<<<S, 1024, 0, S_(st)>>>(logits, ldl, V, lrow, hist, count, gen, gen_cap, tokens_next, pos_inc, done,
                                     eos, n_eos);
   return (int)cudaGetLastError();
 }
@@ -463,7 +576,7 @@ int arcb_rng_i8(uint64_t seed, uint64_t stream, int8_t* out, int64_t n, void* st
   int blocks = (int)((n + 255) / 256);
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (blocks < 1) blocks = 1;
-  k_rng_i8<<<blocks, 256, 0, S(st)>>>(key, out, n);
+  k_rng_i8<<<blocks, 256, 0, S_(st)>>>(key, out, n);
   return (int)cudaGetLastError();
 }
 

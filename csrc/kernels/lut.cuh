@@ -14,4 +14,6 @@ constexpr ExpLut make_exp_lut() {
   return t;
 }
 
-static __constant__ ExpLut c_exp_lut = make_exp_lut();
+// Global (L1-cached) rather than __constant__: lookups are data-dependent,
+// and divergent constant-bank reads serialise across a warp.
+static __device__ const ExpLut g_exp_lut = make_exp_lut();
