@@ -87,6 +87,32 @@ class DenseModel:
         return self.lm.M
 
 
+def _swap12(a):
+    return a.transpose(1, 2) if isinstance(a, torch.Tensor) else np.swapaxes(a, 1, 2)
+
+
+def interleave_heads(a, n_heads: int, dh: int):
+    """Reorder the rows of each head from (0..half-1, half..dh-1) to
+    (0, half, 1, half+1, ...): the two rows of one RoPE rotation pair become
+    adjacent, so the fused GEMM epilogue rotates them with one lane shuffle.
+    Works on [n_heads*dh, K] weights and [n_heads*dh] scales."""
+    half = dh // 2
+    tail = tuple(a.shape[1:])
+    r = _swap12(a.reshape(n_heads, 2, half, *tail))
+    return r.reshape(n_heads * dh, *tail)
+
+
+def interleave_pairs(g, u):
+    """Rows g0, u0, g1, u1, ...: gate and up of one FFN unit adjacent."""
+    st = torch.stack if isinstance(g, torch.Tensor) else np.stack
+    r = st([g, u], 1)
+    return r.reshape(2 * g.shape[0], *tuple(g.shape[1:]))
+
+
+def _contig(a):
+    return a.contiguous() if isinstance(a, torch.Tensor) else np.ascontiguousarray(a)
+
+
 def _shard_rows(a, rank, size):
     n = a.shape[0] // size
     return a[rank * n:(rank + 1) * n]
@@ -120,12 +146,14 @@ def from_host(m: Int8Model, device, tp_rank: int = 0, tp_size: int = 1) -> Dense
     layers = []
     for L in m.layers:
         r, s_ = tp_rank, tp_size
+        nhl, nkl = c.n_heads // s_, c.n_kv_heads // s_
         wq, wk, wv = (_shard_rows(L[n], r, s_) for n in ("wq", "wk", "wv"))
         sq, sk, sv = (_shard_rows(L[n + "_s"], r, s_) for n in ("wq", "wk", "wv"))
-        qkv = Linear(T(np.concatenate([wq, wk, wv])), T(np.concatenate([sq, sk, sv])))
+        qkv = Linear(T(np.concatenate([interleave_heads(wq, nhl, dh), interleave_heads(wk, nkl, dh), wv])),
+                     T(np.concatenate([interleave_heads(sq, nhl, dh), interleave_heads(sk, nkl, dh), sv])))
         wo = Linear(T(_shard_cols(L["wo"], r, s_)), T(L["wo_s"]))
-        gu = Linear(T(np.concatenate([_shard_rows(L["gate"], r, s_), _shard_rows(L["up"], r, s_)])),
-                    T(np.concatenate([_shard_rows(L["gate_s"], r, s_), _shard_rows(L["up_s"], r, s_)])))
+        gu = Linear(T(interleave_pairs(_shard_rows(L["gate"], r, s_), _shard_rows(L["up"], r, s_))),
+                    T(interleave_pairs(_shard_rows(L["gate_s"], r, s_), _shard_rows(L["up_s"], r, s_))))
         down = Linear(T(_shard_cols(L["down"], r, s_)), T(L["down_s"]))
         layers.append(DenseLayer(qkv.build_map(), wo.build_map(), gu.build_map(), down.build_map(),
                                  T(L["attn_norm"]), T(L["ffn_norm"])))
@@ -167,12 +195,15 @@ def random_device(cfg: ModelConfig, device, seed: int = 0, tp_rank: int = 0, tp_
         wq, sq = rows_of(tid(0), d, d)
         wk, sk = rows_of(tid(1), dkv, d)
         wv, sv = rows_of(tid(2), dkv, d)
-        qkv = Linear(torch.cat([wq, wk, wv]), torch.cat([sq, sk, sv]))
+        nhl, nkl = cfg.n_heads // s_, cfg.n_kv_heads // s_
+        dh = cfg.d_head
+        qkv = Linear(torch.cat([interleave_heads(wq, nhl, dh), interleave_heads(wk, nkl, dh), wv]).contiguous(),
+                     torch.cat([interleave_heads(sq, nhl, dh), interleave_heads(sk, nkl, dh), sv]).contiguous())
         del wq, wk, wv
         wo, so = cols_of(tid(3), d, d)
         wg, sg = rows_of(tid(4), dff, d)
         wu, su = rows_of(tid(5), dff, d)
-        gu = Linear(torch.cat([wg, wu]), torch.cat([sg, su]))
+        gu = Linear(interleave_pairs(wg, wu).contiguous(), interleave_pairs(sg, su).contiguous())
         del wg, wu
         wd, sd = cols_of(tid(6), d, dff)
         an = torch.from_numpy(gen.gamma(seed, (tid(7) << 2) | 1, d)).to(dev)

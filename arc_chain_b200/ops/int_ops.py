@@ -167,3 +167,44 @@ def sample(logits, V, n, hist, count, gen, tokens_next, pos_inc=None, done=None,
 def rng_i8(seed: int, stream: int, out: torch.Tensor) -> None:
     _count()
     check(lib().arcb_rng_i8(seed, stream, _p(out), out.numel(), _s()), "rng_i8")
+
+
+# --------------------------------------------------------------- fused GEMM
+class Epi(C.Structure):
+    """Mirror of fg::Epi (csrc/kernels/gemm_fused.cu)."""
+
+    _fields_ = [("mode", C.c_int), ("scales", C.c_void_p), ("out", C.c_void_p), ("ldo", C.c_int),
+                ("ss_out", C.c_void_p), ("n_heads", C.c_int), ("n_kv", C.c_int), ("dh", C.c_int),
+                ("q_out", C.c_void_p), ("Kc", C.c_void_p), ("Vc", C.c_void_p), ("pt", C.c_void_p),
+                ("pt_stride", C.c_int), ("pos", C.c_void_p), ("rcos", C.c_void_p), ("rsin", C.c_void_p),
+                ("max_seq", C.c_int), ("X", C.c_void_p), ("ldx", C.c_int), ("lmax_out", C.c_void_p),
+                ("err", C.c_void_p), ("B", C.c_int)]
+
+
+PARTIAL, STORE, RESID, QKV, SWIGLU = 0, 1, 2, 3, 4
+
+
+def fgemm_bn(B: int) -> int:
+    return lib().arcb_fgemm_bn(B)
+
+
+def fgemm(wmap: TensorMap, xmap: TensorMap, M: int, K: int, B: int, lmax, P, tile_cnt, epi: Epi,
+          pdl: bool = True) -> None:
+    """Persistent stream-K limb GEMM with the finalize fused in (mode in epi)."""
+    _count()
+    check(lib().arcb_fgemm(wmap.addr, xmap.addr, M, K, B, xmap.box_rows, _p(lmax), _p(P), _p(tile_cnt),
+                           C.addressof(epi), int(pdl), _s()), "fgemm")
+
+
+def epi(mode, scales, err, **kw) -> Epi:
+    e = Epi()
+    e.mode = mode
+    e.scales = _p(scales)
+    e.err = _p(err)
+    for k, v in kw.items():
+        setattr(e, k, _p(v) if isinstance(v, torch.Tensor) else v)
+    return e
+
+
+def set_pdl(on: bool) -> None:
+    lib().arcb_set_pdl(int(on))

@@ -50,6 +50,11 @@ class Comm:
     def gather_logits(self, local: torch.Tensor, full: torch.Tensor, B: int, vocab_offset: int) -> None:
         pass
 
+    def fgemm_reduce(self, lin, xmap, B: int, lmax: torch.Tensor, bb: "StepBuffers", epi) -> None:
+        """Row-parallel GEMM whose epilogue sees the full (all-rank) sum; on
+        one GPU that is the plain fused GEMM."""
+        ops.fgemm(lin.tmap, xmap, lin.M, lin.K, B, lmax, bb.P, bb.tiles, epi)
+
     @property
     def n_launches(self) -> int:
         return 0
@@ -70,7 +75,8 @@ class StepBuffers:
         self.pt = torch.zeros(B, max_pages, dtype=I32, device=dev)
         self.h = torch.zeros(B, d, dtype=I64, device=dev)
         self.q = torch.zeros(B, dl, dtype=I64, device=dev)
-        self.bn = ops.gemm_bn(B)
+        self.bn = ops.fgemm_bn(B)
+        self.epis = None
         rows = max(8 * B, self.bn)  # the TMA box never exceeds the tensor
         self.Xd = torch.zeros(rows, d, dtype=I8, device=dev)
         self.Xo = torch.zeros(rows, dl, dtype=I8, device=dev)
@@ -95,14 +101,8 @@ class StepBuffers:
         self.done = torch.zeros(B, dtype=I32, device=dev)
         self.eos = torch.zeros(8, dtype=I32, device=dev)
         self.n_eos = 0
-        # split-K per GEMM for this B
-        self.ks = {
-            "qkv": ops.choose_ksplit(L0.qkv.M, L0.qkv.K, self.bn),
-            "wo": ops.choose_ksplit(L0.wo.M, L0.wo.K, self.bn),
-            "gu": ops.choose_ksplit(L0.gu.M, L0.gu.K, self.bn),
-            "down": ops.choose_ksplit(L0.down.M, L0.down.K, self.bn),
-            "lm": ops.choose_ksplit(model.lm.M, model.lm.K, self.bn),
-        }
+        # per-M-tile arrival counters of the fused GEMM (zero between uses)
+        self.tiles = torch.zeros((mmax + 127) // 128 + 1, dtype=I32, device=dev)
 
 
 class Engine:
@@ -139,29 +139,57 @@ class Engine:
         assert B == bb.B, "a StepBuffers instance serves exactly B slots (tensor maps are sized for it)"
         ops.embed(bb.tokens, m.emb, m.emb_s, c.vocab, d, B, bb.h, bb.cnt, bb.ss)
         ss = bb.ss
+        E = self._epis(bb)
+        reduce_in_kernel = cm.size == 1 or getattr(cm, "fused", False)
         for l, Ly in enumerate(m.layers):
             c0, c1, c2, c3 = (bb.cnt[4 * l + i:4 * l + i + 1] for i in range(4))
+            e = E[l]
             ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
-            ops.gemm_i8(Ly.qkv.tmap, bb.mXd, Ly.qkv.M, Ly.qkv.K, B, bb.ks["qkv"], c0, bb.P, bb.err)
-            ops.finalize_qkv(bb.P, B, c0, Ly.qkv.s, nh, nkv, dh, bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos,
-                             m.rope_cos, m.rope_sin, self.max_seq, bb.err)
+            ops.fgemm(Ly.qkv.tmap, bb.mXd, Ly.qkv.M, Ly.qkv.K, B, c0, bb.P, bb.tiles, e["qkv"])
             ops.attn_decode(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo,
                             c1, self.max_pages * PAGE, bb.attn, bb.err)
-            ops.gemm_i8(Ly.wo.tmap, bb.mXo, Ly.wo.M, Ly.wo.K, B, bb.ks["wo"], c1, bb.P, bb.err)
-            cm.reduce_partials(bb.P, 8 * B, d, c1)
-            ops.finalize(bb.P, d, B, c1, Ly.wo.s, bb.h, d, 1, ss[2 * l + 1])
+            if reduce_in_kernel:
+                cm.fgemm_reduce(Ly.wo, bb.mXo, B, c1, bb, e["wo"])
+            else:
+                ops.fgemm(Ly.wo.tmap, bb.mXo, Ly.wo.M, Ly.wo.K, B, c1, bb.P, bb.tiles, e["partial"])
+                cm.reduce_partials(bb.P, 8 * B, d, c1)
+                ops.finalize(bb.P, d, B, c1, Ly.wo.s, bb.h, d, 1, ss[2 * l + 1])
             ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
-            ops.gemm_i8(Ly.gu.tmap, bb.mXd, Ly.gu.M, Ly.gu.K, B, bb.ks["gu"], c2, bb.P, bb.err)
-            ops.finalize_swiglu(bb.P, dffl, B, c2, Ly.gu.s, bb.Xf, c3)
-            ops.gemm_i8(Ly.down.tmap, bb.mXf, Ly.down.M, Ly.down.K, B, bb.ks["down"], c3, bb.P, bb.err)
-            cm.reduce_partials(bb.P, 8 * B, d, c3)
-            ops.finalize(bb.P, d, B, c3, Ly.down.s, bb.h, d, 1, ss[2 * l + 2])
+            ops.fgemm(Ly.gu.tmap, bb.mXd, Ly.gu.M, Ly.gu.K, B, c2, bb.P, bb.tiles, e["gu"])
+            if reduce_in_kernel:
+                cm.fgemm_reduce(Ly.down, bb.mXf, B, c3, bb, e["down"])
+            else:
+                ops.fgemm(Ly.down.tmap, bb.mXf, Ly.down.M, Ly.down.K, B, c3, bb.P, bb.tiles, e["partial"])
+                cm.reduce_partials(bb.P, 8 * B, d, c3)
+                ops.finalize(bb.P, d, B, c3, Ly.down.s, bb.h, d, 1, ss[2 * l + 2])
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
             ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
-            ops.gemm_i8(m.lm.tmap, bb.mXd, m.lm.M, m.lm.K, B, bb.ks["lm"], cf, bb.P, bb.err)
-            ops.finalize(bb.P, m.lm.M, B, cf, m.lm.s, bb.logits_local, m.lm.M, 0)
+            ops.fgemm(m.lm.tmap, bb.mXd, m.lm.M, m.lm.K, B, cf, bb.P, bb.tiles, E[-1]["lm"])
             cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset)
+
+    def _epis(self, bb: StepBuffers):
+        """Epilogue descriptors of every fused GEMM of a forward over `bb`."""
+        if bb.epis is not None:
+            return bb.epis
+        m, c = self.m, self.m.cfg
+        d, dh = c.d_model, c.d_head
+        out = []
+        for l, Ly in enumerate(m.layers):
+            ss = bb.ss
+            out.append({
+                "qkv": ops.epi(ops.QKV, Ly.qkv.s, bb.err, n_heads=m.n_heads_local, n_kv=m.n_kv_local, dh=dh,
+                               q_out=bb.q, Kc=self.kv.K[l], Vc=self.kv.V[l], pt=bb.pt, pt_stride=bb.pt.shape[1],
+                               pos=bb.pos, rcos=m.rope_cos, rsin=m.rope_sin, max_seq=self.max_seq),
+                "wo": ops.epi(ops.RESID, Ly.wo.s, bb.err, out=bb.h, ldo=d, ss_out=ss[2 * l + 1]),
+                "gu": ops.epi(ops.SWIGLU, Ly.gu.s, bb.err, X=bb.Xf, ldx=m.d_ff_local,
+                              lmax_out=bb.cnt[4 * l + 3:4 * l + 4]),
+                "down": ops.epi(ops.RESID, Ly.down.s, bb.err, out=bb.h, ldo=d, ss_out=ss[2 * l + 2]),
+                "partial": ops.epi(ops.PARTIAL, Ly.wo.s, bb.err),
+            })
+        out.append({"lm": ops.epi(ops.STORE, m.lm.s, bb.err, out=bb.logits_local, ldo=m.lm.M)})
+        bb.epis = out
+        return out
 
     def decode_step(self, bb: StepBuffers) -> None:
         """forward + sample for every slot; slots advance in place."""

@@ -153,6 +153,34 @@ __host__ __device__ __forceinline__ uint32_t idesc_i8(int M, int N) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with the PDL attribute
+// may start while its predecessor still runs; it must call pdl_wait()
+// before touching anything the predecessor writes.  Both are no-ops for a
+// normal launch.
+__device__ __forceinline__ void pdl_wait_dep() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_allow_next() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// Process-wide switch (arcb_set_pdl) read by every launcher.
+int arcb_pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+static inline int launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                           Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = arcb_pdl_enabled();
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k, ((KArgs)args)...);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ void red_add_s32(int* p, int v) {
   asm volatile("red.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");

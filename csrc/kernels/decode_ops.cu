@@ -25,6 +25,8 @@
 #include "common.cuh"
 #include "lut.cuh"
 
+extern "C" int arcb_get_pdl(void);
+
 using namespace q16;
 
 namespace {
@@ -125,6 +127,8 @@ __device__ __forceinline__ uint64_t sq16(int64_t x) { return (uint64_t)(wmul(x, 
 __global__ void k_embed(const int* __restrict__ tokens, const int8_t* __restrict__ emb,
                         const int64_t* __restrict__ emb_s, int V, int d, int B, int64_t* __restrict__ h,
                         int* __restrict__ counters, int ncounters, uint64_t* __restrict__ ss, int nss) {
+  pdl_wait_dep();
+  pdl_allow_next();
   __shared__ uint64_t sh[32];
   const int b = blockIdx.x;
   const uint32_t tok = (uint32_t)tokens[b];
@@ -148,6 +152,8 @@ __global__ void k_embed(const int* __restrict__ tokens, const int8_t* __restrict
 __global__ void k_norm_limbs(const int64_t* __restrict__ h, const uint64_t* __restrict__ ss,
                              const int64_t* __restrict__ gamma, int ngamma, int d, int B, int8_t* __restrict__ X,
                              int* __restrict__ lmax, int64_t* __restrict__ y_out) {
+  pdl_wait_dep();
+  pdl_allow_next();
   __shared__ int shi[32];
   const int b = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
@@ -167,6 +173,8 @@ __global__ void k_norm_limbs(const int64_t* __restrict__ h, const uint64_t* __re
 __global__ void k_rmsnorm_limbs(const int64_t* __restrict__ h, const int64_t* __restrict__ gamma, int ngamma,
                                 int d, int B, int8_t* __restrict__ X, int* __restrict__ lmax,
                                 int64_t* __restrict__ y_out) {
+  pdl_wait_dep();
+  pdl_allow_next();
   __shared__ uint64_t sh[32];
   __shared__ int shi[32];
   const int b = blockIdx.x;
@@ -191,6 +199,8 @@ __global__ void k_rmsnorm_limbs(const int64_t* __restrict__ h, const int64_t* __
 __global__ void k_finalize(int* __restrict__ P, int M, int B, const int* __restrict__ lmax,
                            const int64_t* __restrict__ scales, int64_t* __restrict__ out, int ldo, int mode,
                            uint64_t* __restrict__ ss_out) {
+  pdl_wait_dep();
+  pdl_allow_next();
   __shared__ uint64_t sh[32];
   const int b = blockIdx.y;
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
@@ -216,6 +226,8 @@ __global__ void k_finalize_qkv(int* __restrict__ P, int B, const int* __restrict
                                int64_t* __restrict__ Vc, const int* __restrict__ pt, int pt_stride,
                                const int* __restrict__ pos, const int64_t* __restrict__ rcos,
                                const int64_t* __restrict__ rsin, int max_seq, int* __restrict__ err) {
+  pdl_wait_dep();
+  pdl_allow_next();
   const int b = blockIdx.y;
   const int half = dh / 2;
   const int d = n_heads * dh, dkv = n_kv * dh;
@@ -261,6 +273,8 @@ __global__ void k_finalize_qkv(int* __restrict__ P, int B, const int* __restrict
 __global__ void k_finalize_swiglu(int* __restrict__ P, int dff, int B, const int* __restrict__ lmax,
                                   const int64_t* __restrict__ scales, int8_t* __restrict__ X,
                                   int* __restrict__ lmax_out, int64_t* __restrict__ y_out) {
+  pdl_wait_dep();
+  pdl_allow_next();
   __shared__ int shi[32];
   const int b = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
@@ -295,6 +309,8 @@ __global__ void k_attn_scores(const int64_t* __restrict__ q, const int64_t* __re
                               const int* __restrict__ pt, int pt_stride, const int* __restrict__ pos,
                               int n_heads, int n_kv, int dh, int64_t attn_scale, int chunk, int max_T,
                               int64_t* __restrict__ S, long long* __restrict__ Mx, int* __restrict__ err) {
+  pdl_wait_dep();
+  pdl_allow_next();
   __shared__ int64_t qs[256];
   __shared__ int64_t shm[32];
   const int hq = blockIdx.x, b = blockIdx.y;
@@ -346,6 +362,8 @@ __global__ void k_attn_pv(const int64_t* __restrict__ Vc, const int* __restrict_
                           const int64_t* __restrict__ S, long long* __restrict__ Mx,
                           unsigned long long* __restrict__ O, int* __restrict__ cnt, int B,
                           int8_t* __restrict__ X, int* __restrict__ lmax, int64_t* __restrict__ o_out) {
+  pdl_wait_dep();
+  pdl_allow_next();
   __shared__ int64_t lut[EXP_LUT_N];
   __shared__ int64_t wsh[512];
   __shared__ uint64_t shu[32];
@@ -423,6 +441,8 @@ __global__ void k_sample(int64_t* __restrict__ logits, int ldl, int V, const int
                          int* __restrict__ hist, int* __restrict__ count, int* __restrict__ gen, int gen_cap,
                          int* __restrict__ tokens_next, int* __restrict__ pos_inc, int* __restrict__ done,
                          const int* __restrict__ eos, int n_eos) {
+  pdl_wait_dep();
+  pdl_allow_next();
   __shared__ int64_t sv[32];
   __shared__ int si[32];
   const int s = blockIdx.x;
@@ -490,10 +510,14 @@ __global__ void k_sample(int64_t* __restrict__ logits, int ldl, int V, const int
 
 }  // namespace
 
+int arcb_pdl_enabled() { return arcb_get_pdl(); }
+
 #include "../common/rng.h"
 
 namespace {
 __global__ void k_rng_i8(uint64_t key, int8_t* __restrict__ out, int64_t n) {
+  pdl_wait_dep();
+  pdl_allow_next();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = arcrng::weight_i8(key, (uint64_t)i);
 }
@@ -502,32 +526,32 @@ __global__ void k_rng_i8(uint64_t key, int8_t* __restrict__ out, int64_t n) {
 // ==================================================================== C ABI
 extern "C" {
 
+static int g_pdl = 1;
+void arcb_set_pdl(int on) { g_pdl = on ? 1 : 0; }
+int arcb_get_pdl(void) { return g_pdl; }
+
 static inline cudaStream_t S_(void* s) { return (cudaStream_t)s; }
 
 int arcb_embed(const int* tokens, const int8_t* emb, const int64_t* emb_s, int V, int d, int B, int64_t* h,
                int* counters, int ncounters, uint64_t* ss, int nss, void* st) {
-  k_embed<<<B, 512, 0, S_(st)>>>(tokens, emb, emb_s, V, d, B, h, counters, ncounters, ss, nss);
-  return (int)cudaGetLastError();
+  return launch_k(k_embed, dim3(B), dim3(512), 0, S_(st), tokens, emb, emb_s, V, d, B, h, counters, ncounters, ss, nss);
 }
 
 int arcb_norm_limbs(const int64_t* h, const uint64_t* ss, const int64_t* gamma, int ngamma, int d, int B,
                     int8_t* X, int* lmax, int64_t* y_out, void* st) {
   dim3 g((d + 255) / 256, B);
-  k_norm_limbs<<<g, 256, 0, S_(st)>>>(h, ss, gamma, ngamma, d, B, X, lmax, y_out);
-  return (int)cudaGetLastError();
+  return launch_k(k_norm_limbs, dim3(g), dim3(256), 0, S_(st), h, ss, gamma, ngamma, d, B, X, lmax, y_out);
 }
 
 int arcb_rmsnorm_limbs(const int64_t* h, const int64_t* gamma, int ngamma, int d, int B, int8_t* X, int* lmax,
                        int64_t* y_out, void* st) {
-  k_rmsnorm_limbs<<<B, 512, 0, S_(st)>>>(h, gamma, ngamma, d, B, X, lmax, y_out);
-  return (int)cudaGetLastError();
+  return launch_k(k_rmsnorm_limbs, dim3(B), dim3(512), 0, S_(st), h, gamma, ngamma, d, B, X, lmax, y_out);
 }
 
 int arcb_finalize(int* P, int M, int B, const int* lmax, const int64_t* scales, int64_t* out, int ldo, int mode,
                   uint64_t* ss_out, void* st) {
   dim3 g((M + 255) / 256, B);
-  k_finalize<<<g, 256, 0, S_(st)>>>(P, M, B, lmax, scales, out, ldo, mode, ss_out);
-  return (int)cudaGetLastError();
+  return launch_k(k_finalize, dim3(g), dim3(256), 0, S_(st), P, M, B, lmax, scales, out, ldo, mode, ss_out);
 }
 
 int arcb_finalize_qkv(int* P, int B, const int* lmax, const int64_t* scales, int n_heads, int n_kv, int dh,
@@ -536,16 +560,14 @@ int arcb_finalize_qkv(int* P, int B, const int* lmax, const int64_t* scales, int
   const int d = n_heads * dh, dkv = n_kv * dh;
   const int n = d / 2 + dkv / 2 + dkv;
   dim3 g((n + 127) / 128, B);
-  k_finalize_qkv<<<g, 128, 0, S_(st)>>>(P, B, lmax, scales, n_heads, n_kv, dh, q_out, Kc, Vc, pt, pt_stride, pos,
+  return launch_k(k_finalize_qkv, dim3(g), dim3(128), 0, S_(st), P, B, lmax, scales, n_heads, n_kv, dh, q_out, Kc, Vc, pt, pt_stride, pos,
                                          rcos, rsin, max_seq, err);
-  return (int)cudaGetLastError();
 }
 
 int arcb_finalize_swiglu(int* P, int dff, int B, const int* lmax, const int64_t* scales, int8_t* X,
                          int* lmax_out, int64_t* y_out, void* st) {
   dim3 g((dff + 255) / 256, B);
-  k_finalize_swiglu<<<g, 256, 0, S_(st)>>>(P, dff, B, lmax, scales, X, lmax_out, y_out);
-  return (int)cudaGetLastError();
+  return launch_k(k_finalize_swiglu, dim3(g), dim3(256), 0, S_(st), P, dff, B, lmax, scales, X, lmax_out, y_out);
 }
 
 // Attention scratch: S [B, n_heads, max_T] i64, Mx [B, n_heads] (init
@@ -557,18 +579,16 @@ int arcb_attn_decode(const int64_t* q, const int64_t* Kc, const int64_t* Vc, con
   if (dh > 256 || chunk > 512 || chunk < 1) return -1;
   const int nsplit = (max_T + chunk - 1) / chunk;
   dim3 g(n_heads, B, nsplit);
-  k_attn_scores<<<g, 128, 0, S_(st)>>>(q, Kc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, chunk, max_T, S,
+  int rc = launch_k(k_attn_scores, g, dim3(128), 0, S_(st), q, Kc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, chunk, max_T, S,
                                         Mx, err);
-  k_attn_pv<<<g, 128, 0, S_(st)>>>(Vc, pt, pt_stride, pos, n_heads, n_kv, dh, chunk, max_T, S, Mx, O, cnt, B, X,
+  return launch_k(k_attn_pv, dim3(g), dim3(128), 0, S_(st), Vc, pt, pt_stride, pos, n_heads, n_kv, dh, chunk, max_T, S, Mx, O, cnt, B, X,
                                     lmax, o_out);
-  return (int)cudaGetLastError();
 }
 
 int arcb_sample(int64_t* logits, int ldl, int V, const int* lrow, int S, int* hist, int* count, int* gen,
                 int gen_cap, int* tokens_next, int* pos_inc, int* done, const int* eos, int n_eos, void* st) {
-  k_sample<<<S, 1024, 0, S_(st)>>>(logits, ldl, V, lrow, hist, count, gen, gen_cap, tokens_next, pos_inc, done,
+  return launch_k(k_sample, dim3(S), dim3(1024), 0, S_(st), logits, ldl, V, lrow, hist, count, gen, gen_cap, tokens_next, pos_inc, done,
                                     eos, n_eos);
-  return (int)cudaGetLastError();
 }
 
 int arcb_rng_i8(uint64_t seed, uint64_t stream, int8_t* out, int64_t n, void* st) {
@@ -576,8 +596,7 @@ int arcb_rng_i8(uint64_t seed, uint64_t stream, int8_t* out, int64_t n, void* st
   int blocks = (int)((n + 255) / 256);
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (blocks < 1) blocks = 1;
-  k_rng_i8<<<blocks, 256, 0, S_(st)>>>(key, out, n);
-  return (int)cudaGetLastError();
+  return launch_k(k_rng_i8, dim3(blocks), dim3(256), 0, S_(st), key, out, n);
 }
 
 }  // extern "C"

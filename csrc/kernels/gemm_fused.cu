@@ -1,0 +1,484 @@
+// K1 (fused): persistent stream-K int8 x int64 limb GEMM with the finalize
+// fused into the epilogue.  Same exact arithmetic as gemm_i8.cu (signed
+// radix-256 limb planes, tcgen05.mma kind::i8, s32 partials in TMEM); what
+// changes is the schedule and what happens after the MMA:
+//
+//  * Persistent: one CTA per SM.  The work list is every (n-tile, m-tile,
+//    128-byte K chunk) item; CTA c takes a contiguous, balanced range of it,
+//    so the TMA stream of weights never drains between tiles and no SM idles
+//    (stream-K).  A range is cut into segments (runs of one (n, m) tile); each
+//    segment accumulates into one of two TMEM buffers, so the epilogue of a
+//    segment overlaps the MMAs of the next.
+//  * Fused finalize: a segment that covers a whole tile finalizes straight
+//    from TMEM; otherwise it adds its int32 partials into P (red.global.add)
+//    and the CTA whose arrival completes the tile's counter finalizes from P
+//    (integer adds: order free, exact) and zeroes what it read.
+//  * Epilogue modes: store (LM head), residual add + next-norm sum of squares
+//    (W_o, W_down), RoPE + paged KV append (QKV, rows of a head interleaved as
+//    (e, e + d_head/2) pairs so a lane pair holds a rotation pair), SwiGLU +
+//    limb split for the next GEMM (gate/up rows interleaved), partial-only
+//    (tensor-parallel partials reduced by the caller).
+//  * Programmatic dependent launch: the producer issues the first weight
+//    tiles before griddepcontrol.wait, so weights stream in while the
+//    previous kernel (norm, attention) is still finishing.
+//
+// Warp roles (192 threads): warp 0 lane 0 TMA producer, warp 1 lane 0 MMA
+// issuer (warp 1 owns the TMEM allocation), warps 2-5 epilogue (TMEM lane
+// quarter = warp % 4).  All waits are bounded (common.cuh).
+#include <climits>
+
+#include "common.cuh"
+#include "lut.cuh"
+
+using namespace q16;
+
+namespace fg {
+
+constexpr int BM = 128;
+constexpr int BK = 128;
+constexpr int NTHREADS = 192;
+constexpr int PAGE = 16;
+
+enum Mode : int { PARTIAL = 0, STORE = 1, RESID = 2, QKV = 3, SWIGLU = 4 };
+
+struct Epi {
+  int mode;
+  const int64_t* scales;  // per fused row
+  int64_t* out;           // STORE / RESID target [B, ldo]
+  int ldo;
+  unsigned long long* ss_out;  // RESID: next norm's sum of squares per slot
+  // QKV
+  int n_heads, n_kv, dh;
+  int64_t* q_out;
+  int64_t* Kc;
+  int64_t* Vc;
+  const int* pt;
+  int pt_stride;
+  const int* pos;
+  const int64_t* rcos;
+  const int64_t* rsin;
+  int max_seq;
+  // SWIGLU: limb planes of the next GEMM's operand [8][B][ldx]
+  int8_t* X;
+  int ldx;
+  int* lmax_out;
+  int* err;
+  int B;  // slots in the step (plane stride of X = B * ldx)
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN <= 16 ? 11 : (BN <= 32 ? 10 : (BN <= 64 ? 8 : (BN <= 128 ? 6 : 4)));
+  static constexpr int ACC_COLS = BN < 32 ? 32 : BN;       // one TMEM accumulator
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;          // double buffered
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+};
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld1(uint32_t taddr, uint32_t& r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+}
+
+__device__ __forceinline__ uint64_t sq16(int64_t x) { return (uint64_t)(wmul(x, x) >> FRAC_BITS); }
+
+__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
+  return v;
+}
+
+// Applies the epilogue to output row m (fused-row index) of slot b, given the
+// recombined wrapping accumulator acc = sum_k W[m,k] x_b[k].  Called by all 32
+// lanes of a warp together (rows m0..m0+31) so pair exchanges can shuffle.
+__device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid, int b, uint64_t acc,
+                                          int& need) {
+  const int64_t s = valid ? E.scales[m] : 0;
+  const int64_t v = mulshr((int64_t)acc, s);
+  const int lane = threadIdx.x & 31;
+  switch (E.mode) {
+    case STORE:
+      if (valid) E.out[(size_t)b * E.ldo + m] = v;
+      break;
+    case RESID: {
+      uint64_t sq = 0;
+      if (valid) {
+        int64_t* o = E.out + (size_t)b * E.ldo + m;
+        const int64_t r = wadd(*o, v);
+        *o = r;
+        sq = sq16(r);
+      }
+      if (E.ss_out) {
+        sq = warp_sum_u64(sq);
+        if (lane == 0) atomicAdd(E.ss_out + b, (unsigned long long)sq);
+      }
+      break;
+    }
+    case QKV: {
+      const int d = E.n_heads * E.dh, dkv = E.n_kv * E.dh, half = E.dh / 2;
+      const int64_t partner = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, 1);
+      if (!valid) break;
+      const int p = E.pos[b];
+      if (p < 0 || p >= E.max_seq) {
+        set_error(E.err, ARCB_ERR_SEQ_OVERFLOW);
+        break;
+      }
+      const int page = E.pt[(size_t)b * E.pt_stride + p / PAGE];
+      const int slot = p % PAGE;
+      if (m < d + dkv) {
+        const bool is_q = m < d;
+        const int r = is_q ? m : m - d;
+        const int head = r / E.dh, w = r % E.dh, i = w >> 1, role = w & 1;
+        int64_t x0 = role ? partner : v, x1 = role ? v : partner;
+        rope_pair(x0, x1, E.rcos[(size_t)p * half + i], E.rsin[(size_t)p * half + i]);
+        const int e = role ? i + half : i;
+        const int64_t y = role ? x1 : x0;
+        if (is_q) E.q_out[(size_t)b * d + head * E.dh + e] = y;
+        else E.Kc[(((size_t)page * E.n_kv + head) * PAGE + slot) * E.dh + e] = y;
+      } else {
+        const int j = m - d - dkv;
+        E.Vc[(((size_t)page * E.n_kv + j / E.dh) * PAGE + slot) * E.dh + (j % E.dh)] = v;
+      }
+      break;
+    }
+    case SWIGLU: {
+      const int64_t partner = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, 1);
+      if (valid && (m & 1) == 0) {
+        const int j = m >> 1;
+        const int64_t y = swiglu(v, partner, g_exp_lut.v);
+        int8_t dg[8];
+        const int n = limb_split8(y, dg);
+        need = n > need ? n : need;
+        const size_t ps = (size_t)E.ldx * E.B;
+        const size_t off = (size_t)b * E.ldx + j;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) E.X[l * ps + off] = dg[l];
+      }
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Work item -> (n-tile, m-tile, chunk); CTA c owns items [it0, it1).
+struct Work {
+  int Mt, nch, it0, it1;
+  __device__ void range(int ntu) {
+    const long long total = (long long)ntu * Mt * nch;
+    it0 = (int)(total * blockIdx.x / gridDim.x);
+    it1 = (int)(total * (blockIdx.x + 1) / gridDim.x);
+  }
+  __device__ int nt(int it) const { return it / (Mt * nch); }
+  __device__ int mt(int it) const { return (it / nch) % Mt; }
+  __device__ int kc(int it) const { return it % nch; }
+  __device__ int seg_end(int it) const { return min(it1, (it / nch + 1) * nch); }
+};
+
+template <int BN>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_gemm_fused(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
+                 int B, int n_tiles_max, int prefetch_ok, const int* __restrict__ lmax, int* __restrict__ P,
+                 int* __restrict__ tile_cnt, const __grid_constant__ Epi E) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t a_base = base;
+  const uint32_t b_base = base + C::STAGES * C::A_BYTES;
+  const uint32_t bar = b_base + C::STAGES * C::B_BYTES;
+  auto full = [&](int s) { return bar + 8u * s; };
+  auto empty = [&](int s) { return bar + 8u * (C::STAGES + s); };
+  auto seg_full = [&](int t) { return bar + 8u * (2 * C::STAGES + t); };
+  auto seg_free = [&](int t) { return bar + 8u * (2 * C::STAGES + 2 + t); };
+  const uint32_t tslot = bar + 8u * (2 * C::STAGES + 4);
+  volatile uint32_t* tslot_ptr = (volatile uint32_t*)(smem_raw + (tslot - raw));
+  volatile int* flag_ptr = (volatile int*)(smem_raw + (tslot + 8 - raw));
+  volatile int* ok_ptr = (volatile int*)(smem_raw + (tslot + 12 - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  Work W{(M + BM - 1) / BM, (K + BK - 1) / BK, 0, 0};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(seg_full(t), 1);
+      mbar_init(seg_free(t), 4);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot_ptr;
+  pdl_launch();
+
+  // Weights do not depend on the previous kernel: start streaming them.
+  int pre = 0;
+  if (warp == 0 && lane == 0 && prefetch_ok) {
+    W.range(1);
+    pre = min(C::STAGES, W.it1 - W.it0);
+    for (int i = 0; i < pre; ++i) {
+      const int it = W.it0 + i;
+      mbar_arrive_expect_tx(full(i), C::STAGE_BYTES);
+      tma_load_2d(a_base + i * C::A_BYTES, &tmA, full(i), W.kc(it) * BK, W.mt(it) * BM);
+    }
+  }
+  pdl_wait();
+  const int L = max(1, *lmax);
+  const int nrows = L * B;
+  const int ntu = min(n_tiles_max, (nrows + BN - 1) / BN);
+  W.range(ntu);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      const int n = W.it1 - W.it0;
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < n; ++i) {
+        const int it = W.it0 + i, s = i % C::STAGES;
+        const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
+        const int kx = W.kc(it) * BK;
+        if (i < pre) {
+          tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, W.nt(it) * BN);
+          ++issued;
+          continue;
+        }
+        if (i >= C::STAGES && !mbar_wait(empty(s), ph ^ 1u)) {
+          set_error(E.err, ARCB_ERR_TIMEOUT_EMPTY);
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(full(s), C::STAGE_BYTES);
+        tma_load_2d(a_base + s * C::A_BYTES, &tmA, full(s), kx, W.mt(it) * BM);
+        tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, W.nt(it) * BN);
+        ++issued;
+      }
+      if (!ok)
+        for (int i = max(0, issued - C::STAGES); i < issued; ++i)
+          mbar_wait(full(i % C::STAGES), (uint32_t)(i / C::STAGES) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      int i = 0, seg = 0;
+      bool ok = true;
+      for (int it = W.it0; it < W.it1 && ok; ++seg) {
+        const int se = W.seg_end(it), tb = seg & 1;
+        if (seg >= 2 && !mbar_wait(seg_free(tb), (uint32_t)((seg >> 1) - 1) & 1u)) {
+          set_error(E.err, ARCB_ERR_TIMEOUT_DONE);
+          break;
+        }
+        tc_fence_after();
+        const int n0 = W.nt(it) * BN;
+        const int n_mma = (min(BN, nrows - n0) + 15) & ~15;
+        const uint32_t idesc = idesc_i8(BM, n_mma);
+        const uint32_t dst = tmem + (uint32_t)(tb * C::ACC_COLS);
+        for (int j = it; j < se; ++j, ++i) {
+          const int s = i % C::STAGES;
+          if (!mbar_wait(full(s), (uint32_t)(i / C::STAGES) & 1u)) {
+            set_error(E.err, ARCB_ERR_TIMEOUT_FULL);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            const uint64_t ad = sw128_kmajor_desc(a_base + s * C::A_BYTES + kk * 32);
+            const uint64_t bd = sw128_kmajor_desc(b_base + s * C::B_BYTES + kk * 32);
+            mma_i8(dst, ad, bd, idesc, (j > it || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(empty(s));
+        }
+        mma_commit(seg_full(tb));
+        it = se;
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5
+    const int q = warp & 3;
+    int seg = 0;
+    for (int it = W.it0; it < W.it1; ++seg) {
+      const int se = W.seg_end(it), tb = seg & 1;
+      const int nt = W.nt(it), mt = W.mt(it);
+      // One thread waits (bounded); the four warps then branch together, since
+      // the named barriers below have no timeout of their own.
+      if (warp == 2 && lane == 0) *ok_ptr = mbar_wait(seg_full(tb), (uint32_t)(seg >> 1) & 1u) ? 1 : 0;
+      epi_bar();
+      const bool got = *ok_ptr != 0;
+      epi_bar();
+      if (!got) {
+        set_error(E.err, ARCB_ERR_TIMEOUT_DONE);
+        break;
+      }
+      tc_fence_after();
+      const int m = mt * BM + q * 32 + lane;
+      const bool valid = m < M;
+      const int n0 = nt * BN;
+      const int n_mma = (min(BN, nrows - n0) + 15) & ~15;
+      const bool whole = (W.kc(it) == 0) && (se - it == W.nch);
+      const bool direct = whole && ntu == 1 && E.mode != PARTIAL;
+      const uint32_t taddr = tmem + (uint32_t)(tb * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
+      int need = 0;
+      if (direct) {
+        for (int b = 0; b < B; ++b) {
+          uint32_t r[8];
+          for (int l = 0; l < L; ++l) tmem_ld1(taddr + (uint32_t)(l * B + b), r[l]);
+          tmem_ld_wait();
+          uint64_t acc = 0;
+          for (int l = 0; l < L; ++l) acc += (uint64_t)(int64_t)(int)r[l] << (8 * l);
+          apply_row(E, M, m, valid, b, acc, need);
+        }
+      } else {
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + (uint32_t)c0, r);
+          tmem_ld_wait();
+          if (valid) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int n = n0 + c0 + j;
+              if (n < nrows && r[j] != 0) red_add_s32(P + (size_t)n * M + m, (int)r[j]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(seg_free(tb));
+      if (!direct && E.mode != PARTIAL) {
+        __threadfence();
+        epi_bar();
+        if (warp == 2 && lane == 0) {
+          const int add = se - it;
+          const int old = atomicAdd(tile_cnt + mt, add);
+          *flag_ptr = (old + add == ntu * W.nch) ? 1 : 0;
+        }
+        epi_bar();
+        const bool last = *flag_ptr != 0;
+        if (last) {
+          __threadfence();
+          for (int b = 0; b < B; ++b) {
+            uint64_t acc = 0;
+            if (valid)
+              for (int l = 0; l < L; ++l) {
+                int* p = P + (size_t)(l * B + b) * M + m;
+                acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
+                *p = 0;
+              }
+            apply_row(E, M, m, valid, b, acc, need);
+          }
+          if (warp == 2 && lane == 0) tile_cnt[mt] = 0;
+        }
+        epi_bar();
+      }
+      if (E.mode == SWIGLU && E.lmax_out) {
+        need = __reduce_max_sync(0xffffffffu, need);
+        if (lane == 0 && need > 0) atomicMax(E.lmax_out, need);
+      }
+      it = se;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN>
+int launch(const CUtensorMap* a, const CUtensorMap* b, int M, int K, int B, const int* lmax, int* P, int* cnt,
+           const Epi& E, cudaStream_t st, int pdl) {
+  using C = Cfg<BN>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_fused<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return (int)e;
+    attr = true;
+  }
+  const int n_tiles_max = (8 * B + BN - 1) / BN;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms());
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_fused<BN>, *a, *b, M, K, B, n_tiles_max,
+                                     (int)(n_tiles_max == 1), lmax, P, cnt, E);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+}  // namespace fg
+
+extern "C" {
+
+// Box height for the fused GEMM's limb operand: all 8 planes of B slots fit
+// one N tile up to B = 32 (so the work list is known before the dependency
+// wait and weight prefetch is allowed); larger batches tile N by 256.
+int arcb_fgemm_bn(int B) {
+  const int want = 8 * B;
+  if (want <= 16) return 16;
+  if (want <= 32) return 32;
+  if (want <= 64) return 64;
+  if (want <= 128) return 128;
+  return 256;
+}
+
+// Fused GEMM + epilogue.  `epi` points to an fg::Epi in host memory (copied
+// into the launch).  tile_cnt: zeroed int array with one entry per M tile.
+int arcb_fgemm(const void* tmA, const void* tmB, int M, int K, int B, int bn, const int* lmax, int* P,
+               int* tile_cnt, const void* epi, int pdl, void* stream) {
+  const CUtensorMap* a = (const CUtensorMap*)tmA;
+  const CUtensorMap* b = (const CUtensorMap*)tmB;
+  fg::Epi E = *(const fg::Epi*)epi;
+  pdl = pdl && arcb_pdl_enabled();
+  E.B = B;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (bn) {
+    case 16: return fg::launch<16>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
+    case 32: return fg::launch<32>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
+    case 64: return fg::launch<64>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
+    case 128: return fg::launch<128>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
+    case 256: return fg::launch<256>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
+  }
+  return -3;
+}
+
+int arcb_fgemm_epi_size(void) { return (int)sizeof(fg::Epi); }
+
+}  // extern "C"

@@ -69,6 +69,42 @@ def test_gemm_i8_exact(M, K, B, mag):
         assert int(P.abs().max().item()) == 0  # finalize zeroed the partials
 
 
+@pytest.mark.parametrize("M,K,B,mag", [(128, 128, 1, 1 << 17), (4096, 4096, 1, 1 << 18), (1000, 688, 3, 1 << 40),
+                                       (32000, 256, 2, 1 << 20), (640, 1024, 40, 1 << 17), (384, 512, 33, 1 << 62),
+                                       (256, 2048, 130, 1 << 23)])
+def test_fused_gemm_store_and_partial(M, K, B, mag):
+    """Persistent stream-K GEMM: STORE epilogue (fused finalize) and PARTIAL."""
+    ops = _ops()
+    rng = np.random.default_rng(M + 3 * K + B)
+    w = rng.integers(-127, 128, size=(M, K), dtype=np.int64).astype(np.int8)
+    s = rng.integers(1, 5000, size=M).astype(np.int64)
+    x = rng.integers(-mag, mag, size=(B, K), dtype=np.int64)
+    planes, need = _limbs(x, B, K)
+    bn = ops.fgemm_bn(B)
+    if planes.shape[0] < bn:
+        planes = np.concatenate([planes, np.zeros((bn - planes.shape[0], K), np.int8)])
+    dev = torch.device("cuda")
+    W, X, S = (torch.from_numpy(a).to(dev) for a in (w, planes, s))
+    wm, xm = ops.TensorMap(W, 128), ops.TensorMap(X, bn)
+    lmax = torch.tensor([need], dtype=torch.int32, device=dev)
+    P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
+    tiles = torch.zeros((M + 127) // 128 + 1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.zeros(B, M, dtype=torch.int64, device=dev)
+    ref = np.stack([arcref.matmul_i8(w, s, x[b]) for b in range(B)])
+    for rep in range(2):
+        out.zero_()
+        ops.fgemm(wm, xm, M, K, B, lmax, P, tiles, ops.epi(ops.STORE, S, err, out=out, ldo=M))
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        np.testing.assert_array_equal(out.cpu().numpy(), ref)
+        assert int(P.abs().max().item()) == 0 and int(tiles.abs().max().item()) == 0
+    ops.fgemm(wm, xm, M, K, B, lmax, P, tiles, ops.epi(ops.PARTIAL, S, err))
+    ops.finalize(P, M, B, lmax, S, out, M, 0)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
 def test_rmsnorm_limbs_exact():
     ops = _ops()
     rng = np.random.default_rng(1)
