@@ -1,0 +1,112 @@
+"""Kernel microbenchmarks with roofline fractions.
+
+Times each hot kernel alone with CUDA events after warm-up, rotating over
+enough weight copies that every launch streams from HBM (working set > the
+126 MB L2).  Reports achieved bandwidth against the measured HBM copy peak
+(MEASURED_PEAKS.json ``hbm_gbs``; 6650 GB/s fallback) as JSON lines.
+
+    python -m arc_chain_b200.bench.kernels [--shape 22016x4096] [--B 1] [--iters 50]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+from arc_chain_b200.ops import int_ops as ops
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+SHAPES_7B = {"qkv": (12288, 4096), "wo": (4096, 4096), "gate_up": (22016, 4096), "down": (4096, 11008),
+             "lm_head": (32000, 4096)}
+
+
+def hbm_peak_gbs() -> float:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except Exception:
+        return 6650.0
+
+
+def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True):
+    dev = torch.device("cuda")
+    nbytes = M * K
+    copies = max(2, -(-300_000_000 // nbytes))
+    Ws = [ops.tile_weight(torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev)) for _ in range(copies)]
+    maps = [ops.TensorMap(w, 128) for w in Ws]
+    S = torch.randint(1, 100, (M,), dtype=torch.int64, device=dev)
+    bn = ops.fgemm_bn(B)
+    X = torch.randint(-127, 128, (max(8 * B, bn), K), dtype=torch.int8, device=dev)
+    xm = ops.TensorMap(X, bn)
+    lmax = torch.tensor([3], dtype=torch.int32, device=dev)
+    P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
+    tiles = torch.zeros(M // 128 + 2, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.zeros(B, M, dtype=torch.int64, device=dev)
+    e = ops.epi(ops.STORE if mode == "store" else ops.PARTIAL, S, err, out=out, ldo=M)
+    ops.set_pdl(pdl)
+    for i in range(5):
+        ops.fgemm(maps[i % copies], xm, M, K, B, lmax, P, tiles, e)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(iters):
+        ops.fgemm(maps[i % copies], xm, M, K, B, lmax, P, tiles, e)
+    t1.record()
+    torch.cuda.synchronize()
+    us = t0.elapsed_time(t1) * 1000 / iters
+    gbs = nbytes / us / 1e3
+    assert int(err.item()) == 0
+    return {"kernel": "fgemm", "M": M, "K": K, "B": B, "mode": mode, "pdl": pdl, "us": round(us, 2),
+            "GB_s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak_gbs(), 3)}
+
+
+def bench_attn(T, n_heads=32, dh=128, B=1, iters=50):
+    dev = torch.device("cuda")
+    pages = (T + 15) // 16
+    npg = pages * B
+    K = torch.randint(-(1 << 18), 1 << 18, (npg, n_heads, 16, dh), dtype=torch.int64, device=dev)
+    V = torch.randint(-(1 << 18), 1 << 18, (npg, n_heads, 16, dh), dtype=torch.int64, device=dev)
+    q = torch.randint(-(1 << 18), 1 << 18, (B, n_heads * dh), dtype=torch.int64, device=dev)
+    pt = torch.arange(npg, dtype=torch.int32, device=dev).view(B, pages)
+    pos = torch.full((B,), T - 1, dtype=torch.int32, device=dev)
+    X = torch.zeros(8 * B, n_heads * dh, dtype=torch.int8, device=dev)
+    lm = torch.zeros(1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    for _ in range(3):
+        ops.attn(q, K, V, pt, pos, n_heads, n_heads, dh, 5793, B, X, lm, pages * 16, err)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(iters):
+        ops.attn(q, K, V, pt, pos, n_heads, n_heads, dh, 5793, B, X, lm, pages * 16, err)
+    t1.record()
+    torch.cuda.synchronize()
+    us = t0.elapsed_time(t1) * 1000 / iters
+    nbytes = 2 * B * T * n_heads * dh * 8
+    return {"kernel": "attn_cluster", "T": T, "heads": n_heads, "B": B, "us": round(us, 2),
+            "GB_s": round(nbytes / us / 1e3, 1), "cluster": ops.attn_cluster_size(B, n_heads)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--B", type=int, default=1)
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--only", default="")
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    if a.only in ("", "gemm"):
+        for name, (M, K) in SHAPES_7B.items():
+            for pdl in (True, False):
+                r = bench_fgemm(M, K, a.B, a.iters, pdl=pdl)
+                r["name"] = name
+                print(json.dumps(r), flush=True)
+    if a.only in ("", "attn"):
+        for T in (130, 386, 1024, 2048):
+            print(json.dumps(bench_attn(T, B=a.B, iters=a.iters)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

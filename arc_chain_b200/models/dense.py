@@ -27,21 +27,24 @@ from arc_chain_b200.ops import int_ops as ops
 
 @dataclass
 class Linear:
-    w: torch.Tensor          # int8 [M, K]
+    """One INT8 matrix with per-row Q16 scales.  ``build_map`` converts the
+    row-major [M, K] weight into the tiled layout the fused GEMM streams
+    (128x128-byte tiles, each contiguous) and encodes its TMA map."""
+
+    w: torch.Tensor          # int8 [M, K] row-major; tiled after build_map()
     s: torch.Tensor          # int64 [M]
     tmap: ops.TensorMap = None
-
-    @property
-    def M(self):
-        return self.w.shape[0]
-
-    @property
-    def K(self):
-        return self.w.shape[1]
+    M: int = 0
+    K: int = 0
 
     def build_map(self):
+        self.M, self.K = self.w.shape
+        self.w = ops.tile_weight(self.w)
         self.tmap = ops.TensorMap(self.w, ops.BM)
         return self
+
+    def row_major(self) -> torch.Tensor:
+        return ops.untile_weight(self.w, self.M, self.K)
 
 
 @dataclass

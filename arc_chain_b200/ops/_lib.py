@@ -29,6 +29,7 @@ _SIGS = {
                                vp, vp, vp]),
     "arcb_sample": (i32, [vp, i32, i32, vp, i32, vp, vp, vp, i32, vp, vp, vp, vp, i32, vp]),
     "arcb_rng_i8": (i32, [u64, u64, vp, i64, vp]),
+    "arcb_attn_cluster": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, i32, i64, i32, i32, i32, vp, vp, vp, vp, vp]),
     "arcb_fgemm_bn": (i32, [i32]),
     "arcb_fgemm": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp]),
     "arcb_fgemm_epi_size": (i32, []),

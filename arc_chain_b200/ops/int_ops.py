@@ -208,3 +208,38 @@ def epi(mode, scales, err, **kw) -> Epi:
 
 def set_pdl(on: bool) -> None:
     lib().arcb_set_pdl(int(on))
+
+
+def tile_weight(w: torch.Tensor) -> torch.Tensor:
+    """[M, K] int8 -> tiled [Mt*nch*128, 128]: tile (m, k) (128 rows x 128
+    bytes, zero padded at the M and K edges) is contiguous at row
+    (m*nch + k)*128, the order the fused GEMM streams it."""
+    M, K = w.shape
+    Mt, nch = (M + BM - 1) // BM, (K + BK - 1) // BK
+    if M % BM or K % BK:
+        wp = torch.zeros(Mt * BM, nch * BK, dtype=torch.int8, device=w.device)
+        wp[:M, :K] = w
+    else:
+        wp = w
+    return wp.view(Mt, BM, nch, BK).permute(0, 2, 1, 3).contiguous().view(Mt * nch * BM, BK)
+
+
+def untile_weight(t: torch.Tensor, M: int, K: int) -> torch.Tensor:
+    Mt, nch = (M + BM - 1) // BM, (K + BK - 1) // BK
+    return t.view(Mt, nch, BM, BK).permute(0, 2, 1, 3).reshape(Mt * BM, nch * BK)[:M, :K].contiguous()
+
+
+def attn_cluster_size(B: int, n_heads: int) -> int:
+    """CTAs per (slot, head): spread few heads over many SMs, keep one CTA
+    per head when the batch already fills the GPU."""
+    n = B * n_heads
+    return 8 if n <= 64 else (4 if n <= 128 else (2 if n <= 512 else 1))
+
+
+def attn(q, Kc, Vc, pt, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax, max_T, err, o_out=None, cluster=None):
+    """Exact paged decode attention, one launch (thread-block clusters)."""
+    _count()
+    cs = cluster or attn_cluster_size(B, n_heads)
+    check(lib().arcb_attn_cluster(_p(q), _p(Kc), _p(Vc), _p(pt), pt.shape[1], _p(pos), n_heads, n_kv, dh,
+                                  int(attn_scale), max_T, B, cs, _p(X), _p(lmax), _p(o_out), _p(err), _s()),
+          "attn_cluster")

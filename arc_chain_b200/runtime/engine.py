@@ -90,7 +90,6 @@ class StepBuffers:
         self.cnt = torch.zeros(4 * c.n_layers + 4, dtype=I32, device=dev)
         # per-norm sum of squares: [2 * n_layers + 1, B] (u64 bits in int64)
         self.ss = torch.zeros(2 * c.n_layers + 1, B, dtype=I64, device=dev)
-        self.attn = ops.AttnScratch(B, model.n_heads_local, dh, max_pages * PAGE, dev)
         self.err = torch.zeros(1, dtype=I32, device=dev)
         self.logits_local = torch.zeros(B, model.vocab_local, dtype=I64, device=dev)
         self.logits = self.logits_local if model.tp_size == 1 else torch.zeros(B, c.vocab, dtype=I64, device=dev)
@@ -146,8 +145,8 @@ class Engine:
             e = E[l]
             ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
             ops.fgemm(Ly.qkv.tmap, bb.mXd, Ly.qkv.M, Ly.qkv.K, B, c0, bb.P, bb.tiles, e["qkv"])
-            ops.attn_decode(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo,
-                            c1, self.max_pages * PAGE, bb.attn, bb.err)
+            ops.attn(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo, c1,
+                     self.max_pages * PAGE, bb.err)
             if reduce_in_kernel:
                 cm.fgemm_reduce(Ly.wo, bb.mXo, B, c1, bb, e["wo"])
             else:

@@ -1,0 +1,247 @@
+// K5: exact paged decode attention in one launch, one thread-block cluster
+// per (slot, query head).
+//
+// Integer semantics (crates/arc-inference/src/cached_integer_model.rs:
+// 1448-1476, softmax_i64 integer_lut.rs:78-100): score_j = ((q.k_j >> 16) *
+// attn_scale) >> 16 with wrapping i64 dots; w = softmax_i64(scores) which
+// needs the exact global max and the exact global sum of the LUT exps; and
+// o = sum_j (w_j * v_j) >> 16 rounded per term.  Online (running-max)
+// softmax would round differently, so the keys are split over the CTAs of a
+// cluster and the three cross-CTA reductions (max, sum of exps, partial
+// outputs) are exchanged through distributed shared memory between cluster
+// barriers: all integer, so the result does not depend on the split.
+//
+// grid = (CS, n_heads, B) with cluster (CS, 1, 1); CTA rank r takes keys
+// [r*ceil(T/CS), ...).  The output is written straight into the limb planes
+// of the W_o GEMM operand (signed radix-256 digits) with its limb count.
+#include <climits>
+
+#include "common.cuh"
+#include "lut.cuh"
+
+using namespace q16;
+
+namespace {
+
+constexpr int PAGE = 16;
+constexpr int NT = 128;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint64_t ld_cluster_u64(const void* local, uint32_t rank) {
+  uint32_t la = smem_u32(local), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+  uint64_t v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(ra) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
+  return v;
+}
+
+template <int CS>
+__global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
+                                                     const int64_t* __restrict__ Vc, const int* __restrict__ pt,
+                                                     int pt_stride, const int* __restrict__ pos, int n_heads,
+                                                     int n_kv, int dh, int64_t attn_scale, int max_T, int B,
+                                                     int8_t* __restrict__ X, int* __restrict__ lmax,
+                                                     int64_t* __restrict__ o_out, int* __restrict__ err) {
+  pdl_wait_dep();
+  pdl_allow_next();
+  extern __shared__ int64_t dyn[];
+  __shared__ int64_t lut[EXP_LUT_N];
+  __shared__ int64_t qs[256];
+  __shared__ unsigned long long xo[256];
+  __shared__ int64_t red[NT / 32];
+  __shared__ long long xmax;
+  __shared__ unsigned long long xsum;
+  __shared__ int xneed;
+  int64_t* sc = dyn;  // local scores, then exps, then weights
+
+  const uint32_t rank = cluster_rank();
+  const int hq = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = pos[b] + 1;
+  const bool bad = T > max_T || T < 1;
+  if (bad && rank == 0 && tid == 0) set_error(err, ARCB_ERR_SEQ_OVERFLOW);
+  const int chunk = bad ? 0 : (T + CS - 1) / CS;
+  const int j0 = min(T, (int)rank * chunk), j1 = bad ? 0 : min(T, j0 + chunk);
+  const int n = max(0, j1 - j0);
+  const int kvh = hq * n_kv / n_heads;
+  const int d = n_heads * dh;
+  const int* ptb = pt + (size_t)b * pt_stride;
+
+  for (int i = tid; i < EXP_LUT_N; i += NT) lut[i] = g_exp_lut.v[i];
+  for (int e = tid; e < dh; e += NT) qs[e] = bad ? 0 : q[(size_t)b * d + hq * dh + e];
+  __syncthreads();
+
+  // ---- phase 1: scores of the local keys, local max
+  int64_t mx = INT64_MIN;
+  for (int jj = warp; jj < n; jj += 2 * (NT / 32)) {
+    const int ja = j0 + jj, jb = ja + NT / 32;
+    const bool hb = jj + NT / 32 < n;
+    const int64_t* ka = Kc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * dh;
+    const int64_t* kb = hb ? Kc + (((size_t)ptb[jb / PAGE] * n_kv + kvh) * PAGE + (jb % PAGE)) * dh : ka;
+    uint64_t aa = 0, ab = 0;
+#pragma unroll 4
+    for (int e = lane; e < dh; e += 32) {
+      const uint64_t qe = (uint64_t)qs[e];
+      aa += qe * (uint64_t)__ldg(ka + e);
+      ab += qe * (uint64_t)__ldg(kb + e);
+    }
+    aa = warp_sum_u64(aa);
+    ab = warp_sum_u64(ab);
+    const int64_t sa = attn_score((int64_t)aa, attn_scale), sb = attn_score((int64_t)ab, attn_scale);
+    if (lane == 0) {
+      sc[jj] = sa;
+      if (hb) sc[jj + NT / 32] = sb;
+    }
+    mx = sa > mx ? sa : mx;
+    if (hb) mx = sb > mx ? sb : mx;
+  }
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    int64_t m = red[0];
+    for (int w = 1; w < NT / 32; ++w) m = red[w] > m ? red[w] : m;
+    xmax = m;
+  }
+  cluster_sync();
+  int64_t gmax = INT64_MIN;
+#pragma unroll
+  for (int r = 0; r < CS; ++r) {
+    const int64_t v = (int64_t)ld_cluster_u64(&xmax, r);
+    gmax = v > gmax ? v : gmax;
+  }
+
+  // ---- phase 2: exps of the local keys, local sum
+  uint64_t s = 0;
+  for (int jj = tid; jj < n; jj += NT) {
+    const int64_t e = integer_exp(wsub(sc[jj], gmax), lut);
+    sc[jj] = e;
+    s += (uint64_t)e;
+  }
+  s = warp_sum_u64(s);
+  __syncthreads();
+  if (lane == 0) red[warp] = (int64_t)s;
+  __syncthreads();
+  if (tid == 0) {
+    uint64_t t = 0;
+    for (int w = 0; w < NT / 32; ++w) t += (uint64_t)red[w];
+    xsum = t;
+  }
+  cluster_sync();
+  uint64_t gs = 0;
+#pragma unroll
+  for (int r = 0; r < CS; ++r) gs += ld_cluster_u64(&xsum, r);
+  const int64_t gsum = (int64_t)gs;
+
+  // ---- phase 3: weights, partial outputs of the local keys
+  for (int jj = tid; jj < n; jj += NT) {
+    int64_t w;
+    if (T == 1) w = ONE;
+    else if (gsum == 0) w = ONE / T;
+    else w = wmul(sc[jj], ONE) / gsum;
+    sc[jj] = w;
+  }
+  __syncthreads();
+  for (int e = tid; e < dh; e += NT) {
+    uint64_t o0 = 0, o1 = 0;
+    int jj = 0;
+    for (; jj + 1 < n; jj += 2) {
+      const int ja = j0 + jj, jb = ja + 1;
+      const int64_t va = __ldg(Vc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * dh + e);
+      const int64_t vb = __ldg(Vc + (((size_t)ptb[jb / PAGE] * n_kv + kvh) * PAGE + (jb % PAGE)) * dh + e);
+      o0 += (uint64_t)mulshr(sc[jj], va);
+      o1 += (uint64_t)mulshr(sc[jj + 1], vb);
+    }
+    if (jj < n) {
+      const int ja = j0 + jj;
+      o0 += (uint64_t)mulshr(sc[jj], __ldg(Vc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * dh + e));
+    }
+    xo[e] = o0 + o1;
+  }
+  if (tid == 0) xneed = 0;
+  cluster_sync();
+
+  // ---- cross-CTA sum of partial outputs; rank r finalises a slice of dh
+  const int per = (dh + CS - 1) / CS;
+  int need = 0;
+  for (int e = (int)rank * per + tid; e < min(dh, ((int)rank + 1) * per); e += NT) {
+    uint64_t o = 0;
+#pragma unroll
+    for (int r = 0; r < CS; ++r) o += ld_cluster_u64(&xo[e], r);
+    if (bad) continue;
+    const size_t off = (size_t)b * d + hq * dh + e;
+    if (o_out) o_out[off] = (int64_t)o;
+    if (X) {
+      int8_t dg[8];
+      const int nl = limb_split8((int64_t)o, dg);
+      need = nl > need ? nl : need;
+      const size_t ps = (size_t)B * d;
+#pragma unroll
+      for (int l = 0; l < 8; ++l) X[l * ps + off] = dg[l];
+    }
+  }
+  need = __reduce_max_sync(0xffffffffu, need);
+  if (lane == 0 && need) atomicMax(&xneed, need);
+  __syncthreads();
+  if (tid == 0 && lmax && xneed) atomicMax(lmax, xneed);
+  cluster_sync();  // no CTA may exit while a peer still reads its shared memory
+}
+
+template <int CS>
+int launch(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride, const int* pos,
+           int n_heads, int n_kv, int dh, int64_t attn_scale, int max_T, int B, int8_t* X, int* lmax,
+           int64_t* o_out, int* err, cudaStream_t st) {
+  const size_t smem = (size_t)((max_T + CS - 1) / CS + 1) * 8;
+  static size_t attr = 0;
+  if (smem > attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_attn_cluster<CS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    attr = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CS, n_heads, B);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CS;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = arcb_pdl_enabled();
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_attn_cluster<CS>, q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh,
+                                     attn_scale, max_T, B, X, lmax, o_out, err);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" int arcb_attn_cluster(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt,
+                                 int pt_stride, const int* pos, int n_heads, int n_kv, int dh, int64_t attn_scale,
+                                 int max_T, int B, int cluster, int8_t* X, int* lmax, int64_t* o_out, int* err,
+                                 void* stream) {
+  if (dh > 256) return -1;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (cluster) {
+    case 1: return launch<1>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, max_T, B, X, lmax, o_out, err, st);
+    case 2: return launch<2>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, max_T, B, X, lmax, o_out, err, st);
+    case 4: return launch<4>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, max_T, B, X, lmax, o_out, err, st);
+    case 8: return launch<8>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, max_T, B, X, lmax, o_out, err, st);
+  }
+  return -2;
+}

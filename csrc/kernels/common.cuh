@@ -24,7 +24,7 @@ enum ArcbErr : int {
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
 

@@ -182,6 +182,10 @@ struct Work {
   __device__ int mt(int it) const { return (it / nch) % Mt; }
   __device__ int kc(int it) const { return it % nch; }
   __device__ int seg_end(int it) const { return min(it1, (it / nch + 1) * nch); }
+  // Weights are stored tiled: tile (m, k) is 128 rows x 128 bytes, contiguous,
+  // at row (m * nch + k) * 128 of a [Mt * nch * 128, 128] byte matrix, so one
+  // TMA box is one contiguous 16 KB DRAM block.
+  __device__ int tile_row(int it) const { return (mt(it) * nch + kc(it)) * BM; }
 };
 
 template <int BN>
@@ -239,7 +243,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int i = 0; i < pre; ++i) {
       const int it = W.it0 + i;
       mbar_arrive_expect_tx(full(i), C::STAGE_BYTES);
-      tma_load_2d(a_base + i * C::A_BYTES, &tmA, full(i), W.kc(it) * BK, W.mt(it) * BM);
+      tma_load_2d(a_base + i * C::A_BYTES, &tmA, full(i), 0, W.tile_row(it));
     }
   }
   pdl_wait();
@@ -269,7 +273,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           break;
         }
         mbar_arrive_expect_tx(full(s), C::STAGE_BYTES);
-        tma_load_2d(a_base + s * C::A_BYTES, &tmA, full(s), kx, W.mt(it) * BM);
+        tma_load_2d(a_base + s * C::A_BYTES, &tmA, full(s), 0, W.tile_row(it));
         tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, W.nt(it) * BN);
         ++issued;
       }

@@ -85,7 +85,9 @@ def test_fused_gemm_store_and_partial(M, K, B, mag):
         planes = np.concatenate([planes, np.zeros((bn - planes.shape[0], K), np.int8)])
     dev = torch.device("cuda")
     W, X, S = (torch.from_numpy(a).to(dev) for a in (w, planes, s))
-    wm, xm = ops.TensorMap(W, 128), ops.TensorMap(X, bn)
+    Wt = ops.tile_weight(W)
+    assert torch.equal(ops.untile_weight(Wt, M, K), W)
+    wm, xm = ops.TensorMap(Wt, 128), ops.TensorMap(X, bn)
     lmax = torch.tensor([need], dtype=torch.int32, device=dev)
     P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
     tiles = torch.zeros((M + 127) // 128 + 1, dtype=torch.int32, device=dev)
