@@ -103,9 +103,52 @@ def main():
                 r = bench_fgemm(M, K, a.B, a.iters, pdl=pdl)
                 r["name"] = name
                 print(json.dumps(r), flush=True)
+    if a.only == "timeline":
+        for name, (M, K) in SHAPES_7B.items():
+            print(json.dumps(timeline_fgemm(M, K, a.B)), flush=True)
+        return
     if a.only in ("", "attn"):
         for T in (130, 386, 1024, 2048):
             print(json.dumps(bench_attn(T, B=a.B, iters=a.iters)), flush=True)
+
+
+
+def timeline_fgemm(M, K, B=1, reps=5):
+    """Per-CTA %globaltimer stamps of one fused GEMM (microseconds from the
+    earliest CTA entry): entry, after the dependency wait, first stage
+    consumed, last MMA issued, epilogue done, exit."""
+    dev = torch.device("cuda")
+    W = ops.tile_weight(torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev))
+    wm = ops.TensorMap(W, 128)
+    S = torch.randint(1, 100, (M,), dtype=torch.int64, device=dev)
+    bn = ops.fgemm_bn(B)
+    X = torch.randint(-127, 128, (max(8 * B, bn), K), dtype=torch.int8, device=dev)
+    xm = ops.TensorMap(X, bn)
+    lmax = torch.tensor([3], dtype=torch.int32, device=dev)
+    P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
+    tiles = torch.zeros(M // 128 + 2, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.zeros(B, M, dtype=torch.int64, device=dev)
+    prof = torch.zeros(ops.num_sms() * 8, dtype=torch.int64, device=dev)
+    e = ops.epi(ops.STORE, S, err, out=out, ldo=M)
+    e.prof = prof.data_ptr()
+    flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+    res = []
+    for _ in range(reps):
+        flush.zero_()
+        prof.zero_()
+        ops.fgemm(wm, xm, M, K, B, lmax, P, tiles, e, pdl=False)
+        torch.cuda.synchronize()
+        t = prof.view(-1, 8).cpu().numpy().astype("float64")
+        t0 = t[:, 0][t[:, 0] > 0].min()
+        row = {}
+        for k, name in ((0, "entry"), (1, "dep_wait"), (2, "first_stage"), (3, "last_mma"), (4, "epi_done"),
+                        (6, "exit")):
+            v = t[:, k][t[:, k] > 0] - t0
+            if len(v):
+                row[name] = [round(float(x) / 1000, 2) for x in (v.min(), float(__import__("numpy").median(v)), v.max())]
+        res.append(row)
+    return {"kernel": "fgemm_timeline", "M": M, "K": K, "B": B, "us_min_med_max": res[-1]}
 
 
 if __name__ == "__main__":

@@ -178,7 +178,9 @@ class Epi(C.Structure):
                 ("q_out", C.c_void_p), ("Kc", C.c_void_p), ("Vc", C.c_void_p), ("pt", C.c_void_p),
                 ("pt_stride", C.c_int), ("pos", C.c_void_p), ("rcos", C.c_void_p), ("rsin", C.c_void_p),
                 ("max_seq", C.c_int), ("X", C.c_void_p), ("ldx", C.c_int), ("lmax_out", C.c_void_p),
-                ("err", C.c_void_p), ("B", C.c_int)]
+                ("err", C.c_void_p), ("B", C.c_int),
+                ("rp", C.c_int), ("npeers", C.c_int), ("peer_P", C.c_void_p), ("peer_cnt", C.c_void_p),
+                ("peer_lmax", C.c_void_p), ("cnt_local", C.c_void_p), ("lmax_fin", C.c_void_p), ("prof", C.c_void_p)]
 
 
 PARTIAL, STORE, RESID, QKV, SWIGLU = 0, 1, 2, 3, 4

@@ -50,7 +50,7 @@ class Comm:
     def gather_logits(self, local: torch.Tensor, full: torch.Tensor, B: int, vocab_offset: int) -> None:
         pass
 
-    def fgemm_reduce(self, lin, xmap, B: int, lmax: torch.Tensor, bb: "StepBuffers", epi) -> None:
+    def fgemm_reduce(self, lin, xmap, B: int, lmax: torch.Tensor, bb: "StepBuffers", epi, site: int = 0) -> None:
         """Row-parallel GEMM whose epilogue sees the full (all-rank) sum; on
         one GPU that is the plain fused GEMM."""
         ops.fgemm(lin.tmap, xmap, lin.M, lin.K, B, lmax, bb.P, bb.tiles, epi)
@@ -148,7 +148,7 @@ class Engine:
             ops.attn(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo, c1,
                      self.max_pages * PAGE, bb.err)
             if reduce_in_kernel:
-                cm.fgemm_reduce(Ly.wo, bb.mXo, B, c1, bb, e["wo"])
+                cm.fgemm_reduce(Ly.wo, bb.mXo, B, c1, bb, e["wo"], site=0)
             else:
                 ops.fgemm(Ly.wo.tmap, bb.mXo, Ly.wo.M, Ly.wo.K, B, c1, bb.P, bb.tiles, e["partial"])
                 cm.reduce_partials(bb.P, 8 * B, d, c1)
@@ -156,7 +156,7 @@ class Engine:
             ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
             ops.fgemm(Ly.gu.tmap, bb.mXd, Ly.gu.M, Ly.gu.K, B, c2, bb.P, bb.tiles, e["gu"])
             if reduce_in_kernel:
-                cm.fgemm_reduce(Ly.down, bb.mXf, B, c3, bb, e["down"])
+                cm.fgemm_reduce(Ly.down, bb.mXf, B, c3, bb, e["down"], site=1)
             else:
                 ops.fgemm(Ly.down.tmap, bb.mXf, Ly.down.M, Ly.down.K, B, c3, bb.P, bb.tiles, e["partial"])
                 cm.reduce_partials(bb.P, 8 * B, d, c3)

@@ -51,7 +51,7 @@ def main():
     ap.add_argument("--model", default="llama7b")
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--gen-len", type=int, default=256)
-    ap.add_argument("--comm", default="nccl", choices=["nccl", "fused"])
+    ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -85,6 +85,12 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", torch.cuda.current_device())
 
+    t_start = time.time()
+
+    def log(msg):
+        if os.environ.get("ARCB_BENCH_LOG"):
+            print(f"[rank {rank} +{time.time() - t_start:7.1f}s] {msg}", file=sys.stderr, flush=True)
+
     def barrier():
         if world > 1:
             dist.barrier()
@@ -94,7 +100,9 @@ def main():
     max_seq = 1 + args.prompt_len + args.gen_len + 1
     max_seq = (max_seq + 15) // 16 * 16
     cfg.max_seq = max_seq
+    log("generating weights")
     model = dense.random_device(cfg, dev, seed=0, tp_rank=rank, tp_size=world)
+    log("weights ready")
     eng = Engine(model, max_seq=max_seq, comm=comm, n_pages=2 * ((max_seq + 15) // 16))
     prompt = gen.seeded_prompt(args.prompt_len, cfg.vocab, 1)
 
@@ -108,12 +116,15 @@ def main():
     with ClockSampler(local) as clk:
         while timed < K:
             rid = eng.new_request(1 + len(prompt) + G)
+            log("prefill")
             eng.prefill(rid, [1] + prompt)
+            log("prefill done")
             bb = eng.buffers(1, gen_cap=G)
             eng._reset_sampling(bb, [rid], [prompt[-1]], [len(prompt) + 1], ())
             if launches_per_step is None:
                 n0 = ops.LAUNCHES[0]
                 g = eng._graph_for(bb)
+                log("graph captured")
                 launches_per_step = (ops.LAUNCHES[0] - n0) // 2  # eager warm-up step + captured step
             else:
                 g = eng._graph_for(bb)
@@ -185,7 +196,14 @@ def main():
         }
         print(json.dumps(out))
     if world > 1:
+        # CUDA graphs holding NCCL calls must be released before the process
+        # group is destroyed, or the exit blocks.
+        import gc
+
+        g = None
         eng._graphs.clear()
+        gc.collect()
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -64,6 +64,21 @@ struct Epi {
   int* lmax_out;
   int* err;
   int B;  // slots in the step (plane stride of X = B * ldx)
+  // Tensor-parallel push mode (rp = 1): partials go to every rank's P over
+  // NVLink (peer pointers of a symmetric allocation), arrivals to every
+  // rank's per-tile counters; tile mt is finalised on each rank by its CTA
+  // mt % gridDim.x once all ranks' chunks have arrived.
+  int rp;
+  int npeers;
+  int* const* peer_P;
+  int* const* peer_cnt;
+  int* const* peer_lmax;
+  int* cnt_local;
+  int* lmax_fin;
+  // optional per-CTA %globaltimer stamps [grid][8]: 0 entry, 1 after the
+  // dependency wait, 2 first stage consumed, 3 last MMA issued, 4 epilogue
+  // done, 5 finaliser done, 6 exit
+  unsigned long long* prof;
 };
 
 template <int BN>
@@ -166,6 +181,25 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
   }
 }
 
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait for a counter written by other GPUs (and this GPU's CTAs).
+__device__ __forceinline__ bool wait_counter_geq(const int* p, int target) {
+  if (ld_acquire_sys(p) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_acquire_sys(p) >= target) return true;
+    if ((i & 63) == 63) {
+      if (globaltimer_ns() - t0 > ARCB_WAIT_NS) return false;
+      __nanosleep(64);
+    }
+  }
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -233,6 +267,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot_ptr;
+  if (E.prof && threadIdx.x == 0) E.prof[blockIdx.x * 8 + 0] = globaltimer_ns();
   pdl_launch();
 
   // Weights do not depend on the previous kernel: start streaming them.
@@ -247,10 +282,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   }
   pdl_wait();
+  if (E.prof && threadIdx.x == 0) E.prof[blockIdx.x * 8 + 1] = globaltimer_ns();
   const int L = max(1, *lmax);
   const int nrows = L * B;
   const int ntu = min(n_tiles_max, (nrows + BN - 1) / BN);
   W.range(ntu);
+  if (E.rp && warp == 2 && lane == 0) {
+    // Publish this rank's limb count before any arrival (finalisers read the
+    // max over ranks), then count the n-tiles this rank has no rows for, so
+    // every rank contributes n_tiles_max * nch arrivals per tile.
+    for (int p = 0; p < E.npeers; ++p) atomicMax_system(E.peer_lmax[p], L);
+    __threadfence_system();
+    const int virt = (n_tiles_max - ntu) * W.nch;
+    if (blockIdx.x == 0 && virt > 0)
+      for (int mt = 0; mt < W.Mt; ++mt)
+        for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + mt, virt);
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -305,6 +352,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             break;
           }
           tc_fence_after();
+          if (E.prof && i == 0) E.prof[blockIdx.x * 8 + 2] = globaltimer_ns();
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             const uint64_t ad = sw128_kmajor_desc(a_base + s * C::A_BYTES + kk * 32);
@@ -314,6 +362,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           mma_commit(empty(s));
         }
         mma_commit(seg_full(tb));
+        if (E.prof) E.prof[blockIdx.x * 8 + 3] = globaltimer_ns();
         it = se;
       }
     }
@@ -340,7 +389,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int n0 = nt * BN;
       const int n_mma = (min(BN, nrows - n0) + 15) & ~15;
       const bool whole = (W.kc(it) == 0) && (se - it == W.nch);
-      const bool direct = whole && ntu == 1 && E.mode != PARTIAL;
+      const bool direct = whole && ntu == 1 && E.mode != PARTIAL && !E.rp;
       const uint32_t taddr = tmem + (uint32_t)(tb * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
       int need = 0;
       if (direct) {
@@ -361,7 +410,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int n = n0 + c0 + j;
-              if (n < nrows && r[j] != 0) red_add_s32(P + (size_t)n * M + m, (int)r[j]);
+              if (n < nrows && r[j] != 0) {
+                if (E.rp) {
+                  for (int p = 0; p < E.npeers; ++p) red_add_s32(E.peer_P[p] + (size_t)n * M + m, (int)r[j]);
+                } else {
+                  red_add_s32(P + (size_t)n * M + m, (int)r[j]);
+                }
+              }
             }
           }
         }
@@ -369,7 +424,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(seg_free(tb));
-      if (!direct && E.mode != PARTIAL) {
+      if (E.rp) {
+        __threadfence_system();
+        epi_bar();
+        if (warp == 2 && lane == 0)
+          for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + mt, se - it);
+      } else if (!direct && E.mode != PARTIAL) {
         __threadfence();
         epi_bar();
         if (warp == 2 && lane == 0) {
@@ -401,7 +461,41 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       it = se;
     }
+    if (E.prof && warp == 2 && lane == 0) E.prof[blockIdx.x * 8 + 4] = globaltimer_ns();
+    if (E.rp && E.mode != PARTIAL) {
+      // ---- finaliser: tiles mt = blockIdx.x (mod grid) of this rank's copy
+      const int target = E.npeers * n_tiles_max * W.nch;
+      for (int mt = blockIdx.x; mt < W.Mt; mt += gridDim.x) {
+        if (warp == 2 && lane == 0) *ok_ptr = wait_counter_geq(E.cnt_local + mt, target) ? 1 : 0;
+        epi_bar();
+        const bool ok = *ok_ptr != 0;
+        epi_bar();
+        if (!ok) {
+          if (warp == 2 && lane == 0) set_error(E.err, ARCB_ERR_COMM_TIMEOUT);
+          continue;
+        }
+        __threadfence_system();
+        const int Lf = min(8, max(L, ld_acquire_sys(E.lmax_fin)));
+        const int m = mt * BM + q * 32 + lane;
+        const bool valid = m < M;
+        int need = 0;
+        for (int b = 0; b < B; ++b) {
+          uint64_t acc = 0;
+          if (valid)
+            for (int l = 0; l < Lf; ++l) {
+              int* p = P + (size_t)(l * B + b) * M + m;
+              acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
+              *p = 0;
+            }
+          apply_row(E, M, m, valid, b, acc, need);
+        }
+        epi_bar();
+        if (warp == 2 && lane == 0) E.cnt_local[mt] = 0;
+      }
+      if (E.prof && warp == 2 && lane == 0) E.prof[blockIdx.x * 8 + 5] = globaltimer_ns();
+    }
   }
+  if (E.prof && threadIdx.x == 0) E.prof[blockIdx.x * 8 + 6] = globaltimer_ns();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
