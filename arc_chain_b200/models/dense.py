@@ -43,8 +43,27 @@ class Linear:
         self.tmap = ops.TensorMap(self.w, ops.BM)
         return self
 
+    q4: Optional[torch.Tensor] = None  # packed Q4 tiles (ops.pack_q4) when quantised
+
     def row_major(self) -> torch.Tensor:
         return ops.untile_weight(self.w, self.M, self.K)
+
+    def to_q4(self, mode: str = "group") -> "Linear":
+        """Quantise to Q4 in place.  mode "group": group-32 4-bit weights
+        with 4-bit group multipliers (row scale kept); mode "values": the
+        int8 data already holds Q4 values in [-8, 7] (reference per-row Q4
+        prepared on the host), multipliers 1."""
+        w = self.row_major()
+        if mode == "group":
+            q, mult = ops.q4_group_quantize(w)
+        elif mode == "values":
+            q = w
+            mult = torch.ones(self.M, (self.K + 31) // 32, dtype=torch.uint8, device=w.device)
+        else:
+            raise ValueError(mode)
+        self.q4 = ops.pack_q4(q, mult)
+        self.w, self.tmap = None, None
+        return self
 
 
 @dataclass
@@ -139,8 +158,52 @@ def check_tp(cfg: ModelConfig, tp: int):
         raise ValueError("sharded K must stay a multiple of 16 bytes (TMA row stride)")
 
 
-def from_host(m: Int8Model, device, tp_rank: int = 0, tp_size: int = 1) -> DenseModel:
-    """Upload an Int8Model (numpy) to the device, sharded for TP."""
+def linears(model: "DenseModel"):
+    for Ly in model.layers:
+        yield from (Ly.qkv, Ly.wo, Ly.gu, Ly.down)
+    yield model.lm
+
+
+def to_q4(model: "DenseModel", mode: str = "group") -> "DenseModel":
+    """Quantise every matrix of a device model to Q4 (see Linear.to_q4)."""
+    if mode == "group" and model.tp_size > 1:
+        for k in (model.cfg.d_model, model.cfg.d_ff):
+            if (k // model.tp_size) % 32:
+                raise ValueError("group-32 Q4 with TP needs K shards that are multiples of 32")
+    for lin in linears(model):
+        lin.to_q4(mode)
+    torch.cuda.synchronize()
+    return model
+
+
+def q4_row_host(m: Int8Model) -> Int8Model:
+    """The reference's per-row Q4 applied on the host before sharding
+    (absmax over the whole row): data becomes the Q4 values, scales s * qpu."""
+    from arc_chain_b200 import spec
+    import copy
+
+    out = copy.copy(m)
+    out.out, out.out_s = spec.q4_from_i8(m.out, m.out_s)
+    out.layers = []
+    for L in m.layers:
+        L2 = dict(L)
+        for n in LAYER_MATS:
+            L2[n], L2[n + "_s"] = spec.q4_from_i8(L[n], L[n + "_s"])
+        out.layers.append(L2)
+    return out
+
+
+def from_host(m: Int8Model, device, tp_rank: int = 0, tp_size: int = 1, q4: Optional[str] = None) -> DenseModel:
+    """Upload an Int8Model (numpy) to the device, sharded for TP.
+
+    q4=None keeps INT8; "row" applies the reference's per-row Q4 (every
+    matrix including the LM head, as enable_q4 does); "group" the group-32
+    Q4 extension."""
+    if q4 == "row":
+        dm = from_host(q4_row_host(m), device, tp_rank, tp_size)
+        return to_q4(dm, "values")
+    if q4 == "group":
+        return to_q4(from_host(m, device, tp_rank, tp_size), "group")
     c = m.cfg
     check_tp(c, tp_size)
     dev = torch.device(device)

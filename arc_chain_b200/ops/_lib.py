@@ -33,6 +33,8 @@ _SIGS = {
     "arcb_fgemm_bn": (i32, [i32]),
     "arcb_fgemm": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp]),
     "arcb_fgemm_epi_size": (i32, []),
+    "arcb_fgemm_q4": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp]),
+    "arcb_verify_sample": (i32, [vp, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
     "arcb_set_pdl": (None, [i32]),
     "arcb_get_pdl": (i32, []),
 }

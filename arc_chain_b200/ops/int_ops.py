@@ -245,3 +245,83 @@ def attn(q, Kc, Vc, pt, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax, max_T, e
     check(lib().arcb_attn_cluster(_p(q), _p(Kc), _p(Vc), _p(pt), pt.shape[1], _p(pos), n_heads, n_kv, dh,
                                   int(attn_scale), max_T, B, cs, _p(X), _p(lmax), _p(o_out), _p(err), _s()),
           "attn_cluster")
+
+
+# --------------------------------------------------------------- Q4 weights
+Q4_TILE = 128 * 64 + 128 * 2
+
+
+def pack_q4(q: torch.Tensor, mult: torch.Tensor) -> torch.Tensor:
+    """Pack Q4 weights into the tiles the Q4 GEMM streams.
+
+    q: int [M, K] values in [-8, 7]; mult: int [M, ceil(K/32)] group
+    multipliers in [1, 15].  Tile (m, k) (128 rows x 128 columns) is
+    Q4_TILE contiguous bytes: 128 rows x 64 bytes of bias-8 nibbles (low
+    nibble = even column) then 128 rows x 2 bytes of multipliers (group g
+    of the chunk in bits 4g..4g+3).  Padding is q = 0, multiplier 1."""
+    M, K = q.shape
+    Mt, nch = (M + BM - 1) // BM, (K + BK - 1) // BK
+    dev = q.device
+    qp = torch.zeros(Mt * BM, nch * BK, dtype=torch.int16, device=dev)
+    qp[:M, :K] = q.to(torch.int16)
+    nib = (qp + 8).to(torch.uint8)
+    packed = nib[:, 0::2] | (nib[:, 1::2] << 4)
+    ng = (K + 31) // 32
+    mp = torch.ones(Mt * BM, nch * 4, dtype=torch.int32, device=dev)
+    mp[:M, :ng] = mult.to(torch.int32)
+    mm = mp.view(Mt * BM, nch, 4)
+    m16 = (mm[..., 0] | (mm[..., 1] << 4) | (mm[..., 2] << 8) | (mm[..., 3] << 12))
+    mb = torch.stack([(m16 & 0xFF), (m16 >> 8) & 0xFF], -1).to(torch.uint8)  # [Mt*128, nch, 2]
+    nibt = packed.view(Mt, BM, nch, 64).permute(0, 2, 1, 3).reshape(Mt * nch, BM * 64)
+    mbt = mb.view(Mt, BM, nch, 2).permute(0, 2, 1, 3).reshape(Mt * nch, BM * 2)
+    return torch.cat([nibt, mbt], 1).contiguous().view(-1)
+
+
+def q4_group_quantize(w: torch.Tensor):
+    """Group-32 Q4 of an int8 matrix (the extension format): per 32-column
+    group m = clamp(ceil(absmax / 7), 1, 15), q = clamp(trunc(w / m), -8, 7);
+    the effective int8 weight is m * q and the row scale is unchanged."""
+    M, K = w.shape
+    ng = (K + 31) // 32
+    wp = torch.zeros(M, ng * 32, dtype=torch.int32, device=w.device)
+    wp[:, :K] = w.to(torch.int32)
+    g = wp.view(M, ng, 32)
+    am = g.abs().amax(-1).clamp(min=1)
+    m = ((am + 6) // 7).clamp(1, 15)
+    q = torch.div(g, m.unsqueeze(-1), rounding_mode="trunc").clamp(-8, 7).view(M, ng * 32)[:, :K]
+    return q.to(torch.int8), m.to(torch.uint8)
+
+
+def q4_row_quantize(w: torch.Tensor, s: torch.Tensor):
+    """The reference's per-row Q4 (Q4WeightsX86::from_i8,
+    cached_integer_model.rs:670-701): qpu = max(1, ceil(absmax_row / 7)),
+    q = clamp(trunc(w / qpu), -8, 7), row scale s * qpu; group multipliers 1."""
+    am = w.to(torch.int32).abs().amax(-1).clamp(min=1)
+    qpu = ((am + 6) // 7).clamp(min=1)
+    q = torch.div(w.to(torch.int32), qpu.unsqueeze(-1), rounding_mode="trunc").clamp(-8, 7).to(torch.int8)
+    mult = torch.ones(w.shape[0], (w.shape[1] + 31) // 32, dtype=torch.uint8, device=w.device)
+    return q, mult, s * qpu.to(torch.int64)
+
+
+def fgemm_q4(packed: torch.Tensor, xmap: TensorMap, M: int, K: int, B: int, lmax, P, tile_cnt, epi: Epi,
+             pdl: bool = True) -> None:
+    """K2: the fused GEMM over Q4 tiles (dequantised to int8 in shared memory)."""
+    _count()
+    check(lib().arcb_fgemm_q4(_p(packed), xmap.addr, M, K, B, xmap.box_rows, _p(lmax), _p(P), _p(tile_cnt),
+                              C.addressof(epi), int(pdl), _s()), "fgemm_q4")
+
+
+def linear_gemm(lin, xmap: TensorMap, B: int, lmax, P, tile_cnt, epi: Epi) -> None:
+    """Dispatch a Linear (int8 tiles or Q4 tiles) to its fused GEMM."""
+    if getattr(lin, "q4", None) is not None:
+        fgemm_q4(lin.q4, xmap, lin.M, lin.K, B, lmax, P, tile_cnt, epi)
+    else:
+        fgemm(lin.tmap, xmap, lin.M, lin.K, B, lmax, P, tile_cnt, epi)
+
+
+def verify_sample(logits, V: int, lanes: int, k: int, drafts, hist, count, y) -> None:
+    """Speculative verify: penalty + argmax at each of the k+1 positions of
+    every lane, with history = confirmed tokens + the preceding drafts."""
+    _count()
+    check(lib().arcb_verify_sample(_p(logits), logits.shape[1], V, lanes, k, _p(drafts), _p(hist), _p(count),
+                                   _p(y), _s()), "verify_sample")

@@ -84,4 +84,4 @@ class FusedComm(NcclComm):
             self._epis[key] = (e, epi)  # keep the source alive: its id is the key
         else:
             e = e[0]
-        ops.fgemm(lin.tmap, xmap, lin.M, lin.K, B, lmax, s.P, bb.tiles, e)
+        ops.linear_gemm(lin, xmap, B, lmax, s.P, bb.tiles, e)

@@ -53,7 +53,7 @@ class Comm:
     def fgemm_reduce(self, lin, xmap, B: int, lmax: torch.Tensor, bb: "StepBuffers", epi, site: int = 0) -> None:
         """Row-parallel GEMM whose epilogue sees the full (all-rank) sum; on
         one GPU that is the plain fused GEMM."""
-        ops.fgemm(lin.tmap, xmap, lin.M, lin.K, B, lmax, bb.P, bb.tiles, epi)
+        ops.linear_gemm(lin, xmap, B, lmax, bb.P, bb.tiles, epi)
 
     @property
     def n_launches(self) -> int:
@@ -144,27 +144,27 @@ class Engine:
             c0, c1, c2, c3 = (bb.cnt[4 * l + i:4 * l + i + 1] for i in range(4))
             e = E[l]
             ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
-            ops.fgemm(Ly.qkv.tmap, bb.mXd, Ly.qkv.M, Ly.qkv.K, B, c0, bb.P, bb.tiles, e["qkv"])
+            ops.linear_gemm(Ly.qkv, bb.mXd, B, c0, bb.P, bb.tiles, e["qkv"])
             ops.attn(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo, c1,
                      self.max_pages * PAGE, bb.err)
             if reduce_in_kernel:
                 cm.fgemm_reduce(Ly.wo, bb.mXo, B, c1, bb, e["wo"], site=0)
             else:
-                ops.fgemm(Ly.wo.tmap, bb.mXo, Ly.wo.M, Ly.wo.K, B, c1, bb.P, bb.tiles, e["partial"])
+                ops.linear_gemm(Ly.wo, bb.mXo, B, c1, bb.P, bb.tiles, e["partial"])
                 cm.reduce_partials(bb.P, 8 * B, d, c1)
                 ops.finalize(bb.P, d, B, c1, Ly.wo.s, bb.h, d, 1, ss[2 * l + 1])
             ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
-            ops.fgemm(Ly.gu.tmap, bb.mXd, Ly.gu.M, Ly.gu.K, B, c2, bb.P, bb.tiles, e["gu"])
+            ops.linear_gemm(Ly.gu, bb.mXd, B, c2, bb.P, bb.tiles, e["gu"])
             if reduce_in_kernel:
                 cm.fgemm_reduce(Ly.down, bb.mXf, B, c3, bb, e["down"], site=1)
             else:
-                ops.fgemm(Ly.down.tmap, bb.mXf, Ly.down.M, Ly.down.K, B, c3, bb.P, bb.tiles, e["partial"])
+                ops.linear_gemm(Ly.down, bb.mXf, B, c3, bb.P, bb.tiles, e["partial"])
                 cm.reduce_partials(bb.P, 8 * B, d, c3)
                 ops.finalize(bb.P, d, B, c3, Ly.down.s, bb.h, d, 1, ss[2 * l + 2])
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
             ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
-            ops.fgemm(m.lm.tmap, bb.mXd, m.lm.M, m.lm.K, B, cf, bb.P, bb.tiles, E[-1]["lm"])
+            ops.linear_gemm(m.lm, bb.mXd, B, cf, bb.P, bb.tiles, E[-1]["lm"])
             cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset)
 
     def _epis(self, bb: StepBuffers):
@@ -215,16 +215,37 @@ class Engine:
         self.kv.reserve(rid, n_tokens)
         return rid
 
+    @staticmethod
+    def bucket(n: int) -> int:
+        """Slot-count bucket for a prefill chunk (bounded set of buffers)."""
+        b = 16
+        while b < n:
+            b *= 2
+        return b
+
+    @property
+    def scratch_rid(self) -> int:
+        """A one-page request that padding / idle slots write their KV into."""
+        if getattr(self, "_scratch", None) is None:
+            self._scratch = self.new_request(1)
+        return self._scratch
+
     def prefill(self, rid: int, tokens: Sequence[int], start_pos: int = 0, chunk: int = 1024) -> None:
-        """Write KV for `tokens` at positions start_pos.. (logits discarded)."""
-        row = torch.tensor(self.kv.table_row(rid), dtype=I32)
+        """Write KV for `tokens` at positions start_pos.. (logits discarded).
+
+        Chunks are padded to a power-of-two slot count; padding slots feed
+        token 0 at position 0 of the scratch page, which no request reads."""
+        row = self.kv.table_row(rid)
+        srow = self.kv.table_row(self.scratch_rid)
         for s in range(0, len(tokens), chunk):
-            part = list(tokens[s:s + chunk])
-            B = len(part)
+            part = [int(t) for t in tokens[s:s + chunk]]
+            n = len(part)
+            B = self.bucket(n)
             bb = self.buffers(B)
-            bb.tokens.copy_(torch.tensor(part, dtype=I32))
-            bb.pos.copy_(torch.arange(start_pos + s, start_pos + s + B, dtype=I32))
-            bb.pt.copy_(row.unsqueeze(0).expand(B, -1))
+            pad = B - n
+            bb.tokens.copy_(torch.tensor(part + [0] * pad, dtype=I32))
+            bb.pos.copy_(torch.tensor(list(range(start_pos + s, start_pos + s + n)) + [0] * pad, dtype=I32))
+            bb.pt.copy_(torch.tensor([row] * n + [srow] * pad, dtype=I32))
             self.forward(bb, B, with_logits=False)
 
     def generate(self, prompt: Sequence[int], max_tokens: int, eos: Sequence[int] = (),

@@ -1,0 +1,169 @@
+"""Continuous-batching scheduler over the paged KV cache.
+
+The reference serves one request at a time (single-stream ``generate``,
+crates/arc-inference/src/cached_integer_model.rs:1518-1557); batching is an
+extension defined so that every request's output is bit-identical to its
+own single-stream run: each token's computation reads only its own
+request's KV pages, and every reduction is an exact integer sum, so sharing
+a GEMM with other requests changes nothing.
+
+Layout: the decode step has ``max_batch`` fixed *lanes* (one CUDA graph per
+lane count).  A request holds a lane from the end of its prefill to its last
+token; idle lanes are masked (``done`` = 1) and point at a scratch page, so
+the graph never changes shape.  Waiting requests are admitted when a lane
+and enough KV pages are free; their BOS + prompt is prefilled in chunks of
+at most ``prefill_chunk`` tokens between decode steps (logits discarded, as
+in the reference), then the lane starts decoding with the last prompt token
+fed again at position n + 1.  A request finishes on an EOS id (kept in the
+output) or after ``max_tokens`` tokens; its output hash is BLAKE3 of the LE
+u32 ids, as the reference computes it.
+"""
+from __future__ import annotations
+
+import collections
+import time
+from dataclasses import dataclass, field
+from typing import Deque, Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from arc_chain_b200.runtime.engine import Engine, I32
+from arc_chain_b200.utils.hashing import blake3
+
+
+@dataclass
+class Request:
+    rid: int
+    prompt: List[int]
+    max_tokens: int
+    lane: int = -1
+    tokens: List[int] = field(default_factory=list)
+    output_hash: Optional[bytes] = None
+    t_submit: float = 0.0
+    t_first: float = 0.0
+    t_done: float = 0.0
+
+    @property
+    def done(self) -> bool:
+        return self.output_hash is not None
+
+
+class Scheduler:
+    def __init__(self, engine: Engine, max_batch: int = 32, prefill_chunk: int = 1024,
+                 eos: Sequence[int] = (), gen_cap: Optional[int] = None, use_graph: bool = True):
+        self.e = engine
+        self.max_batch = max_batch
+        self.prefill_chunk = prefill_chunk
+        self.eos = [int(x) for x in eos]
+        self.gen_cap = gen_cap or engine.max_seq
+        self.use_graph = use_graph
+        self.waiting: Deque[Request] = collections.deque()
+        self.requests: Dict[int, Request] = {}
+        self.lanes: List[Optional[Request]] = [None] * max_batch
+        self.bb = engine.buffers(max_batch, gen_cap=self.gen_cap)
+        self._scratch_rid = engine.scratch_rid  # page for idle lanes
+        self._init_lanes()
+        self.steps = 0
+        self.tokens_out = 0
+        self.metrics: List[dict] = []
+
+    # ------------------------------------------------------------ lanes
+    def _init_lanes(self):
+        bb = self.bb
+        row = torch.tensor(self.e.kv.table_row(self._scratch_rid), dtype=I32)
+        bb.pt.copy_(row.unsqueeze(0).expand(self.max_batch, -1))
+        bb.tokens.zero_()
+        bb.pos.zero_()
+        bb.hist.zero_()
+        bb.count.zero_()
+        bb.done.fill_(1)
+        bb.n_eos = len(self.eos[:8])
+        if bb.n_eos:
+            bb.eos[:bb.n_eos].copy_(torch.tensor(self.eos[:8], dtype=I32))
+
+    def _open_lane(self, lane: int, r: Request):
+        bb = self.bb
+        n = len(r.prompt)
+        bb.pt[lane].copy_(torch.tensor(self.e.kv.table_row(r.rid), dtype=I32))
+        bb.tokens[lane] = r.prompt[-1] if n else 0
+        bb.pos[lane] = n + 1
+        bb.hist[lane].zero_()
+        bb.count[lane] = 0
+        bb.done[lane] = 0
+        r.lane = lane
+        self.lanes[lane] = r
+
+    def _close_lane(self, lane: int):
+        bb = self.bb
+        bb.done[lane] = 1
+        bb.pt[lane].copy_(torch.tensor(self.e.kv.table_row(self._scratch_rid), dtype=I32))
+        bb.pos[lane] = 0
+        bb.tokens[lane] = 0
+        self.lanes[lane] = None
+
+    # ------------------------------------------------------------ API
+    def submit(self, prompt: Sequence[int], max_tokens: int) -> int:
+        rid = self.e._rid
+        self.e._rid += 1
+        r = Request(rid, [int(t) for t in prompt], int(max_tokens), t_submit=time.perf_counter())
+        if max_tokens > self.gen_cap:
+            raise ValueError(f"max_tokens {max_tokens} > gen_cap {self.gen_cap}")
+        self.requests[rid] = r
+        self.waiting.append(r)
+        return rid
+
+    def _admit(self) -> int:
+        admitted = 0
+        for lane in range(self.max_batch):
+            if self.lanes[lane] is not None or not self.waiting:
+                continue
+            r = self.waiting[0]
+            need = 1 + len(r.prompt) + r.max_tokens
+            if (need + 15) // 16 > len(self.e.kv.pool.free):
+                break
+            self.waiting.popleft()
+            self.e.kv.reserve(r.rid, need)
+            self.e.prefill(r.rid, [1] + r.prompt, chunk=self.prefill_chunk)
+            self._open_lane(lane, r)
+            admitted += 1
+        return admitted
+
+    def step(self) -> int:
+        """Admit, then one decode step over all lanes; returns active lanes."""
+        self._admit()
+        active = sum(1 for x in self.lanes if x is not None)
+        if active == 0:
+            return 0
+        if self.use_graph:
+            self.e._graph_for(self.bb).replay()
+        else:
+            self.e.decode_step(self.bb)
+        self.steps += 1
+        cnt = self.bb.count.cpu().numpy()
+        done = self.bb.done.cpu().numpy()
+        for lane, r in enumerate(self.lanes):
+            if r is None:
+                continue
+            if r.t_first == 0.0 and cnt[lane] > 0:
+                r.t_first = time.perf_counter()
+            if done[lane] or cnt[lane] >= r.max_tokens:
+                self._finish(lane, r, int(min(cnt[lane], r.max_tokens)))
+        self.tokens_out += active
+        return active
+
+    def _finish(self, lane: int, r: Request, n: int):
+        r.tokens = [int(t) for t in self.bb.gen[lane, :n].tolist()]
+        r.output_hash = blake3(np.asarray(r.tokens, dtype="<u4").tobytes())
+        r.t_done = time.perf_counter()
+        self.e.kv.release(r.rid)
+        self._close_lane(lane)
+
+    def run(self, max_steps: Optional[int] = None) -> Dict[int, Request]:
+        s = 0
+        while self.waiting or any(x is not None for x in self.lanes):
+            self.step()
+            s += 1
+            if max_steps is not None and s >= max_steps:
+                break
+        return self.requests

@@ -225,9 +225,11 @@ def q4g_effective(q: np.ndarray, m: np.ndarray) -> np.ndarray:
 
 
 def q4g_from_i8(w: np.ndarray, s: np.ndarray):
-    """Quantise an i8 matrix to group-32 Q4 (used to derive Q4 models from
-    INT8 ones).  Per group: m_g = clamp(ceil(absmax_g / 7), 1, 15)... the
-    product m_g * q approximates the i8 value; the row scale is kept."""
+    """Group-32 Q4 of an int8 matrix: per 32-column group
+    m_g = clamp(ceil(absmax_g / 7), 1, 15) and q = clamp(trunc(w / m_g), -8, 7)
+    (the reference's per-row rule, cached_integer_model.rs:682-690, applied per
+    group with a 4-bit multiplier); the row scale s is kept.  Returns
+    (q int8 [rows, cols], m uint8 [rows, groups], s)."""
     rows, cols = w.shape
     ng = (cols + Q4G - 1) // Q4G
     pad = ng * Q4G - cols
@@ -237,6 +239,27 @@ def q4g_from_i8(w: np.ndarray, s: np.ndarray):
     m = np.clip((am + 6) // 7, 1, 15)
     q = np.clip(tdiv_np(g, m[:, :, None]), -8, 7).reshape(rows, ng * Q4G)[:, :cols]
     return q.astype(np.int8), m.astype(np.uint8), s.copy()
+
+
+def q4g_effective_model(model):
+    """The INT8 model whose weights are the effective group-Q4 values m_g * q
+    (the oracle for group-32 Q4 runs this model)."""
+    import copy
+
+    out = copy.copy(model)
+
+    def eff(w, s):
+        q, m, s2 = q4g_from_i8(w, s)
+        return q4g_effective(q, m), s2
+
+    out.out, out.out_s = eff(model.out, model.out_s)
+    out.layers = []
+    for L in model.layers:
+        L2 = dict(L)
+        for n in ("wq", "wk", "wv", "wo", "gate", "up", "down"):
+            L2[n], L2[n + "_s"] = eff(L[n], L[n + "_s"])
+        out.layers.append(L2)
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -37,6 +37,10 @@ namespace fg {
 constexpr int BM = 128;
 constexpr int BK = 128;
 constexpr int NTHREADS = 192;
+// Q4 tiles (group-32 4-bit weights): 128 rows x 64 bytes of nibbles (low
+// nibble = even column, value = nibble - 8) then 128 rows x 2 bytes of 4-bit
+// group multipliers (group g of the 128-column chunk in bits 4g..4g+3).
+constexpr int Q4_TILE = 128 * 64 + 128 * 2;
 constexpr int PAGE = 16;
 
 enum Mode : int { PARTIAL = 0, STORE = 1, RESID = 2, QKV = 3, SWIGLU = 4 };
@@ -81,15 +85,18 @@ struct Epi {
   unsigned long long* prof;
 };
 
-template <int BN>
+template <int BN, bool Q4 = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN <= 16 ? 11 : (BN <= 32 ? 10 : (BN <= 64 ? 8 : (BN <= 128 ? 6 : 4)));
+  static constexpr int Q_BYTES = Q4 ? Q4_TILE : 0;        // staging of the packed Q4 tile
+  static constexpr int STAGE_BYTES = (Q4 ? Q4_TILE : A_BYTES) + B_BYTES;  // bytes TMA brings per stage
+  static constexpr int STAGES = Q4 ? (BN <= 32 ? 7 : (BN <= 64 ? 6 : (BN <= 128 ? 5 : 3)))
+                                   : (BN <= 16 ? 11 : (BN <= 32 ? 10 : (BN <= 64 ? 8 : (BN <= 128 ? 6 : 4))));
   static constexpr int ACC_COLS = BN < 32 ? 32 : BN;       // one TMEM accumulator
   static constexpr int TMEM_COLS = 2 * ACC_COLS;          // double buffered
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+  static constexpr int THREADS = Q4 ? 320 : NTHREADS;     // + 4 converter warps for Q4
+  static constexpr int SMEM = 1024 + STAGES * (A_BYTES + B_BYTES + Q_BYTES) + 512;
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -222,23 +229,25 @@ struct Work {
   __device__ int tile_row(int it) const { return (mt(it) * nch + kc(it)) * BM; }
 };
 
-template <int BN>
-__global__ void __launch_bounds__(NTHREADS, 1)
+template <int BN, bool Q4>
+__global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
     k_gemm_fused(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
                  int B, int n_tiles_max, int prefetch_ok, const int* __restrict__ lmax, int* __restrict__ P,
-                 int* __restrict__ tile_cnt, const __grid_constant__ Epi E) {
-  using C = Cfg<BN>;
+                 int* __restrict__ tile_cnt, const __grid_constant__ Epi E, const uint8_t* __restrict__ q4w) {
+  using C = Cfg<BN, Q4>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t a_base = base;
   const uint32_t b_base = base + C::STAGES * C::A_BYTES;
-  const uint32_t bar = b_base + C::STAGES * C::B_BYTES;
+  const uint32_t q_base = b_base + C::STAGES * C::B_BYTES;  // Q4 staging (Q_BYTES per stage)
+  const uint32_t bar = q_base + C::STAGES * C::Q_BYTES;
   auto full = [&](int s) { return bar + 8u * s; };
   auto empty = [&](int s) { return bar + 8u * (C::STAGES + s); };
   auto seg_full = [&](int t) { return bar + 8u * (2 * C::STAGES + t); };
   auto seg_free = [&](int t) { return bar + 8u * (2 * C::STAGES + 2 + t); };
-  const uint32_t tslot = bar + 8u * (2 * C::STAGES + 4);
+  auto conv = [&](int s) { return bar + 8u * (2 * C::STAGES + 4 + s); };  // Q4: A tile converted
+  const uint32_t tslot = bar + 8u * (3 * C::STAGES + 4);
   volatile uint32_t* tslot_ptr = (volatile uint32_t*)(smem_raw + (tslot - raw));
   volatile int* flag_ptr = (volatile int*)(smem_raw + (tslot + 8 - raw));
   volatile int* ok_ptr = (volatile int*)(smem_raw + (tslot + 12 - raw));
@@ -255,6 +264,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(seg_full(t), 1);
       mbar_init(seg_free(t), 4);
     }
+    if (Q4)
+      for (int s = 0; s < C::STAGES; ++s) mbar_init(conv(s), 4);
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -270,6 +281,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (E.prof && threadIdx.x == 0) E.prof[blockIdx.x * 8 + 0] = globaltimer_ns();
   pdl_launch();
 
+  // Weight tile of work item `it` into stage s: an int8 tile by TMA, or the
+  // packed Q4 tile by a bulk copy into the staging area (converted below).
+  auto load_a = [&](int s, int it) {
+    if constexpr (Q4) {
+      const uint8_t* src = q4w + (size_t)(W.mt(it) * W.nch + W.kc(it)) * Q4_TILE;
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              q_base + s * C::Q_BYTES),
+          "l"(src), "r"(Q4_TILE), "r"(full(s))
+          : "memory");
+    } else {
+      tma_load_2d(a_base + s * C::A_BYTES, &tmA, full(s), 0, W.tile_row(it));
+    }
+  };
   // Weights do not depend on the previous kernel: start streaming them.
   int pre = 0;
   if (warp == 0 && lane == 0 && prefetch_ok) {
@@ -278,7 +303,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int i = 0; i < pre; ++i) {
       const int it = W.it0 + i;
       mbar_arrive_expect_tx(full(i), C::STAGE_BYTES);
-      tma_load_2d(a_base + i * C::A_BYTES, &tmA, full(i), 0, W.tile_row(it));
+      load_a(i, it);
     }
   }
   pdl_wait();
@@ -320,7 +345,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           break;
         }
         mbar_arrive_expect_tx(full(s), C::STAGE_BYTES);
-        tma_load_2d(a_base + s * C::A_BYTES, &tmA, full(s), 0, W.tile_row(it));
+        load_a(s, it);
         tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, W.nt(it) * BN);
         ++issued;
       }
@@ -346,7 +371,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t dst = tmem + (uint32_t)(tb * C::ACC_COLS);
         for (int j = it; j < se; ++j, ++i) {
           const int s = i % C::STAGES;
-          if (!mbar_wait(full(s), (uint32_t)(i / C::STAGES) & 1u)) {
+          if (!mbar_wait(Q4 ? conv(s) : full(s), (uint32_t)(i / C::STAGES) & 1u)) {
             set_error(E.err, ARCB_ERR_TIMEOUT_FULL);
             ok = false;
             break;
@@ -365,6 +390,45 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (E.prof) E.prof[blockIdx.x * 8 + 3] = globaltimer_ns();
         it = se;
       }
+    }
+  } else if (Q4 && warp >= 6) {
+    // ---------------- Q4 converter warps 6..9: packed tile -> swizzled int8 A
+    const int r = threadIdx.x - 192;  // tile row
+    const int n = W.it1 - W.it0;
+    for (int i = 0; i < n; ++i) {
+      const int s = i % C::STAGES;
+      if (!mbar_wait(full(s), (uint32_t)(i / C::STAGES) & 1u)) {
+        set_error(E.err, ARCB_ERR_TIMEOUT_FULL);
+        break;
+      }
+      const uint8_t* st = smem_raw + (q_base + s * C::Q_BYTES - raw);
+      const uint4* nib = (const uint4*)(st + r * 64);
+      const uint32_t mul = *(const uint16_t*)(st + 128 * 64 + r * 2);
+      uint8_t* arow = smem_raw + (a_base + s * C::A_BYTES - raw) + r * 128;
+#pragma unroll
+      for (int c2 = 0; c2 < 4; ++c2) {  // 16 nibble bytes = 32 columns = one group
+        const uint4 v = nib[c2];
+        const int m = (int)((mul >> (4 * c2)) & 0xF);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // two 16-column output granules
+          uint32_t o[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t word = w4[h * 2 + (k >> 1)];
+            const uint32_t b0 = (word >> (16 * (k & 1))) & 0xFF, b1 = (word >> (16 * (k & 1) + 8)) & 0xFF;
+            const int v0 = ((int)(b0 & 15) - 8) * m, v1 = ((int)(b0 >> 4) - 8) * m;
+            const int v2 = ((int)(b1 & 15) - 8) * m, v3 = ((int)(b1 >> 4) - 8) * m;
+            o[k] = (uint32_t)(v0 & 0xFF) | ((uint32_t)(v1 & 0xFF) << 8) | ((uint32_t)(v2 & 0xFF) << 16) |
+                   ((uint32_t)(v3 & 0xFF) << 24);
+          }
+          const int g16 = c2 * 2 + h;  // 16-byte granule index in the 128-byte row
+          *(uint4*)(arow + ((g16 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(conv(s));
     }
   } else {
     // ---------------- epilogue warps 2..5
@@ -515,20 +579,20 @@ static int num_sms() {
   return n;
 }
 
-template <int BN>
+template <int BN, bool Q4>
 int launch(const CUtensorMap* a, const CUtensorMap* b, int M, int K, int B, const int* lmax, int* P, int* cnt,
-           const Epi& E, cudaStream_t st, int pdl) {
-  using C = Cfg<BN>;
+           const Epi& E, cudaStream_t st, int pdl, const uint8_t* q4w) {
+  using C = Cfg<BN, Q4>;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_fused<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_fused<BN, Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return (int)e;
     attr = true;
   }
   const int n_tiles_max = (8 * B + BN - 1) / BN;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms());
-  cfg.blockDim = dim3(NTHREADS);
+  cfg.blockDim = dim3(C::THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
@@ -536,8 +600,8 @@ int launch(const CUtensorMap* a, const CUtensorMap* b, int M, int K, int B, cons
   at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_fused<BN>, *a, *b, M, K, B, n_tiles_max,
-                                     (int)(n_tiles_max == 1), lmax, P, cnt, E);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_fused<BN, Q4>, *a, *b, M, K, B, n_tiles_max,
+                                     (int)(n_tiles_max == 1), lmax, P, cnt, E, q4w);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
@@ -568,15 +632,37 @@ int arcb_fgemm(const void* tmA, const void* tmB, int M, int K, int B, int bn, co
   E.B = B;
   cudaStream_t st = (cudaStream_t)stream;
   switch (bn) {
-    case 16: return fg::launch<16>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
-    case 32: return fg::launch<32>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
-    case 64: return fg::launch<64>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
-    case 128: return fg::launch<128>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
-    case 256: return fg::launch<256>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl);
+    case 16: return fg::launch<16, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
+    case 32: return fg::launch<32, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
+    case 64: return fg::launch<64, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
+    case 128: return fg::launch<128, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
+    case 256: return fg::launch<256, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
   }
   return -3;
 }
 
 int arcb_fgemm_epi_size(void) { return (int)sizeof(fg::Epi); }
+
+// K2: same GEMM with Q4 group-32 weights, dequantised to int8 in shared
+// memory (value = (nibble - 8) * group multiplier, exact); `q4w` holds the
+// tiles produced by arc_chain_b200.ops.int_ops.pack_q4 (Q4_TILE bytes each,
+// tile (m, k) at index m * nch + k).
+int arcb_fgemm_q4(const uint8_t* q4w, const void* tmB, int M, int K, int B, int bn, const int* lmax, int* P,
+                  int* tile_cnt, const void* epi, int pdl, void* stream) {
+  const CUtensorMap* b = (const CUtensorMap*)tmB;
+  fg::Epi E = *(const fg::Epi*)epi;
+  E.B = B;
+  pdl = pdl && arcb_pdl_enabled();
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((uintptr_t)q4w & 15) return -4;
+  switch (bn) {
+    case 16: return fg::launch<16, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
+    case 32: return fg::launch<32, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
+    case 64: return fg::launch<64, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
+    case 128: return fg::launch<128, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
+    case 256: return fg::launch<256, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
+  }
+  return -3;
+}
 
 }  // extern "C"

@@ -186,3 +186,108 @@ def test_device_random_init_matches_host():
         for n in ("qkv", "wo", "gu", "down"):
             assert torch.equal(getattr(a, n).w, getattr(b, n).w)
             assert torch.equal(getattr(a, n).s, getattr(b, n).s)
+
+
+def test_continuous_batching_matches_single_stream():
+    """Requests of different prompt/output lengths share decode steps; each
+    output equals the oracle's single-stream generate."""
+    from arc_chain_b200.runtime.scheduler import Scheduler
+
+    host, eng = _engine_for("micro_gqa")
+    om = arcref.Model(host)
+    sch = Scheduler(eng, max_batch=4, prefill_chunk=16, gen_cap=40)
+    specs = [(gen.seeded_prompt(5 + 7 * i, host.cfg.vocab, 10 + i), 8 + 5 * i) for i in range(7)]
+    rids = [sch.submit(p, n) for p, n in specs]
+    sch.run()
+    for rid, (p, n) in zip(rids, specs):
+        ref, rh = om.generate(p, n)
+        r = sch.requests[rid]
+        assert r.tokens == ref, rid
+        assert r.output_hash == rh
+    assert eng.check_errors() == 0
+
+
+@pytest.mark.parametrize("M,K,B", [(128, 128, 1), (1000, 688, 3), (4096, 4096, 1), (640, 1024, 40)])
+def test_q4_gemm_exact(M, K, B):
+    """K2: Q4 group-32 tiles dequantised in shared memory == int8 GEMM of
+    the effective weights m_g * q."""
+    ops = _ops()
+    rng = np.random.default_rng(M + K + 11 * B)
+    q = rng.integers(-8, 8, size=(M, K)).astype(np.int8)
+    m = rng.integers(1, 16, size=(M, (K + 31) // 32)).astype(np.uint8)
+    s = rng.integers(1, 5000, size=M).astype(np.int64)
+    x = rng.integers(-(1 << 30), 1 << 30, size=(B, K), dtype=np.int64)
+    weff = spec.q4g_effective(q, m)
+    planes, need = _limbs(x, B, K)
+    bn = ops.fgemm_bn(B)
+    if planes.shape[0] < bn:
+        planes = np.concatenate([planes, np.zeros((bn - planes.shape[0], K), np.int8)])
+    dev = torch.device("cuda")
+    packed = ops.pack_q4(torch.from_numpy(q).to(dev), torch.from_numpy(m).to(dev))
+    X, S = torch.from_numpy(planes).to(dev), torch.from_numpy(s).to(dev)
+    xm = ops.TensorMap(X, bn)
+    lmax = torch.tensor([need], dtype=torch.int32, device=dev)
+    P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
+    tiles = torch.zeros((M + 127) // 128 + 1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.zeros(B, M, dtype=torch.int64, device=dev)
+    ops.fgemm_q4(packed, xm, M, K, B, lmax, P, tiles, ops.epi(ops.STORE, S, err, out=out, ldo=M))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = np.stack([arcref.matmul_i8(weff, s, x[b]) for b in range(B)])
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+def test_q4_reference_row_mode_matches_oracle_enable_q4():
+    """The reference's per-row Q4 (enable_q4) end to end."""
+    from arc_chain_b200.models import dense
+    from arc_chain_b200.runtime.engine import Engine
+
+    cfg = preset("micro_gqa")
+    host = gen.random_model(cfg, 2)
+    eng = Engine(dense.from_host(host, "cuda", q4="row"))
+    om = arcref.Model(host)
+    om.enable_q4()
+    prompt = gen.seeded_prompt(16, cfg.vocab, 4)
+    ref, rh = om.generate(prompt, 20)
+    got, gh = eng.generate(prompt, 20)
+    assert got == ref and gh == rh
+
+
+def test_q4_group_mode_matches_oracle():
+    from arc_chain_b200.models import dense
+    from arc_chain_b200.runtime.engine import Engine
+
+    cfg = preset("micro_gqa")
+    host = gen.random_model(cfg, 3)
+    eng = Engine(dense.from_host(host, "cuda", q4="group"))
+    om = arcref.Model(spec.q4g_effective_model(host))
+    prompt = gen.seeded_prompt(16, cfg.vocab, 5)
+    ref, rh = om.generate(prompt, 20)
+    got, gh = eng.generate(prompt, 20)
+    assert got == ref and gh == rh
+
+
+@pytest.mark.parametrize("same_draft", [True, False])
+def test_speculative_decoding_equals_plain_greedy(same_draft):
+    """Accepted output == non-speculative target decoding, whether every draft
+    token is accepted (draft == target) or almost none (unrelated draft)."""
+    from arc_chain_b200.models import dense
+    from arc_chain_b200.runtime.engine import Engine
+    from arc_chain_b200.runtime.spec_decode import SpecDecoder
+
+    cfg = preset("micro_gqa")
+    host = gen.random_model(cfg, 0)
+    target = Engine(dense.from_host(host, "cuda"))
+    dhost = host if same_draft else gen.random_model(cfg, 9)
+    draft = Engine(dense.from_host(dhost, "cuda"))
+    sd = SpecDecoder(target, draft, k=4, lanes=2, gen_cap=64)
+    prompts = [gen.seeded_prompt(12, cfg.vocab, 21), gen.seeded_prompt(19, cfg.vocab, 22)]
+    out = sd.generate(prompts, 30)
+    om = arcref.Model(host)
+    for p, (toks, h) in zip(prompts, out):
+        ref, rh = om.generate(p, 30)
+        assert toks == ref and h == rh
+    if same_draft:
+        assert sd.acceptance == 1.0
+    assert target.check_errors() == 0 and draft.check_errors() == 0
