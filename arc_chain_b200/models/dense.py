@@ -288,3 +288,29 @@ def random_device(cfg: ModelConfig, device, seed: int = 0, tp_rank: int = 0, tp_
     torch.cuda.synchronize(dev)
     return DenseModel(cfg, cfg.resolved_attn_scale(), emb, emb_s, lm, fnorm, torch.from_numpy(rc).to(dev),
                       torch.from_numpy(rs).to(dev), layers, tp_rank, tp_size, lo)
+
+
+def weight_hash_seeded(cfg: ModelConfig, seed: int, device) -> bytes:
+    """The reference weight hash (BLAKE3 over each matrix's i8 bytes then its
+    LE i64 row scales: embedding, output, then per layer wq wk wv wo gate up
+    down; cached_integer_model.rs:1598-1617) of the seeded random model,
+    regenerating each matrix row-major on the device and hashing it there."""
+    from arc_chain_b200.utils.hashing import DeviceBlake3
+
+    dev = torch.device(device)
+    h = DeviceBlake3(dev)
+    d, dkv, dff, V = cfg.d_model, cfg.d_kv, cfg.d_ff, cfg.vocab
+
+    def mat(tid, rows, cols, base=None):
+        w = torch.empty(rows * cols, dtype=torch.int8, device=dev)
+        ops.rng_i8(seed, tid << 2, w)
+        s = gen.row_scales(seed, (tid << 2) | 1, rows, gen.scale_base(cols) if base is None else base)
+        h.update(w, torch.from_numpy(s.astype("<i8")).to(dev))
+
+    mat(0, V, d, gen.EMB_SCALE_BASE)
+    mat(1, V, d)
+    shapes = ((d, d), (dkv, d), (dkv, d), (d, d), (dff, d), (dff, d), (d, dff))
+    for l in range(cfg.n_layers):
+        for j, (r, c) in enumerate(shapes):
+            mat(gen.layer_tensor_id(l, j), r, c)
+    return h.digest()

@@ -35,6 +35,8 @@ _SIGS = {
     "arcb_fgemm_epi_size": (i32, []),
     "arcb_fgemm_q4": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp]),
     "arcb_verify_sample": (i32, [vp, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
+    "arcb_blake3_chunk_cvs": (i32, [vp, vp, i32, i64, i64, vp, vp]),
+    "arcb_blake3_parents": (i32, [vp, i64, vp, vp]),
     "arcb_set_pdl": (None, [i32]),
     "arcb_get_pdl": (i32, []),
 }

@@ -57,6 +57,7 @@ def lib():
                 "arcref_blake3_update": (None, [vp, vp, C.c_size_t]),
                 "arcref_blake3_push_chunk_cv": (None, [vp, vp, u64]),
                 "arcref_blake3_finalize": (None, [vp, vp]),
+                "arcref_blake3_push_subtree_cv": (None, [vp, vp, C.c_int, u64]),
                 "arcref_blake3_free": (None, [vp]),
                 "arcref_rng_fill_i8": (None, [u64, u64, vp, i64]),
                 "arcref_rng_u64": (None, [u64, u64, vp, i64]),

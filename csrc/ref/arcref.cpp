@@ -658,3 +658,7 @@ int arcref_num_threads(void) { return pool().size(); }
 void arcref_set_threads(int n) { pool().resize(n); }
 
 }  // extern "C"
+
+extern "C" void arcref_blake3_push_subtree_cv(void* h, const uint32_t* cv8, int level, uint64_t total_chunks) {
+  ((arcb3::Hasher*)h)->push_subtree_cv(cv8, level, total_chunks);
+}

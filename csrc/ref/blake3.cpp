@@ -84,6 +84,19 @@ void Hasher::push_chunk_cv(const uint32_t cv_in[8], uint64_t total_chunks) {
   memcpy(stack[stack_len++], c, 32);
 }
 
+void Hasher::push_subtree_cv(const uint32_t cv_in[8], int level, uint64_t total_chunks) {
+  uint32_t c[8];
+  memcpy(c, cv_in, 32);
+  uint64_t t = total_chunks >> level;
+  while ((t & 1) == 0) {
+    --stack_len;
+    parent_cv(key, stack[stack_len], c, 0, c);
+    t >>= 1;
+  }
+  memcpy(stack[stack_len++], c, 32);
+  chunk_counter = total_chunks;
+}
+
 void Hasher::update(const void* data, size_t len) {
   const uint8_t* p = (const uint8_t*)data;
   while (len > 0) {

@@ -36,6 +36,9 @@ struct Hasher {
   // Merge a finished chunk's chaining value whose chunk index is
   // `total_chunks - 1`; exposed so a device-side chunk hasher can feed it.
   void push_chunk_cv(const uint32_t cv_in[8], uint64_t total_chunks);
+  // Merge the CV of a complete aligned subtree of 2^level chunks that ends
+  // at chunk count `total_chunks` (a multiple of 2^level).
+  void push_subtree_cv(const uint32_t cv_in[8], int level, uint64_t total_chunks);
 };
 
 void hash(const void* data, size_t len, uint8_t out[32]);
