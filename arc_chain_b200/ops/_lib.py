@@ -37,6 +37,11 @@ _SIGS = {
     "arcb_verify_sample": (i32, [vp, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
     "arcb_blake3_chunk_cvs": (i32, [vp, vp, i32, i64, i64, vp, vp]),
     "arcb_blake3_parents": (i32, [vp, i64, vp, vp]),
+    "arcb_mla_kv": (i32, [vp, i32, i32, vp, i32, vp, vp, i32, vp, vp, vp, i32, i32, vp, vp]),
+    "arcb_mla_q": (i32, [vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, i32, i32, vp, vp]),
+    "arcb_mla_out": (i32, [vp, i32, i32, i32, vp, vp, i32, vp, vp, vp, vp]),
+    "arcb_attn_mla": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, i64, i32, i32, i32, vp, vp, vp]),
+    "arcb_moe_route": (i32, [vp, i32, i32, i32, i32, i32, vp, vp]),
     "arcb_set_pdl": (None, [i32]),
     "arcb_get_pdl": (i32, []),
 }

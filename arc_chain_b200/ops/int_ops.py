@@ -180,10 +180,11 @@ class Epi(C.Structure):
                 ("max_seq", C.c_int), ("X", C.c_void_p), ("ldx", C.c_int), ("lmax_out", C.c_void_p),
                 ("err", C.c_void_p), ("B", C.c_int),
                 ("rp", C.c_int), ("npeers", C.c_int), ("peer_P", C.c_void_p), ("peer_cnt", C.c_void_p),
-                ("peer_lmax", C.c_void_p), ("cnt_local", C.c_void_p), ("lmax_fin", C.c_void_p), ("prof", C.c_void_p)]
+                ("peer_lmax", C.c_void_p), ("cnt_local", C.c_void_p), ("lmax_fin", C.c_void_p), ("prof", C.c_void_p),
+                ("grp_rows", C.c_int), ("grp_koff", C.c_int), ("route", C.c_void_p), ("route_ld", C.c_int)]
 
 
-PARTIAL, STORE, RESID, QKV, SWIGLU = 0, 1, 2, 3, 4
+PARTIAL, STORE, RESID, QKV, SWIGLU, MOE_COMBINE = 0, 1, 2, 3, 4, 5
 
 
 def fgemm_bn(B: int) -> int:
@@ -325,3 +326,33 @@ def verify_sample(logits, V: int, lanes: int, k: int, drafts, hist, count, y) ->
     _count()
     check(lib().arcb_verify_sample(_p(logits), logits.shape[1], V, lanes, k, _p(drafts), _p(hist), _p(count),
                                    _p(y), _s()), "verify_sample")
+
+
+# --------------------------------------------------------------- MLA / MoE
+def mla_kv(kva, r, dr, gamma, cache, pt, pos, rcos, rsin, max_seq, B, err):
+    _count()
+    check(lib().arcb_mla_kv(_p(kva), r, dr, _p(gamma), gamma.numel(), _p(cache), _p(pt), pt.shape[1], _p(pos),
+                            _p(rcos), _p(rsin), max_seq, B, _p(err), _s()), "mla_kv")
+
+
+def mla_q(q, H, dn, dr, r, Wuk, suk, pos, rcos, rsin, max_seq, B, Q):
+    _count()
+    check(lib().arcb_mla_q(_p(q), H, dn, dr, r, _p(Wuk), _p(suk), _p(pos), _p(rcos), _p(rsin), max_seq, B, _p(Q),
+                           _s()), "mla_q")
+
+
+def mla_out(oc, H, r, dv, Wuv, suv, B, X, lmax, o_out=None):
+    _count()
+    check(lib().arcb_mla_out(_p(oc), H, r, dv, _p(Wuv), _p(suv), B, _p(X), _p(lmax), _p(o_out), _s()), "mla_out")
+
+
+def attn_mla(Q, cache, pt, pos, H, dk, dv, attn_scale, max_T, B, oc, err, cluster=None):
+    _count()
+    cs = cluster or attn_cluster_size(B, H)
+    check(lib().arcb_attn_mla(_p(Q), _p(cache), _p(pt), pt.shape[1], _p(pos), H, dk, dv, int(attn_scale), max_T, B,
+                              cs, _p(oc), _p(err), _s()), "attn_mla")
+
+
+def moe_route(logits, E, S, top_k, B, route):
+    _count()
+    check(lib().arcb_moe_route(_p(logits), logits.shape[1], E, S, top_k, B, _p(route), _s()), "moe_route")

@@ -35,11 +35,14 @@ class PagePool:
 
 
 class PagedKV:
-    def __init__(self, n_layers: int, n_pages: int, n_kv: int, d_head: int, device, max_pages_per_seq: int):
+    def __init__(self, n_layers: int, n_pages: int, n_kv: int, d_head: int, device, max_pages_per_seq: int,
+                 with_v: bool = True):
         self.n_layers, self.n_pages, self.n_kv, self.d_head = n_layers, n_pages, n_kv, d_head
         self.max_pages_per_seq = max_pages_per_seq
         self.K = [torch.zeros(n_pages, n_kv, PAGE, d_head, dtype=torch.int64, device=device) for _ in range(n_layers)]
-        self.V = [torch.zeros(n_pages, n_kv, PAGE, d_head, dtype=torch.int64, device=device) for _ in range(n_layers)]
+        # MLA keeps one latent row per token (values alias it): no V planes
+        self.V = [torch.zeros(n_pages, n_kv, PAGE, d_head, dtype=torch.int64, device=device)
+                  for _ in range(n_layers)] if with_v else self.K
         self.pool = PagePool(n_pages)
         self.tables: Dict[int, List[int]] = {}
 

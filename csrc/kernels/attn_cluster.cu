@@ -52,15 +52,16 @@ template <int CS>
 __global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
                                                      const int64_t* __restrict__ Vc, const int* __restrict__ pt,
                                                      int pt_stride, const int* __restrict__ pos, int n_heads,
-                                                     int n_kv, int dh, int64_t attn_scale, int max_T, int B,
+                                                     int n_kv, int dk, int dv, int kst, int vst,
+                                                     int64_t attn_scale, int max_T, int B,
                                                      int8_t* __restrict__ X, int* __restrict__ lmax,
                                                      int64_t* __restrict__ o_out, int* __restrict__ err) {
   pdl_wait_dep();
   pdl_allow_next();
   extern __shared__ int64_t dyn[];
   __shared__ int64_t lut[EXP_LUT_N];
-  __shared__ int64_t qs[256];
-  __shared__ unsigned long long xo[256];
+  __shared__ int64_t qs[640];
+  __shared__ unsigned long long xo[512];
   __shared__ int64_t red[NT / 32];
   __shared__ long long xmax;
   __shared__ unsigned long long xsum;
@@ -77,11 +78,11 @@ __global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__
   const int j0 = min(T, (int)rank * chunk), j1 = bad ? 0 : min(T, j0 + chunk);
   const int n = max(0, j1 - j0);
   const int kvh = hq * n_kv / n_heads;
-  const int d = n_heads * dh;
+  const int dq = n_heads * dk, d = n_heads * dv;
   const int* ptb = pt + (size_t)b * pt_stride;
 
   for (int i = tid; i < EXP_LUT_N; i += NT) lut[i] = g_exp_lut.v[i];
-  for (int e = tid; e < dh; e += NT) qs[e] = bad ? 0 : q[(size_t)b * d + hq * dh + e];
+  for (int e = tid; e < dk; e += NT) qs[e] = bad ? 0 : q[(size_t)b * dq + hq * dk + e];
   __syncthreads();
 
   // ---- phase 1: scores of the local keys, local max
@@ -89,11 +90,11 @@ __global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__
   for (int jj = warp; jj < n; jj += 2 * (NT / 32)) {
     const int ja = j0 + jj, jb = ja + NT / 32;
     const bool hb = jj + NT / 32 < n;
-    const int64_t* ka = Kc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * dh;
-    const int64_t* kb = hb ? Kc + (((size_t)ptb[jb / PAGE] * n_kv + kvh) * PAGE + (jb % PAGE)) * dh : ka;
+    const int64_t* ka = Kc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * kst;
+    const int64_t* kb = hb ? Kc + (((size_t)ptb[jb / PAGE] * n_kv + kvh) * PAGE + (jb % PAGE)) * kst : ka;
     uint64_t aa = 0, ab = 0;
 #pragma unroll 4
-    for (int e = lane; e < dh; e += 32) {
+    for (int e = lane; e < dk; e += 32) {
       const uint64_t qe = (uint64_t)qs[e];
       aa += qe * (uint64_t)__ldg(ka + e);
       ab += qe * (uint64_t)__ldg(kb + e);
@@ -154,19 +155,19 @@ __global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__
     sc[jj] = w;
   }
   __syncthreads();
-  for (int e = tid; e < dh; e += NT) {
+  for (int e = tid; e < dv; e += NT) {
     uint64_t o0 = 0, o1 = 0;
     int jj = 0;
     for (; jj + 1 < n; jj += 2) {
       const int ja = j0 + jj, jb = ja + 1;
-      const int64_t va = __ldg(Vc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * dh + e);
-      const int64_t vb = __ldg(Vc + (((size_t)ptb[jb / PAGE] * n_kv + kvh) * PAGE + (jb % PAGE)) * dh + e);
+      const int64_t va = __ldg(Vc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * vst + e);
+      const int64_t vb = __ldg(Vc + (((size_t)ptb[jb / PAGE] * n_kv + kvh) * PAGE + (jb % PAGE)) * vst + e);
       o0 += (uint64_t)mulshr(sc[jj], va);
       o1 += (uint64_t)mulshr(sc[jj + 1], vb);
     }
     if (jj < n) {
       const int ja = j0 + jj;
-      o0 += (uint64_t)mulshr(sc[jj], __ldg(Vc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * dh + e));
+      o0 += (uint64_t)mulshr(sc[jj], __ldg(Vc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * vst + e));
     }
     xo[e] = o0 + o1;
   }
@@ -174,14 +175,14 @@ __global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__
   cluster_sync();
 
   // ---- cross-CTA sum of partial outputs; rank r finalises a slice of dh
-  const int per = (dh + CS - 1) / CS;
+  const int per = (dv + CS - 1) / CS;
   int need = 0;
-  for (int e = (int)rank * per + tid; e < min(dh, ((int)rank + 1) * per); e += NT) {
+  for (int e = (int)rank * per + tid; e < min(dv, ((int)rank + 1) * per); e += NT) {
     uint64_t o = 0;
 #pragma unroll
     for (int r = 0; r < CS; ++r) o += ld_cluster_u64(&xo[e], r);
     if (bad) continue;
-    const size_t off = (size_t)b * d + hq * dh + e;
+    const size_t off = (size_t)b * d + hq * dv + e;
     if (o_out) o_out[off] = (int64_t)o;
     if (X) {
       int8_t dg[8];
@@ -201,7 +202,7 @@ __global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__
 
 template <int CS>
 int launch(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride, const int* pos,
-           int n_heads, int n_kv, int dh, int64_t attn_scale, int max_T, int B, int8_t* X, int* lmax,
+           int n_heads, int n_kv, int dk, int dv, int kst, int vst, int64_t attn_scale, int max_T, int B, int8_t* X, int* lmax,
            int64_t* o_out, int* err, cudaStream_t st) {
   const size_t smem = (size_t)((max_T + CS - 1) / CS + 1) * 8;
   static size_t attr = 0;
@@ -224,24 +225,40 @@ int launch(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt
   at[1].val.programmaticStreamSerializationAllowed = arcb_pdl_enabled();
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_attn_cluster<CS>, q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh,
-                                     attn_scale, max_T, B, X, lmax, o_out, err);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_attn_cluster<CS>, q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dk, dv,
+                                     kst, vst, attn_scale, max_T, B, X, lmax, o_out, err);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 }  // namespace
 
+// General form: queries/keys of dk values, values of dv values, cache rows
+// of kst / vst int64 (MLA: one shared latent head, dk = r + dr, dv = r,
+// V = the first r values of the K rows).
+static int attn_any(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride,
+                    const int* pos, int n_heads, int n_kv, int dk, int dv, int kst, int vst, int64_t attn_scale,
+                    int max_T, int B, int cluster, int8_t* X, int* lmax, int64_t* o_out, int* err, cudaStream_t st) {
+  if (dk > 640 || dv > 512) return -1;
+  switch (cluster) {
+    case 1: return launch<1>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dk, dv, kst, vst, attn_scale, max_T, B, X, lmax, o_out, err, st);
+    case 2: return launch<2>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dk, dv, kst, vst, attn_scale, max_T, B, X, lmax, o_out, err, st);
+    case 4: return launch<4>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dk, dv, kst, vst, attn_scale, max_T, B, X, lmax, o_out, err, st);
+    case 8: return launch<8>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dk, dv, kst, vst, attn_scale, max_T, B, X, lmax, o_out, err, st);
+  }
+  return -2;
+}
+
 extern "C" int arcb_attn_cluster(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt,
                                  int pt_stride, const int* pos, int n_heads, int n_kv, int dh, int64_t attn_scale,
                                  int max_T, int B, int cluster, int8_t* X, int* lmax, int64_t* o_out, int* err,
                                  void* stream) {
-  if (dh > 256) return -1;
-  cudaStream_t st = (cudaStream_t)stream;
-  switch (cluster) {
-    case 1: return launch<1>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, max_T, B, X, lmax, o_out, err, st);
-    case 2: return launch<2>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, max_T, B, X, lmax, o_out, err, st);
-    case 4: return launch<4>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, max_T, B, X, lmax, o_out, err, st);
-    case 8: return launch<8>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, max_T, B, X, lmax, o_out, err, st);
-  }
-  return -2;
+  return attn_any(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, dh, dh, dh, dh, attn_scale, max_T, B, cluster, X,
+                  lmax, o_out, err, (cudaStream_t)stream);
+}
+
+extern "C" int arcb_attn_mla(const int64_t* q, const int64_t* cache, const int* pt, int pt_stride, const int* pos,
+                             int n_heads, int dk, int dv, int64_t attn_scale, int max_T, int B, int cluster,
+                             int64_t* o_out, int* err, void* stream) {
+  return attn_any(q, cache, cache, pt, pt_stride, pos, n_heads, 1, dk, dv, dk, dk, attn_scale, max_T, B, cluster,
+                  nullptr, nullptr, o_out, err, (cudaStream_t)stream);
 }

@@ -43,7 +43,7 @@ constexpr int NTHREADS = 192;
 constexpr int Q4_TILE = 128 * 64 + 128 * 2;
 constexpr int PAGE = 16;
 
-enum Mode : int { PARTIAL = 0, STORE = 1, RESID = 2, QKV = 3, SWIGLU = 4 };
+enum Mode : int { PARTIAL = 0, STORE = 1, RESID = 2, QKV = 3, SWIGLU = 4, MOE_COMBINE = 5 };
 
 struct Epi {
   int mode;
@@ -83,6 +83,14 @@ struct Epi {
   // dependency wait, 2 first stage consumed, 3 last MMA issued, 4 epilogue
   // done, 5 finaliser done, 6 exit
   unsigned long long* prof;
+  // Grouped (MoE) GEMMs over stacked experts: rows come in groups of
+  // grp_rows per expert; grp_koff > 0 makes group g read operand columns
+  // [g * grp_koff, g * grp_koff + K) (each expert's own intermediate).
+  int grp_rows;
+  int grp_koff;
+  // MOE_COMBINE: h[b, i] += (route[b, g] * y) >> 16 for routed experts.
+  const int64_t* route;
+  int route_ld;
 };
 
 template <int BN, bool Q4 = false>
@@ -181,6 +189,14 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
 #pragma unroll
         for (int l = 0; l < 8; ++l) E.X[l * ps + off] = dg[l];
       }
+      break;
+    }
+    case MOE_COMBINE: {
+      if (!valid) break;
+      const int g = m / E.grp_rows, i = m - g * E.grp_rows;
+      const int64_t w = E.route[(size_t)b * E.route_ld + g];
+      if (w != 0)
+        atomicAdd((unsigned long long*)(E.out + (size_t)b * E.ldo + i), (unsigned long long)mulshr(w, v));
       break;
     }
     default:
@@ -333,7 +349,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       for (int i = 0; i < n; ++i) {
         const int it = W.it0 + i, s = i % C::STAGES;
         const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
-        const int kx = W.kc(it) * BK;
+        const int kx = W.kc(it) * BK + (E.grp_koff ? (W.mt(it) * BM / E.grp_rows) * E.grp_koff : 0);
         if (i < pre) {
           tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, W.nt(it) * BN);
           ++issued;
