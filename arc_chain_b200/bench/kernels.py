@@ -95,8 +95,15 @@ def main():
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--only", default="")
+    ap.add_argument("--shape", default="", help="one of " + ",".join(SHAPES_7B))
     a = ap.parse_args()
     torch.cuda.set_device(0)
+    if a.shape:
+        M, K = SHAPES_7B[a.shape]
+        r = bench_fgemm(M, K, a.B, a.iters)
+        r["name"] = a.shape
+        print(json.dumps(r), flush=True)
+        return
     if a.only in ("", "gemm"):
         for name, (M, K) in SHAPES_7B.items():
             for pdl in (True, False):
