@@ -65,7 +65,7 @@ def rng_u64(seed: int, stream: int, n: int, start: int = 0) -> np.ndarray:
 
 def rng_i8(seed: int, stream: int, n: int) -> np.ndarray:
     """int8 weights in [-127, 127]; uses the C++ filler for big tensors."""
-    if n >= (1 << 24):
+    if n >= (1 << 20):
         from arc_chain_b200.oracle import arcref
 
         out = np.empty(n, dtype=np.int8)

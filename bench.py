@@ -34,6 +34,12 @@ BASELINE_MS = 76.0  # reference GPU engine, 7B INT8 decode, M2 Ultra (published)
 METRIC = "7B INT8 decode ms/token"
 
 
+def tp_comm_none():
+    from arc_chain_b200.runtime.engine import Comm
+
+    return Comm()
+
+
 def reference_arm(args):
     print(json.dumps({"impl": "reference", "metric": METRIC, "n_gpus": args.gpus,
                       "unavailable": "the reference is a Rust workspace (crates/arc-inference) with no Python "
@@ -53,6 +59,11 @@ def main():
     ap.add_argument("--gen-len", type=int, default=256)
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "batched", "moe", "specdec"],
+                    help="decode: the headline 7B single-stream ms/token; batched: 70B-architecture continuous "
+                         "batching tok/s; moe: MLA+MoE batch-32 decode; specdec: Q4 target + INT8 draft")
+    ap.add_argument("--requests", type=int, default=128)
+    ap.add_argument("--batch", type=int, default=0)
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -95,6 +106,33 @@ def main():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+
+    if args.workload != "decode":
+        from arc_chain_b200.bench import workloads as wl
+
+        with ClockSampler(local) as clk:
+            if args.workload == "batched":
+                out = wl.batched(args.model if args.model != "llama7b" else "llama70b", args.requests, rank, world,
+                                 comm or tp_comm_none())
+            elif args.workload == "moe":
+                out = wl.moe_decode("dsv2lite", args.batch or 32, 512, 256, args.steps, args.warmup)
+            else:
+                out = wl.spec_decode("llama7b", "draft1b", args.batch or 8, 256, 256, 4, rank, world,
+                                     comm or tp_comm_none())
+        out.update({"n_gpus": world, "warmup": args.warmup, "steps": args.steps, "scaling": "weak",
+                    "dtype": "int8 weights x int64 Q16 activations (exact)", "impl": "b200",
+                    "data": "synthetic: random-init weights (seeded), seeded prompts", "vs_baseline": None,
+                    "clocks": clk.summary()})
+        if rank == 0:
+            print(json.dumps(out))
+        if world > 1:
+            import gc
+
+            gc.collect()  # graphs holding NCCL calls must be gone before the group is destroyed
+            torch.cuda.synchronize()
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     cfg = preset(args.model)
     max_seq = 1 + args.prompt_len + args.gen_len + 1

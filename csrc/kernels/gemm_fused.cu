@@ -93,6 +93,13 @@ struct Epi {
   int route_ld;
 };
 
+// Ring depth for decode-sized tiles (BN <= 32).  A 5-stage ring (two CTAs
+// per SM, so the next GEMM could prefetch during this one's tail) measured
+// slower on the 7B decode (3.31 vs 3.15 ms/token): the deep ring wins.
+#ifndef ARCB_FG_SMALL_STAGES
+#define ARCB_FG_SMALL_STAGES 11
+#endif
+
 template <int BN, bool Q4 = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK;
@@ -100,7 +107,7 @@ struct Cfg {
   static constexpr int Q_BYTES = Q4 ? Q4_TILE : 0;        // staging of the packed Q4 tile
   static constexpr int STAGE_BYTES = (Q4 ? Q4_TILE : A_BYTES) + B_BYTES;  // bytes TMA brings per stage
   static constexpr int STAGES = Q4 ? (BN <= 32 ? 7 : (BN <= 64 ? 6 : (BN <= 128 ? 5 : 3)))
-                                   : (BN <= 16 ? 11 : (BN <= 32 ? 10 : (BN <= 64 ? 8 : (BN <= 128 ? 6 : 4))));
+                                   : (BN <= 32 ? ARCB_FG_SMALL_STAGES : (BN <= 64 ? 8 : (BN <= 128 ? 6 : 4)));
   static constexpr int ACC_COLS = BN < 32 ? 32 : BN;       // one TMEM accumulator
   static constexpr int TMEM_COLS = 2 * ACC_COLS;          // double buffered
   static constexpr int THREADS = Q4 ? 320 : NTHREADS;     // + 4 converter warps for Q4
