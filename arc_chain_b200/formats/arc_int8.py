@@ -58,6 +58,9 @@ class Int8Model:
     layers: List[Dict[str, np.ndarray]]
     vocab: List[str] = field(default_factory=list)
     extra: Dict[str, np.ndarray] = field(default_factory=dict)
+    # Full-precision Q16 embedding [vocab, d] (models imported from GGUF keep
+    # one; the ARC-INT8 file stores only emb / emb_s).
+    emb_q16: Optional[np.ndarray] = None
 
     def matrices(self):
         """(name, data, scales) in weight-hash order (1598-1617)."""

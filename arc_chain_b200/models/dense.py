@@ -91,6 +91,7 @@ class DenseModel:
     tp_size: int = 1
     vocab_offset: int = 0
     weight_hash: Optional[bytes] = None
+    emb_q16: Optional[torch.Tensor] = None  # full-precision Q16 embedding (GGUF imports)
 
     @property
     def n_heads_local(self):
@@ -225,8 +226,9 @@ def from_host(m: Int8Model, device, tp_rank: int = 0, tp_size: int = 1, q4: Opti
                                  T(L["attn_norm"]), T(L["ffn_norm"])))
     lo, hi = _vocab_range(c.vocab, tp_rank, tp_size)
     lm = Linear(T(m.out[lo:hi]), T(m.out_s[lo:hi])).build_map()
+    q16 = getattr(m, "emb_q16", None)
     return DenseModel(c, int(m.attn_scale), T(m.emb), T(m.emb_s), lm, T(m.final_norm), T(m.rope_cos),
-                      T(m.rope_sin), layers, tp_rank, tp_size, lo)
+                      T(m.rope_sin), layers, tp_rank, tp_size, lo, emb_q16=None if q16 is None else T(q16))
 
 
 def random_device(cfg: ModelConfig, device, seed: int = 0, tp_rank: int = 0, tp_size: int = 1) -> DenseModel:

@@ -59,6 +59,12 @@ def lib():
                 "arcref_blake3_finalize": (None, [vp, vp]),
                 "arcref_blake3_push_subtree_cv": (None, [vp, vp, C.c_int, u64]),
                 "arcref_blake3_free": (None, [vp]),
+                "arcref_blake3_new_derive": (vp, [C.c_char_p, C.c_size_t]),
+                "arcref_set_embedding_q16": (None, [vp, vp]),
+                "arcref_blake3_new_keyed": (vp, [vp]),
+                "arcref_blake3_context_key": (None, [C.c_char_p, C.c_size_t, vp]),
+                "arcref_blake3_batch_commit": (None, [vp, vp, C.c_int64, vp, C.c_char_p, C.c_size_t, vp]),
+                "arcref_merkle_root": (None, [vp, C.c_int64, C.c_char_p, C.c_size_t, vp]),
                 "arcref_rng_fill_i8": (None, [u64, u64, vp, i64]),
                 "arcref_rng_u64": (None, [u64, u64, vp, i64]),
                 "arcref_num_threads": (C.c_int, []),
@@ -160,6 +166,12 @@ class Model:
             ln = (C.c_int64 * len(lens))(*lens)
             self._keep += [ptrs, ln, cfg]
             self.h = L.arcref_from_arrays(C.byref(cfg), ptrs, ln)
+            q16 = getattr(model, "emb_q16", None)
+            if q16 is not None:
+                q16 = np.ascontiguousarray(q16, dtype=np.int64)
+                assert q16.shape == (c.vocab, c.d_model)
+                self._keep.append(q16)
+                L.arcref_set_embedding_q16(self.h, q16.ctypes.data)
         c = Config()
         L.arcref_get_config(self.h, C.byref(c))
         self.cfg = c

@@ -81,9 +81,9 @@ class StepBuffers:
         self.Xd = torch.zeros(rows, d, dtype=I8, device=dev)
         self.Xo = torch.zeros(rows, dl, dtype=I8, device=dev)
         self.Xf = torch.zeros(rows, dffl, dtype=I8, device=dev)
-        self.mXd = ops.TensorMap(self.Xd, self.bn)
-        self.mXo = ops.TensorMap(self.Xo, self.bn)
-        self.mXf = ops.TensorMap(self.Xf, self.bn)
+        self.mXd = ops.TensorMap(self.Xd, self.bn, min(self.bn, 32))
+        self.mXo = ops.TensorMap(self.Xo, self.bn, min(self.bn, 32))
+        self.mXf = ops.TensorMap(self.Xf, self.bn, min(self.bn, 32))
         L0 = model.layers[0]
         mmax = max(L0.qkv.M, d, L0.gu.M, model.vocab_local)
         self.P = torch.zeros(8 * B * mmax, dtype=I32, device=dev)
@@ -136,7 +136,11 @@ class Engine:
         nh, nkv = m.n_heads_local, m.n_kv_local
         dl, dffl = nh * dh, m.d_ff_local
         assert B == bb.B, "a StepBuffers instance serves exactly B slots (tensor maps are sized for it)"
-        ops.embed(bb.tokens, m.emb, m.emb_s, c.vocab, d, B, bb.h, bb.cnt, bb.ss)
+        q16 = getattr(m, "emb_q16", None)
+        if q16 is not None:
+            ops.embed(bb.tokens, q16, None, c.vocab, d, B, bb.h, bb.cnt, bb.ss)
+        else:
+            ops.embed(bb.tokens, m.emb, m.emb_s, c.vocab, d, B, bb.h, bb.cnt, bb.ss)
         ss = bb.ss
         E = self._epis(bb)
         reduce_in_kernel = cm.size == 1 or getattr(cm, "fused", False)

@@ -133,10 +133,12 @@ __global__ void k_embed(const int* __restrict__ tokens, const int8_t* __restrict
   const int b = blockIdx.x;
   const uint32_t tok = (uint32_t)tokens[b];
   const int idx = tok >= (uint32_t)V ? V - 1 : (int)tok;
-  const int64_t s = emb_s[idx];
+  // emb_s == null: emb is a full-precision Q16 table (int64 [V, d])
+  const int64_t s = emb_s ? emb_s[idx] : 0;
+  const int64_t* emb64 = (const int64_t*)emb;
   uint64_t acc = 0;
   for (int j = threadIdx.x; j < d; j += blockDim.x) {
-    const int64_t v = wmul((int64_t)emb[(size_t)idx * d + j], s);
+    const int64_t v = emb_s ? wmul((int64_t)emb[(size_t)idx * d + j], s) : emb64[(size_t)idx * d + j];
     h[(size_t)b * d + j] = v;
     acc += sq16(v);
   }

@@ -250,6 +250,9 @@ void softmax(const int64_t* x, int64_t n, int64_t* out) {
 struct arcref_model {
   arcref_config cfg{};
   I8W emb, out;
+  // Full-precision Q16 embedding [vocab, d] (GGUF-loaded models keep one:
+  // cached_integer_model.rs:1719-1723); null -> i8 * scale per row.
+  const int64_t* emb_q16 = nullptr;
   Vec64 final_norm, rope_cos, rope_sin;
   std::vector<Layer> layers;
   // Q4 mode
@@ -492,8 +495,11 @@ void arcref_forward(arcref_model* m, arcref_cache* cache, uint32_t token, int64_
   int64_t idx = std::min<int64_t>((int64_t)token, c.vocab - 1);
   std::vector<int64_t> h(d), n(d), q(d), kb(c.d_kv), vb(c.d_kv), ao(d), pr(d), g(c.d_ff),
       u(c.d_ff), fo(d);
-  // embedding_q16 = i8 * scale (1821-1830)
-  for (int64_t j = 0; j < d; ++j) h[j] = wmul((int64_t)m->emb.data[idx * d + j], m->emb.scales[idx]);
+  // embedding_q16: the model's own table, or i8 * scale (1821-1830)
+  if (m->emb_q16)
+    for (int64_t j = 0; j < d; ++j) h[j] = m->emb_q16[idx * d + j];
+  else
+    for (int64_t j = 0; j < d; ++j) h[j] = wmul((int64_t)m->emb.data[idx * d + j], m->emb.scales[idx]);
   auto mm = [&](int li, const I8W& w, const int64_t* x, int64_t* o) {
     if (m->q4) matmul_q4(m->q4w[li], x, o);
     else matmul_i8(w, x, o);
@@ -662,3 +668,71 @@ void arcref_set_threads(int n) { pool().resize(n); }
 extern "C" void arcref_blake3_push_subtree_cv(void* h, const uint32_t* cv8, int level, uint64_t total_chunks) {
   ((arcb3::Hasher*)h)->push_subtree_cv(cv8, level, total_chunks);
 }
+
+// ---------------------------------------------------------------- BLAKE3 modes and batch commits
+// Batch transaction commitments: item i hashed as derive_key(context,
+// [domain_i] ++ data[offs[i] .. offs[i+1])) (the domain byte only when
+// `domains` is given); the CPU counterpart of the GPU batch kernel
+// (reference: crates/arc-gpu/src/lib.rs:70-91 cpu_batch_commit{,_domain}).
+extern "C" void* arcref_blake3_new_derive(const char* context, size_t clen) {
+  auto* h = new arcb3::Hasher();
+  h->init_derive_key(context, clen);
+  return h;
+}
+extern "C" void* arcref_blake3_new_keyed(const uint8_t* key32) {
+  auto* h = new arcb3::Hasher();
+  h->init_keyed(key32);
+  return h;
+}
+extern "C" void arcref_blake3_context_key(const char* context, size_t clen, uint32_t* key8) {
+  arcb3::derive_context_key(context, clen, key8);
+}
+extern "C" void arcref_blake3_batch_commit(const uint8_t* data, const int64_t* offs, int64_t n,
+                                           const uint8_t* domains, const char* context, size_t clen,
+                                           uint8_t* out32) {
+  uint32_t k[8];
+  arcb3::derive_context_key(context, clen, k);
+  pool().parallel_for(n, [&](int64_t lo, int64_t hi) {
+    for (int64_t i = lo; i < hi; ++i) {
+      arcb3::Hasher h;
+      h.init();
+      memcpy(h.key, k, 32);
+      memcpy(h.cv, k, 32);
+      h.mode = arcb3::DERIVE_KEY_MATERIAL;
+      if (domains) h.update(domains + i, 1);
+      h.update(data + offs[i], (size_t)(offs[i + 1] - offs[i]));
+      h.finalize(out32 + 32 * i);
+    }
+  });
+}
+// Merkle root over 32-byte leaves: each layer hashes adjacent pairs (64-byte
+// payloads) with the batch commitment; an odd layer is padded with a zero
+// hash; no leaves -> zero hash; one leaf -> the leaf
+// (reference: crates/arc-gpu/src/lib.rs:414-460 gpu_merkle_root).
+extern "C" void arcref_merkle_root(const uint8_t* leaves, int64_t n, const char* context, size_t clen,
+                                   uint8_t* out32) {
+  if (n == 0) {
+    memset(out32, 0, 32);
+    return;
+  }
+  std::vector<uint8_t> cur(leaves, leaves + 32 * n);
+  int64_t m = n;
+  while (m > 1) {
+    if (m & 1) {
+      cur.resize(32 * (m + 1), 0);
+      ++m;
+    }
+    const int64_t np = m / 2;
+    std::vector<int64_t> offs(np + 1);
+    for (int64_t i = 0; i <= np; ++i) offs[i] = 64 * i;
+    std::vector<uint8_t> nxt(32 * np);
+    arcref_blake3_batch_commit(cur.data(), offs.data(), np, nullptr, context, clen, nxt.data());
+    cur.swap(nxt);
+    m = np;
+  }
+  memcpy(out32, cur.data(), 32);
+}
+
+// Installs a full-precision Q16 embedding table (borrowed; the caller keeps
+// it alive for the model's lifetime).
+extern "C" void arcref_set_embedding_q16(arcref_model* m, const int64_t* q16) { m->emb_q16 = q16; }
