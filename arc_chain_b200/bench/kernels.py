@@ -20,6 +20,9 @@ from arc_chain_b200.ops import int_ops as ops
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 SHAPES_7B = {"qkv": (12288, 4096), "wo": (4096, 4096), "gate_up": (22016, 4096), "down": (4096, 11008),
              "lm_head": (32000, 4096)}
+# DeepSeek-V2-Lite architecture: stacked 66-expert gate/up and down, MLA W_o.
+SHAPES_MOE = {"moe_gate_up": (185856, 2048), "moe_down": (135168, 1408), "mla_wo": (2048, 2048),
+              "mla_q": (3072, 2048)}
 
 
 def hbm_peak_gbs() -> float:
@@ -30,7 +33,10 @@ def hbm_peak_gbs() -> float:
         return 6650.0
 
 
-def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True):
+def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True, sub_box=None, ctas=None, limbs=3):
+    """One fused GEMM alone.  sub_box: rows per TMA box of the limb operand
+    (None = the whole BN tile); ctas: persistent CTA budget (None = the
+    split_ctas heuristic, 0 = one per SM); limbs: device limb count."""
     dev = torch.device("cuda")
     nbytes = M * K
     copies = max(2, -(-300_000_000 // nbytes))
@@ -39,13 +45,14 @@ def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True):
     S = torch.randint(1, 100, (M,), dtype=torch.int64, device=dev)
     bn = ops.fgemm_bn(B)
     X = torch.randint(-127, 128, (max(8 * B, bn), K), dtype=torch.int8, device=dev)
-    xm = ops.TensorMap(X, bn)
-    lmax = torch.tensor([3], dtype=torch.int32, device=dev)
+    xm = ops.TensorMap(X, bn, min(sub_box, bn) if sub_box else None)
+    lmax = torch.tensor([limbs], dtype=torch.int32, device=dev)
     P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
     tiles = torch.zeros(M // 128 + 2, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     out = torch.zeros(B, M, dtype=torch.int64, device=dev)
     e = ops.epi(ops.STORE if mode == "store" else ops.PARTIAL, S, err, out=out, ldo=M)
+    e.max_ctas = ops.split_ctas(M, B, bn) if ctas is None else ctas
     ops.set_pdl(pdl)
     for i in range(5):
         ops.fgemm(maps[i % copies], xm, M, K, B, lmax, P, tiles, e)
@@ -59,7 +66,8 @@ def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True):
     us = t0.elapsed_time(t1) * 1000 / iters
     gbs = nbytes / us / 1e3
     assert int(err.item()) == 0
-    return {"kernel": "fgemm", "M": M, "K": K, "B": B, "mode": mode, "pdl": pdl, "us": round(us, 2),
+    return {"kernel": "fgemm", "M": M, "K": K, "B": B, "mode": mode, "pdl": pdl, "sub_box": sub_box,
+            "ctas": e.max_ctas, "limbs": limbs, "us": round(us, 2),
             "GB_s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak_gbs(), 3)}
 
 
@@ -110,6 +118,17 @@ def main():
                 r = bench_fgemm(M, K, a.B, a.iters, pdl=pdl)
                 r["name"] = name
                 print(json.dumps(r), flush=True)
+    if a.only == "batch":
+        # sub-box limb loads and CTA budget across batch sizes
+        shapes = dict(SHAPES_7B, **SHAPES_MOE)
+        for B in (1, 8, 32):
+            for name in ("qkv", "gate_up", "moe_gate_up", "moe_down", "mla_wo", "mla_q"):
+                M, K = shapes[name]
+                for sub, ctas in ((None, 0), (32, 0), (32, None)):
+                    r = bench_fgemm(M, K, B, a.iters, sub_box=sub, ctas=ctas)
+                    r["name"] = name
+                    print(json.dumps(r), flush=True)
+        return
     if a.only == "timeline":
         for name, (M, K) in SHAPES_7B.items():
             print(json.dumps(timeline_fgemm(M, K, a.B)), flush=True)

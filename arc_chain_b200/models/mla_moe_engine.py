@@ -68,13 +68,24 @@ class MlaMoeModel:
     layers: List[MlaLayer]
     tp_size: int = 1
     vocab_offset: int = 0
+    ep_rank: int = 0
+    ep_size: int = 1
 
     @property
     def vocab_local(self):
         return self.lm.M
 
 
-def from_host(m: Int8Model, device) -> MlaMoeModel:
+def local_experts(cfg: ModelConfig, ep_rank: int = 0, ep_size: int = 1) -> List[int]:
+    """Global expert indices (routed 0..E-1, then shared E..E+S-1) that
+    expert-parallel rank `ep_rank` of `ep_size` holds: g % ep_size == ep_rank."""
+    G = cfg.n_experts + cfg.n_shared_experts
+    return [g for g in range(G) if g % ep_size == ep_rank]
+
+
+def from_host(m: Int8Model, device, ep_rank: int = 0, ep_size: int = 1) -> MlaMoeModel:
+    """Device model from a host model; with ep_size > 1 only this rank's
+    experts are kept (all other weights are replicated)."""
     c = m.cfg
     dev = torch.device(device)
     T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
@@ -89,18 +100,75 @@ def from_host(m: Int8Model, device) -> MlaMoeModel:
         else:
             ly.router = lin("router")
             gw, gs, dw, ds = [], [], [], []
-            for kind, cnt in (("e", c.n_experts), ("s", c.n_shared_experts)):
-                for e in range(cnt):
-                    gw.append(interleave_pairs(L[kind + "g"][e], L[kind + "u"][e]))
-                    gs.append(interleave_pairs(L[kind + "g_s"][e], L[kind + "u_s"][e]))
-                    dw.append(L[kind + "d"][e])
-                    ds.append(L[kind + "d_s"][e])
+            for g in local_experts(c, ep_rank, ep_size):
+                kind, e = ("e", g) if g < c.n_experts else ("s", g - c.n_experts)
+                gw.append(interleave_pairs(L[kind + "g"][e], L[kind + "u"][e]))
+                gs.append(interleave_pairs(L[kind + "g_s"][e], L[kind + "u_s"][e]))
+                dw.append(L[kind + "d"][e])
+                ds.append(L[kind + "d_s"][e])
             ly.egu = Linear(T(np.concatenate(gw)), T(np.concatenate(gs))).build_map()
             ly.edown = Linear(T(np.concatenate(dw)), T(np.concatenate(ds))).build_map()
         layers.append(ly)
     lm = Linear(T(m.out), T(m.out_s)).build_map()
     return MlaMoeModel(c, int(m.attn_scale), T(m.emb), T(m.emb_s), lm, T(m.final_norm), T(m.rope_cos),
-                       T(m.rope_sin), layers)
+                       T(m.rope_sin), layers, ep_rank=ep_rank, ep_size=ep_size)
+
+
+def random_device(cfg: ModelConfig, device, seed: int = 0, ep_rank: int = 0, ep_size: int = 1) -> MlaMoeModel:
+    """Seeded random-init MLA + MoE model generated on the device (the same
+    values as :func:`arc_chain_b200.models.mla_moe.random_mla_moe_model`),
+    holding only this expert-parallel rank's experts."""
+    from arc_chain_b200.formats import gen
+    from arc_chain_b200.models.mla_moe import EXPERT_SLOT0, SLOTS, shapes
+
+    dev = torch.device(device)
+    d, V, f = cfg.d_model, cfg.vocab, cfg.moe_d_ff
+
+    def mat(tid, rows, cols, base=None):
+        w = torch.empty(rows * cols, dtype=I8, device=dev)
+        ops.rng_i8(seed, tid << 2, w)
+        sc = gen.row_scales(seed, (tid << 2) | 1, rows, gen.scale_base(cols) if base is None else base)
+        return w.view(rows, cols), torch.from_numpy(sc).to(dev)
+
+    def gamma(tid, n):
+        return torch.from_numpy(gen.gamma(seed, (tid << 2) | 1, n)).to(dev)
+
+    emb, emb_s = mat(0, V, d, base=gen.EMB_SCALE_BASE)
+    out, out_s = mat(1, V, d)
+    rc, rs = gen.rope_tables(cfg.qk_rope_dim, cfg.max_seq, cfg.rope_theta)
+    layers = []
+    for l in range(cfg.n_layers):
+        ext = lambda slot: gen.ext_tensor_id(l, slot)
+        W = {n: mat(ext(SLOTS[n]), *rc_) for n, rc_ in shapes(cfg, l).items()}
+        lin = lambda n: Linear(*W[n]).build_map()
+        ly = MlaLayer(lin("q"), lin("kva"), gamma(ext(SLOTS["kv_norm"]), cfg.kv_lora_rank), W["uk"][0].contiguous(),
+                      W["uk"][1], W["uv"][0].contiguous(), W["uv"][1], lin("wo"),
+                      gamma(ext(SLOTS["attn_norm"]), d), gamma(ext(SLOTS["ffn_norm"]), d))
+        if l < cfg.first_dense_layers:
+            (wg, sg), (wu, su) = W["gate"], W["up"]
+            ly.gu = Linear(interleave_pairs(wg, wu).contiguous(), interleave_pairs(sg, su).contiguous()).build_map()
+            ly.down = lin("down")
+        else:
+            ly.router = lin("router")
+            gw, gs, dw, ds = [], [], [], []
+            for g in local_experts(cfg, ep_rank, ep_size):
+                base = EXPERT_SLOT0 + 3 * g
+                wg, sg = mat(ext(base), f, d)
+                wu, su = mat(ext(base + 1), f, d)
+                wd, sd = mat(ext(base + 2), d, f)
+                gw.append(interleave_pairs(wg, wu))
+                gs.append(interleave_pairs(sg, su))
+                dw.append(wd)
+                ds.append(sd)
+            ly.egu = Linear(torch.cat(gw).contiguous(), torch.cat(gs).contiguous()).build_map()
+            ly.edown = Linear(torch.cat(dw).contiguous(), torch.cat(ds).contiguous()).build_map()
+            del gw, dw
+        layers.append(ly)
+        del W
+    lm = Linear(out, out_s).build_map()
+    return MlaMoeModel(cfg, int(cfg.resolved_attn_scale()), emb.contiguous(), emb_s, lm, gamma(2, d),
+                       torch.from_numpy(rc).to(dev), torch.from_numpy(rs).to(dev), layers, ep_rank=ep_rank,
+                       ep_size=ep_size)
 
 
 class MlaBuffers:
@@ -125,8 +193,9 @@ class MlaBuffers:
         self.Xo = torch.zeros(rows, H * dv, dtype=I8, device=dev)
         self.Xf = torch.zeros(rows, max(c.d_ff, 16), dtype=I8, device=dev)
         self.Xm = torch.zeros(rows, max(G * c.moe_d_ff, 16), dtype=I8, device=dev)
-        self.mXd, self.mXo = ops.TensorMap(self.Xd, self.bn), ops.TensorMap(self.Xo, self.bn)
-        self.mXf, self.mXm = ops.TensorMap(self.Xf, self.bn), ops.TensorMap(self.Xm, self.bn)
+        sub = min(self.bn, 32)
+        self.mXd, self.mXo = ops.TensorMap(self.Xd, self.bn, sub), ops.TensorMap(self.Xo, self.bn, sub)
+        self.mXf, self.mXm = ops.TensorMap(self.Xf, self.bn, sub), ops.TensorMap(self.Xm, self.bn, sub)
         ms = [d, c.vocab, H * (dn + dr), r + dr, 2 * c.d_ff]
         for ly in model.layers:
             for lin in (ly.egu, ly.edown, ly.router):
@@ -155,10 +224,17 @@ class MlaMoeEngine(Engine):
     """Engine for the MLA + MoE model (single GPU); reuses the dense engine's
     request, prefill, generate and CUDA-graph machinery."""
 
-    def __init__(self, model: MlaMoeModel, n_pages: Optional[int] = None, max_seq: Optional[int] = None):
+    def __init__(self, model: MlaMoeModel, n_pages: Optional[int] = None, max_seq: Optional[int] = None,
+                 comm: Optional[Comm] = None):
         self.m = model
         c = model.cfg
-        self.comm = Comm()
+        self.comm = comm or Comm()
+        self.ep = getattr(self.comm, "ep", False)
+        if self.ep and (self.comm.size != model.ep_size or self.comm.rank != model.ep_rank):
+            raise ValueError("model's expert shard does not match the communicator's rank/size")
+        if not self.ep and model.ep_size != 1:
+            raise ValueError("an expert-sharded model needs an expert-parallel communicator")
+        self.n_moe = sum(1 for ly in model.layers if ly.edown is not None)
         self.max_seq = max_seq or c.max_seq
         self.max_pages = (self.max_seq + PAGE - 1) // PAGE
         if n_pages is None:
@@ -168,6 +244,9 @@ class MlaMoeEngine(Engine):
         self._bufs = {}
         self._graphs = {}
         self._rid = 0
+
+    def _moe_index(self, layer: int) -> int:
+        return sum(1 for ly in self.m.layers[:layer] if ly.edown is not None)
 
     def buffers(self, B: int, gen_cap: int = 0) -> MlaBuffers:
         key = (B, gen_cap)
@@ -195,6 +274,11 @@ class MlaMoeEngine(Engine):
                                    lmax_out=bb.cnt[4 * l + 3:4 * l + 4])
                 ed = ops.epi(ops.MOE_COMBINE, ly.edown.s, bb.err, out=bb.h, ldo=d, route=bb.route, route_ld=G)
                 ed.grp_rows, ed.grp_koff = d, c.moe_d_ff
+                if self.ep:
+                    # local group g is global expert rank + g * size
+                    ed.route = bb.route.data_ptr() + 8 * m.ep_rank
+                    ed.route_gs = m.ep_size
+                    ed = self.comm.combine_epi(ed, bb, self._moe_index(l), self.n_moe, d)
                 e["edown"] = ed
             out.append(e)
         out.append({"lm": ops.epi(ops.STORE, m.lm.s, bb.err, out=bb.logits, ldo=m.lm.M)})
@@ -230,6 +314,8 @@ class MlaMoeEngine(Engine):
                 ops.moe_route(bb.rlog, c.n_experts, c.n_shared_experts, c.moe_top_k, B, bb.route)
                 ops.linear_gemm(ly.egu, bb.mXd, B, c2, bb.P, bb.tiles, e["egu"])
                 ops.linear_gemm(ly.edown, bb.mXm, B, c3, bb.P, bb.tiles, e["edown"])
+                if self.ep:
+                    self.comm.after_combine(bb, self._moe_index(l), self.n_moe, d)
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
             ops.rmsnorm_limbs(bb.h, m.final_norm, d, B, bb.Xd, cf)

@@ -37,6 +37,13 @@ _SIGS = {
     "arcb_verify_sample": (i32, [vp, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
     "arcb_blake3_chunk_cvs": (i32, [vp, vp, i32, i64, i64, vp, vp]),
     "arcb_blake3_parents": (i32, [vp, i64, vp, vp]),
+    "arcb_blake3_batch_commit": (i32, [vp, i64, vp, i64, vp, vp, i64, vp, vp]),
+    "arcb_merkle_root": (i32, [vp, i64, vp, vp, vp, vp]),
+    "arcb_ep_wait_apply": (i32, [vp, vp, C.c_uint64, vp, vp, i64, vp, vp, vp]),
+    "arcb_ed25519_init": (i32, [vp, vp, vp, vp, vp, vp]),
+    "arcb_ed25519_verify": (i32, [vp, vp, vp, vp, i64, vp, vp]),
+    "arcb_ed25519_verify_prehashed": (i32, [vp, i64, vp, vp]),
+    "arcb_ed25519_selftest": (i32, [i32, vp, i64, vp, vp, vp]),
     "arcb_mla_kv": (i32, [vp, i32, i32, vp, i32, vp, vp, i32, vp, vp, vp, i32, i32, vp, vp]),
     "arcb_mla_q": (i32, [vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, i32, i32, vp, vp]),
     "arcb_mla_out": (i32, [vp, i32, i32, i32, vp, vp, i32, vp, vp, vp, vp]),

@@ -32,16 +32,22 @@ def _count():
 
 class TensorMap:
     """A CUtensorMap (128 bytes, 64-byte aligned host memory) over a 2-D int8
-    tensor [rows, cols], box = {128 bytes of K, box_rows}, 128-byte swizzle."""
+    tensor [rows, cols], box = {128 bytes of K, box_rows}, 128-byte swizzle.
 
-    def __init__(self, t: torch.Tensor, box_rows: int):
+    For a limb operand, ``enc_rows`` < ``box_rows`` encodes a shorter box: the
+    fused GEMM then loads a BN = box_rows tile as box_rows / enc_rows boxes and
+    skips those past the live rows."""
+
+    def __init__(self, t: torch.Tensor, box_rows: int, enc_rows: Optional[int] = None):
         assert t.dtype == torch.int8 and t.dim() == 2 and t.is_contiguous()
         self._raw = C.create_string_buffer(128 + 64)
         self.addr = (C.addressof(self._raw) + 63) & ~63
         self.tensor = t
         self.rows, self.cols = t.shape
         self.box_rows = box_rows
-        rc = lib().arcb_tmap_i8(self.addr, t.data_ptr(), self.rows, self.cols, box_rows)
+        self.enc_rows = enc_rows or box_rows
+        assert box_rows % self.enc_rows == 0
+        rc = lib().arcb_tmap_i8(self.addr, t.data_ptr(), self.rows, self.cols, self.enc_rows)
         if rc != 0:
             raise RuntimeError(f"cuTensorMapEncodeTiled failed ({rc}) for {tuple(t.shape)} box {box_rows}")
 
@@ -181,7 +187,9 @@ class Epi(C.Structure):
                 ("err", C.c_void_p), ("B", C.c_int),
                 ("rp", C.c_int), ("npeers", C.c_int), ("peer_P", C.c_void_p), ("peer_cnt", C.c_void_p),
                 ("peer_lmax", C.c_void_p), ("cnt_local", C.c_void_p), ("lmax_fin", C.c_void_p), ("prof", C.c_void_p),
-                ("grp_rows", C.c_int), ("grp_koff", C.c_int), ("route", C.c_void_p), ("route_ld", C.c_int)]
+                ("grp_rows", C.c_int), ("grp_koff", C.c_int), ("route", C.c_void_p), ("route_ld", C.c_int),
+                ("max_ctas", C.c_int), ("b_box", C.c_int), ("route_gs", C.c_int), ("peer_h", C.c_void_p),
+                ("peer_sig", C.c_void_p)]
 
 
 PARTIAL, STORE, RESID, QKV, SWIGLU, MOE_COMBINE = 0, 1, 2, 3, 4, 5
@@ -195,6 +203,7 @@ def fgemm(wmap: TensorMap, xmap: TensorMap, M: int, K: int, B: int, lmax, P, til
           pdl: bool = True) -> None:
     """Persistent stream-K limb GEMM with the finalize fused in (mode in epi)."""
     _count()
+    epi.b_box = xmap.enc_rows if xmap.enc_rows < xmap.box_rows else 0
     check(lib().arcb_fgemm(wmap.addr, xmap.addr, M, K, B, xmap.box_rows, _p(lmax), _p(P), _p(tile_cnt),
                            C.addressof(epi), int(pdl), _s()), "fgemm")
 
@@ -308,12 +317,30 @@ def fgemm_q4(packed: torch.Tensor, xmap: TensorMap, M: int, K: int, B: int, lmax
              pdl: bool = True) -> None:
     """K2: the fused GEMM over Q4 tiles (dequantised to int8 in shared memory)."""
     _count()
+    epi.b_box = xmap.enc_rows if xmap.enc_rows < xmap.box_rows else 0
     check(lib().arcb_fgemm_q4(_p(packed), xmap.addr, M, K, B, xmap.box_rows, _p(lmax), _p(P), _p(tile_cnt),
                               C.addressof(epi), int(pdl), _s()), "fgemm_q4")
 
 
+# (max batch, CTAs per tile) pairs for split_ctas; the last entry covers all
+# larger batches.
+SPLIT_TABLE = [(2, 64), (8, 4), (32, 2), (1 << 30, 1)]
+
+
+def split_ctas(M: int, B: int, bn: int) -> int:
+    """CTA budget of the stream-K GEMM: at decode batch 1-2 every SM streams
+    (tiles split many ways; the partials are few); as the batch grows each
+    split adds B x limbs partials per row, so tiles are shared by fewer CTAs."""
+    splits = next(s for b, s in SPLIT_TABLE if B <= b)
+    mt = (M + BM - 1) // BM
+    ntu = max(1, (3 * B + bn - 1) // bn)
+    return max(1, mt * ntu * splits)
+
+
 def linear_gemm(lin, xmap: TensorMap, B: int, lmax, P, tile_cnt, epi: Epi) -> None:
     """Dispatch a Linear (int8 tiles or Q4 tiles) to its fused GEMM."""
+    if epi.rp == 0 and not epi.peer_sig:  # cross-rank arrival counts assume the full grid
+        epi.max_ctas = min(num_sms(), split_ctas(lin.M, B, xmap.box_rows))
     if getattr(lin, "q4", None) is not None:
         fgemm_q4(lin.q4, xmap, lin.M, lin.K, B, lmax, P, tile_cnt, epi)
     else:
@@ -356,3 +383,11 @@ def attn_mla(Q, cache, pt, pos, H, dk, dv, attn_scale, max_T, B, oc, err, cluste
 def moe_route(logits, E, S, top_k, B, route):
     _count()
     check(lib().arcb_moe_route(_p(logits), logits.shape[1], E, S, top_k, B, _p(route), _s()), "moe_route")
+
+
+def ep_wait_apply(cnt, epoch, per_call: int, h, delta, done, err) -> None:
+    """Expert-parallel combine: bounded wait for this call's arrivals, then
+    h += delta (wrapping) and delta = 0 (csrc/kernels/ep_ops.cu)."""
+    _count()
+    check(lib().arcb_ep_wait_apply(_p(cnt), _p(epoch), per_call, _p(h), _p(delta), h.numel(), _p(done), _p(err),
+                                   _s()), "ep_wait_apply")

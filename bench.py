@@ -115,7 +115,8 @@ def main():
                 out = wl.batched(args.model if args.model != "llama7b" else "llama70b", args.requests, rank, world,
                                  comm or tp_comm_none())
             elif args.workload == "moe":
-                out = wl.moe_decode("dsv2lite", args.batch or 32, 512, 256, args.steps, args.warmup)
+                out = wl.moe_decode("dsv2lite", args.batch or 32, args.prompt_len if args.prompt_len != 128 else 512,
+                                    256, args.steps, args.warmup)
             else:
                 out = wl.spec_decode("llama7b", "draft1b", args.batch or 8, 256, 256, 4, rank, world,
                                      comm or tp_comm_none())

@@ -91,6 +91,23 @@ struct Epi {
   // MOE_COMBINE: h[b, i] += (route[b, g] * y) >> 16 for routed experts.
   const int64_t* route;
   int route_ld;
+  // Upper bound on persistent CTAs (0 = one per SM).  Fewer CTAs means
+  // fewer CTAs share a tile, so less partial-sum traffic at larger batch.
+  int max_ctas;
+  // Rows per TMA box of the limb operand's tensor map (0 = BN).  With a box
+  // smaller than BN only the boxes that hold live rows (limbs x slots) are
+  // loaded, so a batch whose activations need few limbs does not stream the
+  // unused limb planes.
+  int b_box;
+  // Expert parallelism: MOE_COMBINE reads route column g * route_gs of
+  // local group g (route points at this rank's first expert column;
+  // 0 = stride 1) and, with peer_h set, adds into the npeers targets
+  // peer_h[p] (every rank's combine buffer) instead of out; with peer_sig
+  // set every CTA, once its adds are fenced, increments every rank's
+  // arrival counter peer_sig[p] by one.
+  int route_gs;
+  int64_t* const* peer_h;
+  unsigned long long* const* peer_sig;
 };
 
 // Ring depth for decode-sized tiles (BN <= 32).  A 5-stage ring (two CTAs
@@ -201,9 +218,16 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
     case MOE_COMBINE: {
       if (!valid) break;
       const int g = m / E.grp_rows, i = m - g * E.grp_rows;
-      const int64_t w = E.route[(size_t)b * E.route_ld + g];
-      if (w != 0)
-        atomicAdd((unsigned long long*)(E.out + (size_t)b * E.ldo + i), (unsigned long long)mulshr(w, v));
+      const int64_t w = E.route[(size_t)b * E.route_ld + (size_t)g * (E.route_gs ? E.route_gs : 1)];
+      if (w != 0) {
+        const unsigned long long add = (unsigned long long)mulshr(w, v);
+        const size_t off = (size_t)b * E.ldo + i;
+        if (E.peer_h) {
+          for (int p = 0; p < E.npeers; ++p) atomicAdd((unsigned long long*)(E.peer_h[p] + off), add);
+        } else {
+          atomicAdd((unsigned long long*)(E.out + off), add);
+        }
+      }
       break;
     }
     default:
@@ -306,6 +330,18 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
 
   // Weight tile of work item `it` into stage s: an int8 tile by TMA, or the
   // packed Q4 tile by a bulk copy into the staging area (converted below).
+  // Decode-sized tiles (BN <= 32) always load their one box; the sub-box
+  // path and the batched TMEM reads below exist for BN >= 64 only, so the
+  // small-batch kernels keep their original code.
+  const int bbox = (BN >= 64 && E.b_box > 0 && E.b_box < BN) ? E.b_box : BN;
+  auto load_b = [&](int s, int it, int kx, int rows) {
+    if constexpr (BN >= 64) {
+      for (int r0 = 0; r0 < rows; r0 += bbox)
+        tma_load_2d(b_base + s * C::B_BYTES + r0 * BK, &tmB, full(s), kx, W.nt(it) * BN + r0);
+    } else {
+      tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, W.nt(it) * BN);
+    }
+  };
   auto load_a = [&](int s, int it) {
     if constexpr (Q4) {
       const uint8_t* src = q4w + (size_t)(W.mt(it) * W.nch + W.kc(it)) * Q4_TILE;
@@ -357,8 +393,8 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         const int it = W.it0 + i, s = i % C::STAGES;
         const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
         const int kx = W.kc(it) * BK + (E.grp_koff ? (W.mt(it) * BM / E.grp_rows) * E.grp_koff : 0);
-        if (i < pre) {
-          tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, W.nt(it) * BN);
+        if (i < pre) {  // its transaction count (full box) was set before the dependency wait
+          load_b(s, it, kx, BN);
           ++issued;
           continue;
         }
@@ -367,9 +403,10 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(full(s), C::STAGE_BYTES);
+        const int live = BN >= 64 ? min(BN, (min(BN, nrows - W.nt(it) * BN) + bbox - 1) / bbox * bbox) : BN;
+        mbar_arrive_expect_tx(full(s), (Q4 ? Q4_TILE : C::A_BYTES) + live * BK);
         load_a(s, it);
-        tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, W.nt(it) * BN);
+        load_b(s, it, kx, live);
         ++issued;
       }
       if (!ok)
@@ -479,7 +516,24 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       const bool direct = whole && ntu == 1 && E.mode != PARTIAL && !E.rp;
       const uint32_t taddr = tmem + (uint32_t)(tb * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
       int need = 0;
-      if (direct) {
+      if (BN >= 64 && direct && (B & 7) == 0) {
+        // 8 slots x L limbs per TMEM read batch (columns l * B + b0 .. + 7)
+        for (int b0 = 0; b0 < B; b0 += 8) {
+          uint32_t r[8][8];
+#pragma unroll
+          for (int l = 0; l < 8; ++l)
+            if (l < L) tmem_ld8(taddr + (uint32_t)(l * B + b0), r[l]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint64_t acc = 0;
+#pragma unroll
+            for (int l = 0; l < 8; ++l)
+              if (l < L) acc += (uint64_t)(int64_t)(int)r[l][j] << (8 * l);
+            apply_row(E, M, m, valid, b0 + j, acc, need);
+          }
+        }
+      } else if (direct) {
         for (int b = 0; b < B; ++b) {
           uint32_t r[8];
           for (int l = 0; l < L; ++l) tmem_ld1(taddr + (uint32_t)(l * B + b), r[l]);
@@ -549,6 +603,12 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       it = se;
     }
     if (E.prof && warp == 2 && lane == 0) E.prof[blockIdx.x * 8 + 4] = globaltimer_ns();
+    if (E.peer_sig) {
+      __threadfence_system();
+      epi_bar();
+      if (warp == 2 && lane == 0)
+        for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_sig[p], 1ull);
+    }
     if (E.rp && E.mode != PARTIAL) {
       // ---- finaliser: tiles mt = blockIdx.x (mod grid) of this rank's copy
       const int target = E.npeers * n_tiles_max * W.nch;
@@ -614,7 +674,7 @@ int launch(const CUtensorMap* a, const CUtensorMap* b, int M, int K, int B, cons
   }
   const int n_tiles_max = (8 * B + BN - 1) / BN;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_sms());
+  cfg.gridDim = dim3(E.max_ctas > 0 && E.max_ctas < num_sms() ? E.max_ctas : num_sms());
   cfg.blockDim = dim3(C::THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;

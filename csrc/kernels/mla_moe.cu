@@ -70,67 +70,140 @@ __global__ void k_mla_kv(const int64_t* __restrict__ kva, int r, int dr, const i
   }
 }
 
-// Absorbed query of head h, slot b: Q[b,h] = [Lin_uk[h](q_nope) | RoPE(q_rope)].
-// q: [B, H, dn + dr]; W_uk: [H * r, dn] int8 row-major, scales [H * r].
-// grid = (H, B), block 256.
-__global__ void k_mla_q(const int64_t* __restrict__ q, int H, int dn, int dr, int r, const int8_t* __restrict__ Wuk,
-                        const int64_t* __restrict__ suk, const int* __restrict__ pos,
-                        const int64_t* __restrict__ rcos, const int64_t* __restrict__ rsin, int max_seq,
-                        int64_t* __restrict__ Q) {
-  pdl_wait_dep();
-  pdl_allow_next();
-  extern __shared__ int64_t qn[];  // dn values
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int64_t* qh = q + ((size_t)b * H + h) * (dn + dr);
-  int64_t* out = Q + ((size_t)b * H + h) * (r + dr);
-  for (int e = threadIdx.x; e < dn; e += blockDim.x) qn[e] = qh[e];
-  __syncthreads();
-  const int8_t* W = Wuk + (size_t)h * r * dn;
-  for (int i = threadIdx.x; i < r; i += blockDim.x) {
-    uint64_t acc = 0;
-    const int8_t* wr = W + (size_t)i * dn;
-    for (int e = 0; e < dn; ++e) acc += (uint64_t)(int64_t)wr[e] * (uint64_t)qn[e];
-    out[i] = mulshr((int64_t)acc, suk[(size_t)h * r + i]);
-  }
-  const int p = min(max(pos[b], 0), max_seq - 1);
-  const int half = dr / 2;
-  for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    int64_t x0 = qh[dn + i], x1 = qh[dn + i + half];
-    rope_pair(x0, x1, rcos[(size_t)p * half + i], rsin[(size_t)p * half + i]);
-    out[r + i] = x0;
-    out[r + i + half] = x1;
+// Per-head batched INT8 linear, the shape shared by the two absorbed MLA
+// projections: y[b, h, i] = (sum_e W[h * R + i, e] * x[b, h, e]) * s >> 16
+// for i < R, e < Kd, over all B slots.  One block owns RB rows of one head:
+// the rows are read from HBM once (not once per slot) into shared memory with
+// a padded stride (odd word count: lanes reading one word of consecutive rows
+// hit distinct banks); slots are staged SC at a time.  Thread t computes row
+// t % RB for slot t / RB of the staged chunk.  The i8 x i64 products are
+// summed in wrapping u64 by four accumulators (the sum modulo 2^64 does not
+// depend on the order, so this equals the oracle's sequential sum).
+constexpr int HL_RB = 16;
+constexpr int HL_SC = 16;
+constexpr int HL_THREADS = HL_RB * HL_SC;
+
+__host__ __device__ inline size_t hl_qstride(int Kd) { return (size_t)Kd + 2; }  // i64 units
+__host__ __device__ inline size_t hl_wstride(int Kd) { return (size_t)Kd + 4; }  // bytes
+inline size_t hl_smem(int Kd) { return HL_SC * hl_qstride(Kd) * 8 + HL_RB * hl_wstride(Kd); }
+
+// Stages W rows [r0, r0 + RB) of head h; returns nothing (caller syncs).
+__device__ __forceinline__ void hl_stage_w(const int8_t* __restrict__ W, int h, int R, int Kd, int r0,
+                                           uint8_t* ws) {
+  const int words = Kd >> 2;
+  const size_t wst = hl_wstride(Kd);
+  for (int idx = threadIdx.x; idx < HL_RB * words; idx += blockDim.x) {
+    const int rr = idx / words, c = idx - rr * words;
+    uint32_t v = 0;
+    if (r0 + rr < R) v = __ldg((const uint32_t*)(W + ((size_t)h * R + r0 + rr) * Kd) + c);
+    *(uint32_t*)(ws + rr * wst + 4 * c) = v;
   }
 }
 
-// Per-head output projection o[b,h] = Lin_uv[h](oc[b,h]) straight into the
-// limb planes of the W_o GEMM operand.  oc: [B, H, r]; W_uv: [H * dv, r].
-// grid = (H, B), block 128.
-__global__ void k_mla_out(const int64_t* __restrict__ oc, int H, int r, int dv, const int8_t* __restrict__ Wuv,
-                          const int64_t* __restrict__ suv, int B, int8_t* __restrict__ X, int* __restrict__ lmax,
-                          int64_t* __restrict__ o_out) {
+__device__ __forceinline__ void hl_stage_x(const int64_t* __restrict__ x, size_t ld_b, size_t ld_h, int h, int Kd,
+                                           int b0, int nb, int64_t* qs) {
+  const size_t qst = hl_qstride(Kd);
+  for (int idx = threadIdx.x; idx < nb * Kd; idx += blockDim.x) {
+    const int sl = idx / Kd, e = idx - sl * Kd;
+    qs[sl * qst + e] = x[(size_t)(b0 + sl) * ld_b + (size_t)h * ld_h + e];
+  }
+}
+
+__device__ __forceinline__ uint64_t hl_dot(const uint8_t* wrow, const int64_t* qv, int Kd) {
+  uint64_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+  const uint32_t* w4 = (const uint32_t*)wrow;
+#pragma unroll 4
+  for (int c = 0; c < (Kd >> 2); ++c) {
+    const uint32_t w = w4[c];
+    const longlong2 q01 = *(const longlong2*)(qv + 4 * c);
+    const longlong2 q23 = *(const longlong2*)(qv + 4 * c + 2);
+    a0 += (uint64_t)(int64_t)(int8_t)(w & 0xFF) * (uint64_t)q01.x;
+    a1 += (uint64_t)(int64_t)(int8_t)((w >> 8) & 0xFF) * (uint64_t)q01.y;
+    a2 += (uint64_t)(int64_t)(int8_t)((w >> 16) & 0xFF) * (uint64_t)q23.x;
+    a3 += (uint64_t)(int64_t)(int8_t)(w >> 24) * (uint64_t)q23.y;
+  }
+  return a0 + a1 + a2 + a3;
+}
+
+// Absorbed query: Q[b, h] = [Lin_uk[h](q_nope[b, h]) | RoPE(q_rope[b, h])].
+// q: [B, H, dn + dr]; W_uk: [H * r, dn] int8, scales [H * r]; Q: [B, H, r + dr].
+// grid = (H, ceil(r / RB)); blocks with blockIdx.y == 0 also rotate q_rope.
+__global__ void __launch_bounds__(HL_THREADS) k_mla_q(const int64_t* __restrict__ q, int H, int dn, int dr, int r,
+                                                      const int8_t* __restrict__ Wuk, const int64_t* __restrict__ suk,
+                                                      const int* __restrict__ pos, const int64_t* __restrict__ rcos,
+                                                      const int64_t* __restrict__ rsin, int max_seq, int B,
+                                                      int64_t* __restrict__ Q) {
+  extern __shared__ __align__(16) int64_t hl_sm[];
+  int64_t* qs = hl_sm;
+  uint8_t* ws = (uint8_t*)(hl_sm + HL_SC * hl_qstride(dn));
+  const int h = blockIdx.x, r0 = blockIdx.y * HL_RB;
+  hl_stage_w(Wuk, h, r, dn, r0, ws);  // weights do not depend on the previous kernel
   pdl_wait_dep();
   pdl_allow_next();
-  extern __shared__ int64_t xs[];  // r values
+  const int row = threadIdx.x % HL_RB, sl = threadIdx.x / HL_RB, i = r0 + row;
+  const int64_t s = i < r ? suk[(size_t)h * r + i] : 0;
+  for (int b0 = 0; b0 < B; b0 += HL_SC) {
+    const int nb = min(HL_SC, B - b0);
+    __syncthreads();
+    hl_stage_x(q, (size_t)H * (dn + dr), dn + dr, h, dn, b0, nb, qs);
+    __syncthreads();
+    if (sl < nb && i < r) {
+      const uint64_t acc = hl_dot(ws + row * hl_wstride(dn), qs + sl * hl_qstride(dn), dn);
+      Q[((size_t)(b0 + sl) * H + h) * (r + dr) + i] = mulshr((int64_t)acc, s);
+    }
+  }
+  if (blockIdx.y == 0) {
+    const int half = dr / 2;
+    for (int idx = threadIdx.x; idx < B * half; idx += blockDim.x) {
+      const int b = idx / half, j = idx - b * half;
+      const int p = min(max(pos[b], 0), max_seq - 1);
+      const int64_t* qh = q + ((size_t)b * H + h) * (dn + dr);
+      int64_t x0 = qh[dn + j], x1 = qh[dn + j + half];
+      rope_pair(x0, x1, rcos[(size_t)p * half + j], rsin[(size_t)p * half + j]);
+      int64_t* out = Q + ((size_t)b * H + h) * (r + dr);
+      out[r + j] = x0;
+      out[r + j + half] = x1;
+    }
+  }
+}
+
+// Per-head output projection o[b, h] = Lin_uv[h](oc[b, h]) straight into the
+// limb planes of the W_o GEMM operand (and o_out when given).
+// oc: [B, H, r]; W_uv: [H * dv, r].  grid = (H, ceil(dv / RB)).
+__global__ void __launch_bounds__(HL_THREADS) k_mla_out(const int64_t* __restrict__ oc, int H, int r, int dv,
+                                                        const int8_t* __restrict__ Wuv,
+                                                        const int64_t* __restrict__ suv, int B,
+                                                        int8_t* __restrict__ X, int* __restrict__ lmax,
+                                                        int64_t* __restrict__ o_out) {
+  extern __shared__ __align__(16) int64_t hl_sm[];
   __shared__ int need_s;
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int64_t* x = oc + ((size_t)b * H + h) * r;
-  for (int e = threadIdx.x; e < r; e += blockDim.x) xs[e] = x[e];
+  int64_t* qs = hl_sm;
+  uint8_t* ws = (uint8_t*)(hl_sm + HL_SC * hl_qstride(r));
+  const int h = blockIdx.x, r0 = blockIdx.y * HL_RB;
+  hl_stage_w(Wuv, h, dv, r, r0, ws);
   if (threadIdx.x == 0) need_s = 0;
-  __syncthreads();
+  pdl_wait_dep();
+  pdl_allow_next();
+  const int row = threadIdx.x % HL_RB, sl = threadIdx.x / HL_RB, i = r0 + row;
+  const int64_t s = i < dv ? suv[(size_t)h * dv + i] : 0;
   const int d_out = H * dv;
   int need = 0;
-  for (int i = threadIdx.x; i < dv; i += blockDim.x) {
-    const int8_t* wr = Wuv + ((size_t)h * dv + i) * r;
-    uint64_t acc = 0;
-    for (int e = 0; e < r; ++e) acc += (uint64_t)(int64_t)wr[e] * (uint64_t)xs[e];
-    const int64_t v = mulshr((int64_t)acc, suv[(size_t)h * dv + i]);
-    const size_t off = (size_t)b * d_out + h * dv + i;
-    if (o_out) o_out[off] = v;
-    int8_t dg[8];
-    const int n = limb_split8(v, dg);
-    need = n > need ? n : need;
+  for (int b0 = 0; b0 < B; b0 += HL_SC) {
+    const int nb = min(HL_SC, B - b0);
+    __syncthreads();
+    hl_stage_x(oc, (size_t)H * r, r, h, r, b0, nb, qs);
+    __syncthreads();
+    if (sl < nb && i < dv) {
+      const uint64_t acc = hl_dot(ws + row * hl_wstride(r), qs + sl * hl_qstride(r), r);
+      const int64_t v = mulshr((int64_t)acc, s);
+      const size_t off = (size_t)(b0 + sl) * d_out + (size_t)h * dv + i;
+      if (o_out) o_out[off] = v;
+      int8_t dg[8];
+      const int n = limb_split8(v, dg);
+      need = n > need ? n : need;
 #pragma unroll
-    for (int l = 0; l < 8; ++l) X[(size_t)l * B * d_out + off] = dg[l];
+      for (int l = 0; l < 8; ++l) X[(size_t)l * B * d_out + off] = dg[l];
+    }
   }
   need = __reduce_max_sync(0xffffffffu, need);
   if ((threadIdx.x & 31) == 0 && need) atomicMax(&need_s, need);
@@ -140,39 +213,67 @@ __global__ void k_mla_out(const int64_t* __restrict__ oc, int H, int r, int dv, 
 
 // MoE routing of one slot: p = softmax_i64(logits[b, :E]); the top_k experts
 // by (p desc, index asc) get weight p_e, the others 0; the S shared experts
-// (columns E..E+S-1) get ONE.  route: [B, E + S] int64.  grid = B, block 32.
+// (columns E..E+S-1) get ONE.  route: [B, E + S] int64.  One warp per slot,
+// lane l owning experts l, l + 32, ...: the max is exact, the wrapping sum is
+// order-free, and each top-k round is a warp argmax on (p, -index).
+// grid = B, block 32.
 __global__ void k_moe_route(const int64_t* __restrict__ logits, int ldl, int E, int S, int top_k,
                             int64_t* __restrict__ route) {
   pdl_wait_dep();
   pdl_allow_next();
-  const int b = blockIdx.x;
-  if (threadIdx.x != 0) return;
+  const int b = blockIdx.x, lane = threadIdx.x;
   const int64_t* z = logits + (size_t)b * ldl;
   int64_t* out = route + (size_t)b * (E + S);
   const int64_t* lut = g_exp_lut.v;
-  int64_t p[256];
+  constexpr int PER = 8;  // E <= 256
+  int64_t p[PER];
   if (E == 1) {
     p[0] = ONE;
   } else {
-    int64_t m = z[0];
-    for (int e = 1; e < E; ++e) m = z[e] > m ? z[e] : m;
-    int64_t s = 0;
-    for (int e = 0; e < E; ++e) {
-      p[e] = integer_exp(wsub(z[e], m), lut);
-      s = wadd(s, p[e]);
+    int64_t m = LLONG_MIN;
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+      if (lane + 32 * j < E) m = max(m, z[lane + 32 * j]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = max(m, (int64_t)__shfl_xor_sync(0xffffffffu, (long long)m, o));
+    uint64_t su = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int e = lane + 32 * j;
+      p[j] = e < E ? integer_exp(wsub(z[e], m), lut) : 0;
+      su += (uint64_t)p[j];
     }
-    for (int e = 0; e < E; ++e) p[e] = s == 0 ? ONE / E : wmul(p[e], ONE) / s;
+    const int64_t sum = (int64_t)warp_sum_u64(su);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) p[j] = sum == 0 ? ONE / E : wmul(p[j], ONE) / sum;
   }
-  uint32_t taken[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int e = 0; e < E + S; ++e) out[e] = e < E ? 0 : ONE;
+  for (int e = lane; e < E + S; e += 32) out[e] = e < E ? 0 : ONE;
+  __syncwarp();
+  uint32_t taken = 0;  // bit j: expert lane + 32 j already chosen
   for (int t = 0; t < top_k && t < E; ++t) {
-    int best = -1;
-    for (int e = 0; e < E; ++e) {
-      if (taken[e >> 5] & (1u << (e & 31))) continue;
-      if (best < 0 || p[e] > p[best]) best = e;
+    int64_t bv = LLONG_MIN;
+    int be = INT_MAX;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !(taken & (1u << j)) && (p[j] > bv || (p[j] == bv && e < be))) {
+        bv = p[j];
+        be = e;
+      }
     }
-    taken[best >> 5] |= 1u << (best & 31);
-    out[best] = p[best];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const int64_t ov = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    if ((be & 31) == lane) {
+      taken |= 1u << (be >> 5);
+      out[be] = bv;
+    }
   }
 }
 
@@ -187,16 +288,29 @@ int arcb_mla_kv(const int64_t* kva, int r, int dr, const int64_t* gamma, int nga
                   pos, rcos, rsin, max_seq, err);
 }
 
+static int hl_attr(const void* k, size_t smem) {
+  if (smem <= 48 * 1024) return 0;
+  return (int)cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
 int arcb_mla_q(const int64_t* q, int H, int dn, int dr, int r, const int8_t* Wuk, const int64_t* suk, const int* pos,
                const int64_t* rcos, const int64_t* rsin, int max_seq, int B, int64_t* Q, void* st) {
-  return launch_k(k_mla_q, dim3(H, B), dim3(256), (size_t)dn * 8, (cudaStream_t)st, q, H, dn, dr, r, Wuk, suk, pos,
-                  rcos, rsin, max_seq, Q);
+  if ((dn & 3) || (dr & 1)) return -1;
+  const size_t sm = hl_smem(dn);
+  if (sm > 227 * 1024) return -2;
+  if (int e = hl_attr((const void*)k_mla_q, sm)) return e;
+  return launch_k(k_mla_q, dim3(H, (r + HL_RB - 1) / HL_RB), dim3(HL_THREADS), sm, (cudaStream_t)st, q, H, dn, dr, r,
+                  Wuk, suk, pos, rcos, rsin, max_seq, B, Q);
 }
 
 int arcb_mla_out(const int64_t* oc, int H, int r, int dv, const int8_t* Wuv, const int64_t* suv, int B, int8_t* X,
                  int* lmax, int64_t* o_out, void* st) {
-  return launch_k(k_mla_out, dim3(H, B), dim3(128), (size_t)r * 8, (cudaStream_t)st, oc, H, r, dv, Wuv, suv, B, X,
-                  lmax, o_out);
+  if (r & 3) return -1;
+  const size_t sm = hl_smem(r);
+  if (sm > 227 * 1024) return -2;
+  if (int e = hl_attr((const void*)k_mla_out, sm)) return e;
+  return launch_k(k_mla_out, dim3(H, (dv + HL_RB - 1) / HL_RB), dim3(HL_THREADS), sm, (cudaStream_t)st, oc, H, r, dv,
+                  Wuv, suv, B, X, lmax, o_out);
 }
 
 int arcb_moe_route(const int64_t* logits, int ldl, int E, int S, int top_k, int B, int64_t* route, void* st) {
