@@ -135,9 +135,175 @@ __global__ void k_parents(const uint32_t* __restrict__ cvs, int64_t n_pairs, uin
   for (int k = 0; k < 8; ++k) out[i * 8 + k] = cv[k];
 }
 
+// ---------------------------------------------------------------- batch commitments
+// One thread per item: derive_key(context, [domain_i] ++ item_i), where the
+// context key (the material hasher's key words) is derived on the host.
+// Items are byte ranges [offs[i], offs[i+1]) of one buffer of `nwords` 32-bit
+// words (the host pads it to a multiple of 16 bytes); a word straddling two
+// aligned words is assembled with a funnel shift.  Items of more than one
+// chunk keep the chaining-value stack in local memory (depth MAXD: items up
+// to 2^MAXD KiB).
+constexpr uint32_t ROOT_F = 8u, DKM = 64u;
+constexpr int MAXD = 20;
+
+struct Key8 {
+  uint32_t w[8];
+};
+
+__device__ __forceinline__ uint32_t item_word(const uint32_t* __restrict__ buf, int64_t nwords, int64_t start,
+                                              int dom, uint32_t dbyte, int64_t vlen, int64_t vpos) {
+  if (vpos >= vlen) return 0;
+  uint32_t w;
+  if (dom && vpos == 0) {
+    // the domain byte, then the first three data bytes
+    w = dbyte;
+    for (int j = 1; j < 4; ++j) {
+      if (j >= vlen) break;
+      const int64_t a = start + j - 1;
+      w |= ((buf[a >> 2] >> (8 * (a & 3))) & 0xFFu) << (8 * j);
+    }
+    return w;
+  }
+  const int64_t a = start + vpos - dom;
+  const int64_t aw = a >> 2;
+  const int sh = (int)(a & 3) * 8;
+  const uint32_t w0 = __ldg(buf + aw);
+  const uint32_t w1 = (sh && aw + 1 < nwords) ? __ldg(buf + aw + 1) : 0u;
+  w = sh ? __funnelshift_r(w0, w1, sh) : w0;
+  const int64_t rem = vlen - vpos;
+  if (rem < 4) w &= 0xFFFFFFFFu >> (8 * (4 - (int)rem));
+  return w;
+}
+
+__global__ void k_batch_commit(const uint32_t* __restrict__ buf, int64_t nwords, const int64_t* __restrict__ offs,
+                               int64_t n, const uint8_t* __restrict__ domains, Key8 key, uint32_t* __restrict__ out) {
+  pdl_wait_dep();
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int64_t start = offs[i], len = offs[i + 1] - start;
+  const int dom = domains ? 1 : 0;
+  const uint32_t dbyte = domains ? domains[i] : 0u;
+  const int64_t vlen = len + dom;
+  const int64_t nch = vlen == 0 ? 1 : (vlen + 1023) / 1024;
+  uint32_t stack[MAXD][8];
+  int sp = 0;
+  uint32_t cv[8];
+  for (int64_t c = 0; c < nch; ++c) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cv[k] = key.w[k];
+    const int64_t clen = min((int64_t)1024, vlen - c * 1024);
+    const int nb = clen <= 0 ? 1 : (int)((clen + 63) / 64);
+    for (int blk = 0; blk < nb; ++blk) {
+      const int64_t v0 = c * 1024 + blk * 64;
+      uint32_t m[16];
+#pragma unroll
+      for (int w = 0; w < 16; ++w) m[w] = item_word(buf, nwords, start, dom, dbyte, vlen, v0 + 4 * w);
+      const uint32_t blen = (uint32_t)max((int64_t)0, min((int64_t)64, clen - blk * 64));
+      uint32_t f = DKM | (blk == 0 ? CHUNK_START : 0u) | (blk == nb - 1 ? CHUNK_END : 0u);
+      if (nch == 1 && blk == nb - 1) f |= ROOT_F;
+      compress_cv(cv, m, (uint64_t)c, blen, f);
+    }
+    if (c + 1 < nch) {
+      // merge completed subtrees: one parent per trailing zero bit of the count
+      uint64_t t = (uint64_t)c + 1;
+      while ((t & 1) == 0 && sp > 0) {
+        uint32_t pm[16];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          pm[k] = stack[sp - 1][k];
+          pm[8 + k] = cv[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) cv[k] = key.w[k];
+        compress_cv(cv, pm, 0, 64, DKM | PARENT);
+        --sp;
+        t >>= 1;
+      }
+      if (sp >= MAXD) return;  // unreachable: the host bounds the item length
+#pragma unroll
+      for (int k = 0; k < 8; ++k) stack[sp][k] = cv[k];
+      ++sp;
+    }
+  }
+  for (int j = sp - 1; j >= 0; --j) {
+    uint32_t pm[16];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      pm[k] = stack[j][k];
+      pm[8 + k] = cv[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cv[k] = key.w[k];
+    compress_cv(cv, pm, 0, 64, DKM | PARENT | (j == 0 ? ROOT_F : 0u));
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) out[i * 8 + k] = cv[k];
+}
+
+// One Merkle layer: out[i] = commit(in[2i] ++ in[2i+1]), in[n_in] = zero hash.
+__global__ void k_merkle_layer(const uint32_t* __restrict__ in, int64_t n_in, Key8 key, uint32_t* __restrict__ out) {
+  pdl_wait_dep();
+  pdl_allow_next();
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= (n_in + 1) / 2) return;
+  uint32_t m[16], cv[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    m[k] = in[(2 * i) * 8 + k];
+    m[8 + k] = 2 * i + 1 < n_in ? in[(2 * i + 1) * 8 + k] : 0u;
+    cv[k] = key.w[k];
+  }
+  compress_cv(cv, m, 0, 64, DKM | CHUNK_START | CHUNK_END | ROOT_F);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) out[i * 8 + k] = cv[k];
+}
+
 }  // namespace
 
 extern "C" {
+
+// Batch commitments of n items (see k_batch_commit).  buf: 4-byte aligned,
+// nbytes a multiple of 4 and >= offs[n]; domains: n bytes or null; key8: the
+// derive_key context key words; out: n x 32 bytes.  Items longer than
+// 2^MAXD KiB are refused (-2).
+int arcb_blake3_batch_commit(const void* buf, int64_t nbytes, const int64_t* offs, int64_t n, const uint8_t* domains,
+                             const uint32_t* key8, int64_t max_item_len, uint32_t* out, void* stream) {
+  if (n <= 0) return 0;
+  if (((uintptr_t)buf & 3) || (nbytes & 3)) return -1;
+  if (max_item_len + 1 > ((int64_t)1024 << MAXD)) return -2;
+  Key8 k;
+  for (int j = 0; j < 8; ++j) k.w[j] = key8[j];
+  const int64_t blocks = (n + 127) / 128;
+  return launch_k(k_batch_commit, dim3((unsigned)blocks), dim3(128), 0, (cudaStream_t)stream, (const uint32_t*)buf,
+                  nbytes / 4, offs, n, domains, k, out);
+}
+
+// Merkle root of n 32-byte leaves into out (8 words).  scratch: at least
+// 2 * 32 * ((n + 1) / 2) bytes, used as two ping-pong layers.
+int arcb_merkle_root(const uint32_t* leaves, int64_t n, const uint32_t* key8, uint32_t* scratch, uint32_t* out,
+                     void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (n <= 0) return (int)cudaMemsetAsync(out, 0, 32, st);
+  if (n == 1) return (int)cudaMemcpyAsync(out, leaves, 32, cudaMemcpyDeviceToDevice, st);
+  Key8 k;
+  for (int j = 0; j < 8; ++j) k.w[j] = key8[j];
+  const int64_t half = (n + 1) / 2;
+  uint32_t* bufs[2] = {scratch, scratch + 8 * half};
+  const uint32_t* cur = leaves;
+  int64_t m = n;
+  int side = 0;
+  while (m > 1) {
+    const int64_t mo = (m + 1) / 2;
+    uint32_t* dst = mo == 1 ? out : bufs[side];
+    const int64_t blocks = (mo + 127) / 128;
+    const int e = launch_k(k_merkle_layer, dim3((unsigned)blocks), dim3(128), 0, st, cur, m, k, dst);
+    if (e) return e;
+    cur = dst;
+    side ^= 1;
+    m = mo;
+  }
+  return 0;
+}
 
 // chunk_base: index of the first chunk in the whole stream (the chunk
 // counter input of BLAKE3's compression).

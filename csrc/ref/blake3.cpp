@@ -1,4 +1,4 @@
-// BLAKE3 hash mode, from the specification.  See blake3.h.
+// BLAKE3 hash, keyed-hash and derive-key modes, from the specification.  See blake3.h.
 #include "blake3.h"
 
 #include <string.h>
@@ -54,8 +54,8 @@ static inline void load_block(const uint8_t* b, uint32_t w[16]) {
            ((uint32_t)b[4 * i + 2] << 16) | ((uint32_t)b[4 * i + 3] << 24);
 }
 
-static void parent_cv(const uint32_t key[8], const uint32_t l[8], const uint32_t r[8],
-                      uint32_t flags, uint32_t out8[8]) {
+static void parent_cv(const uint32_t key[8], const uint32_t l[8], const uint32_t r[8], uint32_t flags,
+                      uint32_t out8[8]) {
   uint32_t blk[16], o[16];
   memcpy(blk, l, 32);
   memcpy(blk + 8, r, 32);
@@ -64,6 +64,7 @@ static void parent_cv(const uint32_t key[8], const uint32_t l[8], const uint32_t
 }
 
 void Hasher::init() {
+  mode = 0;
   memcpy(key, IV, 32);
   memcpy(cv, IV, 32);
   chunk_counter = 0;
@@ -73,12 +74,42 @@ void Hasher::init() {
   memset(block, 0, 64);
 }
 
+void Hasher::init_keyed(const uint8_t key32[32]) {
+  init();
+  for (int i = 0; i < 8; ++i)
+    key[i] = (uint32_t)key32[4 * i] | ((uint32_t)key32[4 * i + 1] << 8) | ((uint32_t)key32[4 * i + 2] << 16) |
+             ((uint32_t)key32[4 * i + 3] << 24);
+  memcpy(cv, key, 32);
+  mode = KEYED_HASH;
+}
+
+void derive_context_key(const char* context, size_t len, uint32_t key_out[8]) {
+  Hasher h;
+  h.init();
+  h.mode = DERIVE_KEY_CONTEXT;
+  h.update(context, len);
+  uint8_t k[32];
+  h.finalize(k);
+  for (int i = 0; i < 8; ++i)
+    key_out[i] = (uint32_t)k[4 * i] | ((uint32_t)k[4 * i + 1] << 8) | ((uint32_t)k[4 * i + 2] << 16) |
+                 ((uint32_t)k[4 * i + 3] << 24);
+}
+
+void Hasher::init_derive_key(const char* context, size_t len) {
+  uint32_t k[8];
+  derive_context_key(context, len, k);
+  init();
+  memcpy(key, k, 32);
+  memcpy(cv, k, 32);
+  mode = DERIVE_KEY_MATERIAL;
+}
+
 void Hasher::push_chunk_cv(const uint32_t cv_in[8], uint64_t total_chunks) {
   uint32_t c[8];
   memcpy(c, cv_in, 32);
   while ((total_chunks & 1) == 0) {
     --stack_len;
-    parent_cv(key, stack[stack_len], c, 0, c);
+    parent_cv(key, stack[stack_len], c, mode, c);
     total_chunks >>= 1;
   }
   memcpy(stack[stack_len++], c, 32);
@@ -90,7 +121,7 @@ void Hasher::push_subtree_cv(const uint32_t cv_in[8], int level, uint64_t total_
   uint64_t t = total_chunks >> level;
   while ((t & 1) == 0) {
     --stack_len;
-    parent_cv(key, stack[stack_len], c, 0, c);
+    parent_cv(key, stack[stack_len], c, mode, c);
     t >>= 1;
   }
   memcpy(stack[stack_len++], c, 32);
@@ -105,7 +136,7 @@ void Hasher::update(const void* data, size_t len) {
     if (blocks_compressed * BLOCK_LEN + block_len == CHUNK_LEN) {
       uint32_t w[16], o[16];
       load_block(block, w);
-      uint32_t flags = CHUNK_END | (blocks_compressed == 0 ? CHUNK_START : 0);
+      uint32_t flags = mode | CHUNK_END | (blocks_compressed == 0 ? CHUNK_START : 0);
       compress(cv, w, chunk_counter, block_len, flags, o);
       ++chunk_counter;
       push_chunk_cv(o, chunk_counter);
@@ -117,7 +148,7 @@ void Hasher::update(const void* data, size_t len) {
     if (block_len == BLOCK_LEN) {
       uint32_t w[16], o[16];
       load_block(block, w);
-      uint32_t flags = blocks_compressed == 0 ? CHUNK_START : 0;
+      uint32_t flags = mode | (blocks_compressed == 0 ? CHUNK_START : 0);
       compress(cv, w, chunk_counter, 64, flags, o);
       memcpy(cv, o, 32);
       ++blocks_compressed;
@@ -139,7 +170,7 @@ void Hasher::finalize(uint8_t out[32]) const {
   memset(blk, 0, 64);
   memcpy(blk, block, block_len);
   load_block(blk, w);
-  uint32_t flags = CHUNK_END | (blocks_compressed == 0 ? CHUNK_START : 0);
+  uint32_t flags = mode | CHUNK_END | (blocks_compressed == 0 ? CHUNK_START : 0);
   uint32_t res[8];
   if (stack_len == 0) {
     compress(cv, w, chunk_counter, block_len, flags | ROOT, o);
@@ -149,7 +180,7 @@ void Hasher::finalize(uint8_t out[32]) const {
     uint32_t c[8];
     memcpy(c, o, 32);
     for (int i = stack_len - 1; i >= 0; --i)
-      parent_cv(key, stack[i], c, i == 0 ? ROOT : 0, c);
+      parent_cv(key, stack[i], c, mode | (i == 0 ? ROOT : 0), c);
     memcpy(res, c, 32);
   }
   for (int i = 0; i < 8; ++i) {

@@ -1,0 +1,63 @@
+"""Worker of tests/test_gpu_ep.py: one rank of an expert-parallel MLA + MoE
+run, launched by torch.distributed.run (one process per GPU).  Every rank
+checks its tokens against the numpy oracle and rank 0 prints one JSON line."""
+import argparse
+import gc
+import json
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
+    a = ap.parse_args()
+    import torch
+    import torch.distributed as dist
+
+    from arc_chain_b200.formats import gen
+    from arc_chain_b200.models import mla_moe, mla_moe_engine as me
+    from arc_chain_b200.models.config import preset
+    from arc_chain_b200.parallel import tp
+    from arc_chain_b200.parallel.ep import EpFusedComm, EpNcclComm
+    from arc_chain_b200.runtime.scheduler import Scheduler
+
+    rank, world = tp.init_distributed(timeout_s=60)
+    cfg = preset("micro_moe")
+    host = gen.random_model(cfg, 4)
+    orc = mla_moe.MlaMoeOracle
+    comm = (EpFusedComm if a.comm == "fused" else EpNcclComm)()
+    eng = me.MlaMoeEngine(me.from_host(host, "cuda", rank, world), comm=comm)
+    res = {"comm": a.comm, "world": world, "ok": True, "checks": 0}
+    prompt = gen.seeded_prompt(9, cfg.vocab, 3)
+    ref, rh = orc(host).generate(prompt, 12)
+    for use_graph in (False, True):
+        got, gh = eng.generate(prompt, 12, use_graph=use_graph)
+        res["ok"] &= got == ref and gh == rh
+        res["checks"] += 1
+    sch = Scheduler(eng, max_batch=8, prefill_chunk=16, gen_cap=10)
+    specs = [(gen.seeded_prompt(3 + 2 * i, cfg.vocab, 90 + i), 5 + (i % 4)) for i in range(10)]
+    rids = [sch.submit(p, n) for p, n in specs]
+    sch.run()
+    for rid, (p, n) in zip(rids, specs):
+        res["ok"] &= sch.requests[rid].tokens == orc(host).generate(p, n)[0]
+        res["checks"] += 1
+    res["kernel_errors"] = eng.check_errors()
+    res["ok"] &= res["kernel_errors"] == 0
+    flag = torch.tensor([0 if res["ok"] else 1], device="cuda")
+    dist.all_reduce(flag)
+    res["ok_all_ranks"] = int(flag.item()) == 0
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    eng._graphs.clear()
+    gc.collect()
+    torch.cuda.synchronize()
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if res["ok_all_ranks"] else 1)
+
+
+if __name__ == "__main__":
+    main()
