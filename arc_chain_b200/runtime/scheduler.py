@@ -17,10 +17,19 @@ in the reference), then the lane starts decoding with the last prompt token
 fed again at position n + 1.  A request finishes on an EOS id (kept in the
 output) or after ``max_tokens`` tokens; its output hash is BLAKE3 of the LE
 u32 ids, as the reference computes it.
+
+Resume and recovery are exact.  A request that has produced g tokens is
+rebuilt by prefilling BOS + prompt + [last prompt token] + its first g - 1
+tokens (exactly the positions its decode steps wrote) and restoring the
+penalty history and count, so it continues as if never interrupted.
+``snapshot`` / ``from_snapshot`` persist and restore serving state this way
+(the KV cache itself is never saved), and a decode step whose kernels raised
+an error bit requeues every active request without that step's tokens.
 """
 from __future__ import annotations
 
 import collections
+import json
 import time
 from dataclasses import dataclass, field
 from typing import Deque, Dict, List, Optional, Sequence
@@ -43,6 +52,7 @@ class Request:
     t_submit: float = 0.0
     t_first: float = 0.0
     t_done: float = 0.0
+    resume: List[int] = field(default_factory=list)  # tokens already produced (resumed requests)
 
     @property
     def done(self) -> bool:
@@ -67,6 +77,8 @@ class Scheduler:
         self.steps = 0
         self.tokens_out = 0
         self.metrics: List[dict] = []
+        self.recoveries = 0
+        self.max_recoveries = 3
 
     # ------------------------------------------------------------ lanes
     def _init_lanes(self):
@@ -85,11 +97,21 @@ class Scheduler:
     def _open_lane(self, lane: int, r: Request):
         bb = self.bb
         n = len(r.prompt)
+        g = len(r.resume)
         bb.pt[lane].copy_(torch.tensor(self.e.kv.table_row(r.rid), dtype=I32))
-        bb.tokens[lane] = r.prompt[-1] if n else 0
-        bb.pos[lane] = n + 1
         bb.hist[lane].zero_()
-        bb.count[lane] = 0
+        if g:
+            bb.tokens[lane] = r.resume[-1]
+            bb.pos[lane] = n + g + 1
+            hist = torch.zeros(64, dtype=I32)
+            for j in range(max(0, g - 64), g):
+                hist[j & 63] = r.resume[j]
+            bb.hist[lane].copy_(hist)
+            bb.gen[lane, :g].copy_(torch.tensor(r.resume, dtype=I32))
+        else:
+            bb.tokens[lane] = r.prompt[-1] if n else 0
+            bb.pos[lane] = n + 1
+        bb.count[lane] = g
         bb.done[lane] = 0
         r.lane = lane
         self.lanes[lane] = r
@@ -124,7 +146,10 @@ class Scheduler:
                 break
             self.waiting.popleft()
             self.e.kv.reserve(r.rid, need)
-            self.e.prefill(r.rid, [1] + r.prompt, chunk=self.prefill_chunk)
+            toks = [1] + r.prompt
+            if r.resume:
+                toks += [r.prompt[-1] if r.prompt else 0] + r.resume[:-1]
+            self.e.prefill(r.rid, toks, chunk=self.prefill_chunk)
             self._open_lane(lane, r)
             admitted += 1
         return admitted
@@ -135,11 +160,15 @@ class Scheduler:
         active = sum(1 for x in self.lanes if x is not None)
         if active == 0:
             return 0
+        before = self.bb.count.cpu().numpy().copy()
         if self.use_graph:
             self.e._graph_for(self.bb).replay()
         else:
             self.e.decode_step(self.bb)
         self.steps += 1
+        if int(self.bb.err.item()) != 0:
+            self._recover(before)
+            return active
         cnt = self.bb.count.cpu().numpy()
         done = self.bb.done.cpu().numpy()
         for lane, r in enumerate(self.lanes):
@@ -158,6 +187,65 @@ class Scheduler:
         r.t_done = time.perf_counter()
         self.e.kv.release(r.rid)
         self._close_lane(lane)
+
+    # ------------------------------------------------------------ recovery and resume
+    def _recover(self, counts_before) -> None:
+        """A step raised a kernel error bit: requeue every active request with
+        the tokens it had before that step, then clear the error."""
+        torch.cuda.synchronize()
+        if self.recoveries >= self.max_recoveries:
+            raise RuntimeError(f"decode step failed again after {self.recoveries} recoveries "
+                               f"(error bits {int(self.bb.err.item()):#x})")
+        gen = self.bb.gen.cpu()
+        requeue = []
+        for lane, r in enumerate(self.lanes):
+            if r is None:
+                continue
+            g = int(min(counts_before[lane], r.max_tokens))
+            r.resume = [int(t) for t in gen[lane, :g].tolist()]
+            self.e.kv.release(r.rid)
+            self._close_lane(lane)
+            requeue.append(r)
+        for r in reversed(requeue):
+            self.waiting.appendleft(r)
+        for bb in self.e._bufs.values():
+            bb.err.zero_()
+        self.recoveries += 1
+
+    def snapshot(self) -> str:
+        """Serving state as JSON (between steps): every request's prompt,
+        budget and tokens so far; finished requests keep their hash."""
+        cnt = self.bb.count.cpu().numpy()
+        gen = self.bb.gen.cpu()
+        reqs = []
+        for rid, r in sorted(self.requests.items()):
+            if r.done:
+                toks = r.tokens
+            elif r.lane >= 0 and self.lanes[r.lane] is r:
+                toks = [int(t) for t in gen[r.lane, :int(min(cnt[r.lane], r.max_tokens))].tolist()]
+            else:
+                toks = list(r.resume)
+            reqs.append({"rid": rid, "prompt": r.prompt, "max_tokens": r.max_tokens, "tokens": toks,
+                         "done": r.done, "output_hash": r.output_hash.hex() if r.done else None})
+        return json.dumps({"version": 1, "eos": self.eos, "requests": reqs})
+
+    @classmethod
+    def from_snapshot(cls, engine: Engine, snap: str, max_batch: int = 32, prefill_chunk: int = 1024,
+                      gen_cap: Optional[int] = None, use_graph: bool = True) -> "Scheduler":
+        d = json.loads(snap)
+        sch = cls(engine, max_batch, prefill_chunk, eos=d["eos"], gen_cap=gen_cap, use_graph=use_graph)
+        for q in d["requests"]:
+            rid = engine._rid
+            engine._rid += 1
+            r = Request(rid, list(q["prompt"]), int(q["max_tokens"]), t_submit=time.perf_counter())
+            if q["done"]:
+                r.tokens = list(q["tokens"])
+                r.output_hash = bytes.fromhex(q["output_hash"])
+            else:
+                r.resume = list(q["tokens"])
+                sch.waiting.append(r)
+            sch.requests[rid] = r
+        return sch
 
     def run(self, max_steps: Optional[int] = None) -> Dict[int, Request]:
         s = 0
