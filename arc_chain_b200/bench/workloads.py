@@ -76,15 +76,16 @@ def batched(model: str, n_requests: int, rank: int, world: int, comm, max_batch:
                        "out_len": list(out_range)}}
 
 
-def moe_decode(model: str, batch: int, prompt_len: int, gen_len: int, steps: int, warmup: int) -> dict:
-    """MLA + MoE batched greedy decode (single GPU)."""
+def moe_decode(model: str, batch: int, prompt_len: int, gen_len: int, steps: int, warmup: int, rank: int = 0,
+               world: int = 1, comm=None) -> dict:
+    """MLA + MoE batched greedy decode; expert-parallel over `world` ranks
+    (weights generated on each device, experts g % world == rank)."""
     from arc_chain_b200.models import mla_moe_engine as me
 
     cfg = preset(model)
     cfg.max_seq = (prompt_len + gen_len + 2 + 15) // 16 * 16
-    host = gen.random_model(cfg, 0)
-    eng = me.MlaMoeEngine(me.from_host(host, "cuda"), n_pages=batch * ((cfg.max_seq + 15) // 16) + 4)
-    del host
+    m = me.random_device(cfg, torch.device("cuda", torch.cuda.current_device()), 0, rank, world)
+    eng = me.MlaMoeEngine(m, n_pages=batch * ((cfg.max_seq + 15) // 16) + 4, comm=comm if world > 1 else None)
     bb = eng.buffers(batch, gen_cap=gen_len)
     rids = []
     for i in range(batch):
@@ -96,19 +97,23 @@ def moe_decode(model: str, batch: int, prompt_len: int, gen_len: int, steps: int
     g = eng._graph_for(bb)
     for _ in range(warmup):
         g.replay()
-    torch.cuda.synchronize()
+    _sync_barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = min(steps, gen_len - warmup)
     e0.record()
     for _ in range(n):
         g.replay()
     e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    _sync_barrier(world)
+    ms = _max_over_ranks(e0.elapsed_time(e1), world)
+    err = eng.check_errors()
+    g = None
+    eng._graphs.clear()
     return {"metric": f"{model} MLA+MoE INT8 batched decode tok/s", "value": round(batch * n / (ms / 1000), 2),
             "unit": "tokens/s", "higher_is_better": True, "ms_per_step": round(ms / n, 4), "batch": batch,
-            "steps": n, "warmup": warmup, "kernel_errors": eng.check_errors(),
-            "config": {"model": model, "prompt_len": prompt_len, "gen_len": gen_len, "parallelism": "ep1"}}
+            "steps": n, "warmup": warmup, "kernel_errors": err,
+            "config": {"model": model, "prompt_len": prompt_len, "gen_len": gen_len, "parallelism": f"ep{world}",
+                       "comm": getattr(comm, "__class__", type(None)).__name__ if world > 1 else "none"}}
 
 
 def spec_decode(target: str, draft: str, batch: int, prompt_len: int, gen_len: int, k: int, rank: int, world: int,

@@ -189,7 +189,8 @@ class Epi(C.Structure):
                 ("peer_lmax", C.c_void_p), ("cnt_local", C.c_void_p), ("lmax_fin", C.c_void_p), ("prof", C.c_void_p),
                 ("grp_rows", C.c_int), ("grp_koff", C.c_int), ("route", C.c_void_p), ("route_ld", C.c_int),
                 ("max_ctas", C.c_int), ("b_box", C.c_int), ("route_gs", C.c_int), ("peer_h", C.c_void_p),
-                ("peer_sig", C.c_void_p)]
+                ("peer_sig", C.c_void_p), ("pf_w", C.c_void_p), ("pf_M", C.c_int), ("pf_K", C.c_int),
+                ("pf_tiles", C.c_int)]
 
 
 PARTIAL, STORE, RESID, QKV, SWIGLU, MOE_COMBINE = 0, 1, 2, 3, 4, 5
@@ -391,3 +392,13 @@ def ep_wait_apply(cnt, epoch, per_call: int, h, delta, done, err) -> None:
     _count()
     check(lib().arcb_ep_wait_apply(_p(cnt), _p(epoch), per_call, _p(h), _p(delta), h.numel(), _p(done), _p(err),
                                    _s()), "ep_wait_apply")
+
+
+def set_prefetch(epi: Epi, next_lin, tiles: int) -> None:
+    """Points a fused GEMM's epilogue descriptor at the next GEMM's int8
+    weights (cross-GEMM L2 prefetch of its first `tiles` tiles per CTA)."""
+    if next_lin is None or getattr(next_lin, "w", None) is None or tiles <= 0:
+        epi.pf_w, epi.pf_tiles = None, 0
+        return
+    epi.pf_w = next_lin.w.data_ptr()
+    epi.pf_M, epi.pf_K, epi.pf_tiles = next_lin.M, next_lin.K, int(tiles)

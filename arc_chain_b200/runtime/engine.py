@@ -120,6 +120,8 @@ class Engine:
         self._bufs: Dict[Tuple[int, int], StepBuffers] = {}
         self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self._rid = 0
+        # weight tiles per CTA each fused GEMM prefetches into L2 for the next one
+        self.prefetch_tiles = 0
 
     # ------------------------------------------------------------------ buffers
     def buffers(self, B: int, gen_cap: int = 0) -> StepBuffers:
@@ -191,6 +193,14 @@ class Engine:
                 "partial": ops.epi(ops.PARTIAL, Ly.wo.s, bb.err),
             })
         out.append({"lm": ops.epi(ops.STORE, m.lm.s, bb.err, out=bb.logits_local, ldo=m.lm.M)})
+        # each GEMM prefetches the first weight tiles of the next one in the step
+        chain = []
+        for l, Ly in enumerate(m.layers):
+            chain += [(out[l]["qkv"], Ly.qkv), (out[l]["wo"], Ly.wo), (out[l]["gu"], Ly.gu),
+                      (out[l]["down"], Ly.down)]
+        chain.append((out[-1]["lm"], m.lm))
+        for (e, _), (_, nxt) in zip(chain, chain[1:]):
+            ops.set_prefetch(e, nxt, self.prefetch_tiles)
         bb.epis = out
         return out
 

@@ -64,6 +64,7 @@ def main():
                          "batching tok/s; moe: MLA+MoE batch-32 decode; specdec: Q4 target + INT8 draft")
     ap.add_argument("--requests", type=int, default=128)
     ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--prefetch", type=int, default=0, help="weight tiles per CTA each GEMM prefetches for the next")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -78,6 +79,8 @@ def main():
     from arc_chain_b200.ops import int_ops as ops
     from arc_chain_b200.runtime.engine import Engine
     from arc_chain_b200.utils.clocks import ClockSampler
+    from arc_chain_b200.utils.hashing import blake3
+    import numpy as np
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = 0
@@ -115,8 +118,13 @@ def main():
                 out = wl.batched(args.model if args.model != "llama7b" else "llama70b", args.requests, rank, world,
                                  comm or tp_comm_none())
             elif args.workload == "moe":
+                ep_comm = None
+                if world > 1:
+                    from arc_chain_b200.parallel.ep import EpFusedComm, EpNcclComm
+
+                    ep_comm = EpFusedComm() if args.comm == "fused" else EpNcclComm()
                 out = wl.moe_decode("dsv2lite", args.batch or 32, args.prompt_len if args.prompt_len != 128 else 512,
-                                    256, args.steps, args.warmup)
+                                    256, args.steps, args.warmup, rank, world, ep_comm)
             else:
                 out = wl.spec_decode("llama7b", "draft1b", args.batch or 8, 256, 256, 4, rank, world,
                                      comm or tp_comm_none())
@@ -143,6 +151,7 @@ def main():
     model = dense.random_device(cfg, dev, seed=0, tp_rank=rank, tp_size=world)
     log("weights ready")
     eng = Engine(model, max_seq=max_seq, comm=comm, n_pages=2 * ((max_seq + 15) // 16))
+    eng.prefetch_tiles = args.prefetch
     prompt = gen.seeded_prompt(args.prompt_len, cfg.vocab, 1)
 
     W, K, G = args.warmup, args.steps, args.gen_len
@@ -229,8 +238,11 @@ def main():
                        "global_batch": 1, "seq_len": args.prompt_len, "gen_len": G,
                        "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
                        "l2": "weights per GPU >> 126 MB L2 (streamed from HBM every step)",
+                       "prefetch_tiles": args.prefetch,
                        "tokens_per_s": round(1000.0 / ms_tok, 2)},
             "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches_per_step * K),
+            "first_sequence": {"tokens": len(tokens_first),
+                               "blake3": blake3(np.asarray(tokens_first, dtype="<u4").tobytes()).hex()},
             "kernel_errors": err, "impl": "b200",
         }
         print(json.dumps(out))

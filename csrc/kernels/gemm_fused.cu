@@ -108,6 +108,13 @@ struct Epi {
   int route_gs;
   int64_t* const* peer_h;
   unsigned long long* const* peer_sig;
+  // Cross-GEMM prefetch: once this CTA's producer has issued its last load,
+  // it asks L2 for the first pf_tiles weight tiles that the same CTA index
+  // will stream in the next GEMM (tiled int8 weights pf_w of [pf_M, pf_K],
+  // one N tile, the same grid), so HBM stays busy through this GEMM's tail
+  // and the next GEMM's first stages hit L2.  null = off.
+  const uint8_t* pf_w;
+  int pf_M, pf_K, pf_tiles;
 };
 
 // Ring depth for decode-sized tiles (BN <= 32).  A 5-stage ring (two CTAs
@@ -232,6 +239,52 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
     }
     default:
       break;
+  }
+}
+
+// Finalises row m of a split tile from the partial buffer P: reads and
+// clears its L x B int32 partials, recombines the limbs and applies the
+// epilogue.  Wide tiles (BN >= 64, i.e. batches of 8 or more) read 8 slots x
+// L limbs per round with every load in flight together; each load otherwise
+// waits for the previous clear, and a batch of 32 slots at 3 limbs would
+// serialise 96 L2 round trips.  Called by all lanes of a warp together.
+template <int BN>
+__device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int m, bool valid, int B, int L,
+                                                int& need) {
+  if (BN >= 64) {
+    constexpr int FS = 4;  // slots per round: 4 x L loads in flight, no spills
+    for (int b0 = 0; b0 < B; b0 += FS) {
+      int v[8][FS];
+#pragma unroll
+      for (int l = 0; l < 8; ++l)
+#pragma unroll
+        for (int j = 0; j < FS; ++j)
+          v[l][j] = (valid && l < L && b0 + j < B) ? __ldcg(P + (size_t)(l * B + b0 + j) * M + m) : 0;
+#pragma unroll
+      for (int l = 0; l < 8; ++l)
+#pragma unroll
+        for (int j = 0; j < FS; ++j)
+          if (valid && l < L && b0 + j < B) __stcg(P + (size_t)(l * B + b0 + j) * M + m, 0);
+#pragma unroll
+      for (int j = 0; j < FS; ++j) {
+        if (b0 + j >= B) break;
+        uint64_t acc = 0;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) acc += (uint64_t)(int64_t)v[l][j] << (8 * l);
+        apply_row(E, M, m, valid, b0 + j, acc, need);
+      }
+    }
+    return;
+  }
+  for (int b = 0; b < B; ++b) {
+    uint64_t acc = 0;
+    if (valid)
+      for (int l = 0; l < L; ++l) {
+        int* p = P + (size_t)(l * B + b) * M + m;
+        acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
+        *p = 0;
+      }
+    apply_row(E, M, m, valid, b, acc, need);
   }
 }
 
@@ -412,6 +465,17 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       if (!ok)
         for (int i = max(0, issued - C::STAGES); i < issued; ++i)
           mbar_wait(full(i % C::STAGES), (uint32_t)(i / C::STAGES) & 1u);
+      if (ok && E.pf_w && E.pf_tiles > 0) {
+        const int mt2 = (E.pf_M + BM - 1) / BM, nch2 = (E.pf_K + BK - 1) / BK;
+        const long long tot2 = (long long)mt2 * nch2;
+        const int a0 = (int)(tot2 * blockIdx.x / gridDim.x), a1 = (int)(tot2 * (blockIdx.x + 1) / gridDim.x);
+        const int np = min(a1 - a0, E.pf_tiles);
+        for (int j = 0; j < np; ++j) {
+          const int it = a0 + j;
+          const uint8_t* src = E.pf_w + ((size_t)((it / nch2) % mt2) * nch2 + (it % nch2)) * (BM * BK);
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(BM * BK) : "memory");
+        }
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -582,16 +646,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         const bool last = *flag_ptr != 0;
         if (last) {
           __threadfence();
-          for (int b = 0; b < B; ++b) {
-            uint64_t acc = 0;
-            if (valid)
-              for (int l = 0; l < L; ++l) {
-                int* p = P + (size_t)(l * B + b) * M + m;
-                acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
-                *p = 0;
-              }
-            apply_row(E, M, m, valid, b, acc, need);
-          }
+          finalize_from_P<BN>(E, P, M, m, valid, B, L, need);
           if (warp == 2 && lane == 0) tile_cnt[mt] = 0;
         }
         epi_bar();
@@ -626,16 +681,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         const int m = mt * BM + q * 32 + lane;
         const bool valid = m < M;
         int need = 0;
-        for (int b = 0; b < B; ++b) {
-          uint64_t acc = 0;
-          if (valid)
-            for (int l = 0; l < Lf; ++l) {
-              int* p = P + (size_t)(l * B + b) * M + m;
-              acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
-              *p = 0;
-            }
-          apply_row(E, M, m, valid, b, acc, need);
-        }
+        finalize_from_P<BN>(E, P, M, m, valid, B, Lf, need);
         epi_bar();
         if (warp == 2 && lane == 0) E.cnt_local[mt] = 0;
       }
