@@ -23,6 +23,7 @@ so the LM head is skipped there).  Decode steps replay one CUDA graph.
 """
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple
@@ -122,6 +123,11 @@ class Engine:
         self._rid = 0
         # weight tiles per CTA each fused GEMM prefetches into L2 for the next one
         self.prefetch_tiles = 0
+        # NVTX ranges per layer and phase (ARCB_NVTX=1), for timeline profilers
+        self.nvtx = bool(os.environ.get("ARCB_NVTX"))
+        # single-stream decode steps as one persistent kernel (runtime/decode_step.py)
+        self.use_step_kernel = os.environ.get("ARCB_STEP_KERNEL", "0") == "1"
+        self._step_progs = {}
 
     # ------------------------------------------------------------------ buffers
     def buffers(self, B: int, gen_cap: int = 0) -> StepBuffers:
@@ -146,9 +152,12 @@ class Engine:
         ss = bb.ss
         E = self._epis(bb)
         reduce_in_kernel = cm.size == 1 or getattr(cm, "fused", False)
+        nv = torch.cuda.nvtx if self.nvtx else None
         for l, Ly in enumerate(m.layers):
             c0, c1, c2, c3 = (bb.cnt[4 * l + i:4 * l + i + 1] for i in range(4))
             e = E[l]
+            if nv:
+                nv.range_push(f"layer {l} attention")
             ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
             ops.linear_gemm(Ly.qkv, bb.mXd, B, c0, bb.P, bb.tiles, e["qkv"])
             ops.attn(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo, c1,
@@ -159,6 +168,9 @@ class Engine:
                 ops.linear_gemm(Ly.wo, bb.mXo, B, c1, bb.P, bb.tiles, e["partial"])
                 cm.reduce_partials(bb.P, 8 * B, d, c1)
                 ops.finalize(bb.P, d, B, c1, Ly.wo.s, bb.h, d, 1, ss[2 * l + 1])
+            if nv:
+                nv.range_pop()
+                nv.range_push(f"layer {l} ffn")
             ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
             ops.linear_gemm(Ly.gu, bb.mXd, B, c2, bb.P, bb.tiles, e["gu"])
             if reduce_in_kernel:
@@ -167,6 +179,8 @@ class Engine:
                 ops.linear_gemm(Ly.down, bb.mXf, B, c3, bb.P, bb.tiles, e["partial"])
                 cm.reduce_partials(bb.P, 8 * B, d, c3)
                 ops.finalize(bb.P, d, B, c3, Ly.down.s, bb.h, d, 1, ss[2 * l + 2])
+            if nv:
+                nv.range_pop()
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
             ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
@@ -205,10 +219,26 @@ class Engine:
         return out
 
     def decode_step(self, bb: StepBuffers) -> None:
-        """forward + sample for every slot; slots advance in place."""
-        self.forward(bb, bb.B, True)
+        """forward + sample for every slot; slots advance in place.  Single-
+        stream steps (B <= 2, one GPU, int8 weights) run as one persistent
+        kernel when ``use_step_kernel`` is set."""
+        prog = self._step_program(bb) if getattr(self, "use_step_kernel", False) else None
+        if prog is not None:
+            m, c = self.m, self.m.cfg
+            ops.embed(bb.tokens, m.emb, m.emb_s, c.vocab, c.d_model, bb.B, bb.h, prog.cnt, bb.ss)
+            prog.launch()
+        else:
+            self.forward(bb, bb.B, True)
         ops.sample(bb.logits, self.m.cfg.vocab, bb.B, bb.hist, bb.count, bb.gen, bb.tokens, pos_inc=bb.pos,
                    done=bb.done, eos=bb.eos[:max(1, bb.n_eos)] if bb.n_eos else None)
+
+    def _step_program(self, bb: StepBuffers):
+        from arc_chain_b200.runtime import decode_step as dstep
+
+        key = id(bb)
+        if key not in self._step_progs:
+            self._step_progs[key] = dstep.StepProgram(self, bb) if dstep.eligible(self, bb) else None
+        return self._step_progs[key]
 
     def capture(self, bb: StepBuffers) -> torch.cuda.CUDAGraph:
         """Capture one decode step of `bb` into a CUDA graph (after a warm-up

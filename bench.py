@@ -65,6 +65,8 @@ def main():
     ap.add_argument("--requests", type=int, default=128)
     ap.add_argument("--batch", type=int, default=0)
     ap.add_argument("--prefetch", type=int, default=0, help="weight tiles per CTA each GEMM prefetches for the next")
+    ap.add_argument("--step-kernel", type=int, default=-1,
+                    help="1: each decode step as one persistent kernel, 0: one kernel per op, -1: engine default")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -152,6 +154,8 @@ def main():
     log("weights ready")
     eng = Engine(model, max_seq=max_seq, comm=comm, n_pages=2 * ((max_seq + 15) // 16))
     eng.prefetch_tiles = args.prefetch
+    if args.step_kernel >= 0:
+        eng.use_step_kernel = bool(args.step_kernel)
     prompt = gen.seeded_prompt(args.prompt_len, cfg.vocab, 1)
 
     W, K, G = args.warmup, args.steps, args.gen_len
@@ -239,6 +243,7 @@ def main():
                        "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
                        "l2": "weights per GPU >> 126 MB L2 (streamed from HBM every step)",
                        "prefetch_tiles": args.prefetch,
+                       "step_kernel": bool(eng.use_step_kernel),
                        "tokens_per_s": round(1000.0 / ms_tok, 2)},
             "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches_per_step * K),
             "first_sequence": {"tokens": len(tokens_first),

@@ -1,0 +1,312 @@
+// Device-side pieces of the persistent fused limb GEMM shared by the
+// per-GEMM kernel (gemm_fused.cu) and the persistent decode-step kernel
+// (decode_step.cu): the epilogue descriptor, tile configuration, epilogue
+// row application, split-tile finalisation, bounded waits and the stream-K
+// work list.  See gemm_fused.cu for the design.
+#pragma once
+#include <climits>
+
+#include "common.cuh"
+#include "lut.cuh"
+
+namespace fg {
+
+using namespace q16;
+
+constexpr int BM = 128;
+constexpr int BK = 128;
+constexpr int NTHREADS = 192;
+// Q4 tiles (group-32 4-bit weights): 128 rows x 64 bytes of nibbles (low
+// nibble = even column, value = nibble - 8) then 128 rows x 2 bytes of 4-bit
+// group multipliers (group g of the 128-column chunk in bits 4g..4g+3).
+constexpr int Q4_TILE = 128 * 64 + 128 * 2;
+constexpr int PAGE = 16;
+
+enum Mode : int { PARTIAL = 0, STORE = 1, RESID = 2, QKV = 3, SWIGLU = 4, MOE_COMBINE = 5 };
+
+struct Epi {
+  int mode;
+  const int64_t* scales;  // per fused row
+  int64_t* out;           // STORE / RESID target [B, ldo]
+  int ldo;
+  unsigned long long* ss_out;  // RESID: next norm's sum of squares per slot
+  // QKV
+  int n_heads, n_kv, dh;
+  int64_t* q_out;
+  int64_t* Kc;
+  int64_t* Vc;
+  const int* pt;
+  int pt_stride;
+  const int* pos;
+  const int64_t* rcos;
+  const int64_t* rsin;
+  int max_seq;
+  // SWIGLU: limb planes of the next GEMM's operand [8][B][ldx]
+  int8_t* X;
+  int ldx;
+  int* lmax_out;
+  int* err;
+  int B;  // slots in the step (plane stride of X = B * ldx)
+  // Tensor-parallel push mode (rp = 1): partials go to every rank's P over
+  // NVLink (peer pointers of a symmetric allocation), arrivals to every
+  // rank's per-tile counters; tile mt is finalised on each rank by its CTA
+  // mt % gridDim.x once all ranks' chunks have arrived.
+  int rp;
+  int npeers;
+  int* const* peer_P;
+  int* const* peer_cnt;
+  int* const* peer_lmax;
+  int* cnt_local;
+  int* lmax_fin;
+  // optional per-CTA %globaltimer stamps [grid][8]: 0 entry, 1 after the
+  // dependency wait, 2 first stage consumed, 3 last MMA issued, 4 epilogue
+  // done, 5 finaliser done, 6 exit
+  unsigned long long* prof;
+  // Grouped (MoE) GEMMs over stacked experts: rows come in groups of
+  // grp_rows per expert; grp_koff > 0 makes group g read operand columns
+  // [g * grp_koff, g * grp_koff + K) (each expert's own intermediate).
+  int grp_rows;
+  int grp_koff;
+  // MOE_COMBINE: h[b, i] += (route[b, g] * y) >> 16 for routed experts.
+  const int64_t* route;
+  int route_ld;
+  // Upper bound on persistent CTAs (0 = one per SM).  Fewer CTAs means
+  // fewer CTAs share a tile, so less partial-sum traffic at larger batch.
+  int max_ctas;
+  // Rows per TMA box of the limb operand's tensor map (0 = BN).  With a box
+  // smaller than BN only the boxes that hold live rows (limbs x slots) are
+  // loaded, so a batch whose activations need few limbs does not stream the
+  // unused limb planes.
+  int b_box;
+  // Expert parallelism: MOE_COMBINE reads route column g * route_gs of
+  // local group g (route points at this rank's first expert column;
+  // 0 = stride 1) and, with peer_h set, adds into the npeers targets
+  // peer_h[p] (every rank's combine buffer) instead of out; with peer_sig
+  // set every CTA, once its adds are fenced, increments every rank's
+  // arrival counter peer_sig[p] by one.
+  int route_gs;
+  int64_t* const* peer_h;
+  unsigned long long* const* peer_sig;
+  // Cross-GEMM prefetch: once this CTA's producer has issued its last load,
+  // it asks L2 for the first pf_tiles weight tiles that the same CTA index
+  // will stream in the next GEMM (tiled int8 weights pf_w of [pf_M, pf_K],
+  // one N tile, the same grid), so HBM stays busy through this GEMM's tail
+  // and the next GEMM's first stages hit L2.  null = off.
+  const uint8_t* pf_w;
+  int pf_M, pf_K, pf_tiles;
+};
+
+// Ring depth for decode-sized tiles (BN <= 32).  A 5-stage ring (two CTAs
+// per SM, so the next GEMM could prefetch during this one's tail) measured
+// slower on the 7B decode (3.31 vs 3.15 ms/token): the deep ring wins.
+#ifndef ARCB_FG_SMALL_STAGES
+#define ARCB_FG_SMALL_STAGES 11
+#endif
+
+template <int BN, bool Q4 = false>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int Q_BYTES = Q4 ? Q4_TILE : 0;        // staging of the packed Q4 tile
+  static constexpr int STAGE_BYTES = (Q4 ? Q4_TILE : A_BYTES) + B_BYTES;  // bytes TMA brings per stage
+  static constexpr int STAGES = Q4 ? (BN <= 32 ? 7 : (BN <= 64 ? 6 : (BN <= 128 ? 5 : 3)))
+                                   : (BN <= 32 ? ARCB_FG_SMALL_STAGES : (BN <= 64 ? 8 : (BN <= 128 ? 6 : 4)));
+  static constexpr int ACC_COLS = BN < 32 ? 32 : BN;       // one TMEM accumulator
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;          // double buffered
+  static constexpr int THREADS = Q4 ? 320 : NTHREADS;     // + 4 converter warps for Q4
+  static constexpr int SMEM = 1024 + STAGES * (A_BYTES + B_BYTES + Q_BYTES) + 512;
+};
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld1(uint32_t taddr, uint32_t& r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+}
+
+__device__ __forceinline__ uint64_t sq16(int64_t x) { return (uint64_t)(wmul(x, x) >> FRAC_BITS); }
+
+__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
+  return v;
+}
+
+// Applies the epilogue to output row m (fused-row index) of slot b, given the
+// recombined wrapping accumulator acc = sum_k W[m,k] x_b[k].  Called by all 32
+// lanes of a warp together (rows m0..m0+31) so pair exchanges can shuffle.
+__device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid, int b, uint64_t acc,
+                                          int& need) {
+  const int64_t s = valid ? E.scales[m] : 0;
+  const int64_t v = mulshr((int64_t)acc, s);
+  const int lane = threadIdx.x & 31;
+  switch (E.mode) {
+    case STORE:
+      if (valid) E.out[(size_t)b * E.ldo + m] = v;
+      break;
+    case RESID: {
+      uint64_t sq = 0;
+      if (valid) {
+        int64_t* o = E.out + (size_t)b * E.ldo + m;
+        // L2 read: in the persistent step kernel another CTA may have updated
+        // this row since this SM last cached it
+        const int64_t r = wadd(__ldcg(o), v);
+        *o = r;
+        sq = sq16(r);
+      }
+      if (E.ss_out) {
+        sq = warp_sum_u64(sq);
+        if (lane == 0) atomicAdd(E.ss_out + b, (unsigned long long)sq);
+      }
+      break;
+    }
+    case QKV: {
+      const int d = E.n_heads * E.dh, dkv = E.n_kv * E.dh, half = E.dh / 2;
+      const int64_t partner = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, 1);
+      if (!valid) break;
+      const int p = E.pos[b];
+      if (p < 0 || p >= E.max_seq) {
+        set_error(E.err, ARCB_ERR_SEQ_OVERFLOW);
+        break;
+      }
+      const int page = E.pt[(size_t)b * E.pt_stride + p / PAGE];
+      const int slot = p % PAGE;
+      if (m < d + dkv) {
+        const bool is_q = m < d;
+        const int r = is_q ? m : m - d;
+        const int head = r / E.dh, w = r % E.dh, i = w >> 1, role = w & 1;
+        int64_t x0 = role ? partner : v, x1 = role ? v : partner;
+        rope_pair(x0, x1, E.rcos[(size_t)p * half + i], E.rsin[(size_t)p * half + i]);
+        const int e = role ? i + half : i;
+        const int64_t y = role ? x1 : x0;
+        if (is_q) E.q_out[(size_t)b * d + head * E.dh + e] = y;
+        else E.Kc[(((size_t)page * E.n_kv + head) * PAGE + slot) * E.dh + e] = y;
+      } else {
+        const int j = m - d - dkv;
+        E.Vc[(((size_t)page * E.n_kv + j / E.dh) * PAGE + slot) * E.dh + (j % E.dh)] = v;
+      }
+      break;
+    }
+    case SWIGLU: {
+      const int64_t partner = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, 1);
+      if (valid && (m & 1) == 0) {
+        const int j = m >> 1;
+        const int64_t y = swiglu(v, partner, g_exp_lut.v);
+        int8_t dg[8];
+        const int n = limb_split8(y, dg);
+        need = n > need ? n : need;
+        const size_t ps = (size_t)E.ldx * E.B;
+        const size_t off = (size_t)b * E.ldx + j;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) E.X[l * ps + off] = dg[l];
+      }
+      break;
+    }
+    case MOE_COMBINE: {
+      if (!valid) break;
+      const int g = m / E.grp_rows, i = m - g * E.grp_rows;
+      const int64_t w = E.route[(size_t)b * E.route_ld + (size_t)g * (E.route_gs ? E.route_gs : 1)];
+      if (w != 0) {
+        const unsigned long long add = (unsigned long long)mulshr(w, v);
+        const size_t off = (size_t)b * E.ldo + i;
+        if (E.peer_h) {
+          for (int p = 0; p < E.npeers; ++p) atomicAdd((unsigned long long*)(E.peer_h[p] + off), add);
+        } else {
+          atomicAdd((unsigned long long*)(E.out + off), add);
+        }
+      }
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+// Finalises row m of a split tile from the partial buffer P: reads and
+// clears its L x B int32 partials, recombines the limbs and applies the
+// epilogue.  Wide tiles (BN >= 64, i.e. batches of 8 or more) read 8 slots x
+// L limbs per round with every load in flight together; each load otherwise
+// waits for the previous clear, and a batch of 32 slots at 3 limbs would
+// serialise 96 L2 round trips.  Called by all lanes of a warp together.
+template <int BN>
+__device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int m, bool valid, int B, int L,
+                                                int& need) {
+  if (BN >= 64) {
+    constexpr int FS = 4;  // slots per round: 4 x L loads in flight, no spills
+    for (int b0 = 0; b0 < B; b0 += FS) {
+      int v[8][FS];
+#pragma unroll
+      for (int l = 0; l < 8; ++l)
+#pragma unroll
+        for (int j = 0; j < FS; ++j)
+          v[l][j] = (valid && l < L && b0 + j < B) ? __ldcg(P + (size_t)(l * B + b0 + j) * M + m) : 0;
+#pragma unroll
+      for (int l = 0; l < 8; ++l)
+#pragma unroll
+        for (int j = 0; j < FS; ++j)
+          if (valid && l < L && b0 + j < B) __stcg(P + (size_t)(l * B + b0 + j) * M + m, 0);
+#pragma unroll
+      for (int j = 0; j < FS; ++j) {
+        if (b0 + j >= B) break;
+        uint64_t acc = 0;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) acc += (uint64_t)(int64_t)v[l][j] << (8 * l);
+        apply_row(E, M, m, valid, b0 + j, acc, need);
+      }
+    }
+    return;
+  }
+  for (int b = 0; b < B; ++b) {
+    uint64_t acc = 0;
+    if (valid)
+      for (int l = 0; l < L; ++l) {
+        int* p = P + (size_t)(l * B + b) * M + m;
+        acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
+        *p = 0;
+      }
+    apply_row(E, M, m, valid, b, acc, need);
+  }
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait for a counter written by other GPUs (and this GPU's CTAs).
+__device__ __forceinline__ bool wait_counter_geq(const int* p, int target) {
+  if (ld_acquire_sys(p) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_acquire_sys(p) >= target) return true;
+    if ((i & 63) == 63) {
+      if (globaltimer_ns() - t0 > ARCB_WAIT_NS) return false;
+      __nanosleep(64);
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Work item -> (n-tile, m-tile, chunk); CTA c owns items [it0, it1).
+struct Work {
+  int Mt, nch, it0, it1;
+  __device__ void range(int ntu) {
+    const long long total = (long long)ntu * Mt * nch;
+    it0 = (int)(total * blockIdx.x / gridDim.x);
+    it1 = (int)(total * (blockIdx.x + 1) / gridDim.x);
+  }
+  __device__ int nt(int it) const { return it / (Mt * nch); }
+  __device__ int mt(int it) const { return (it / nch) % Mt; }
+  __device__ int kc(int it) const { return it % nch; }
+  __device__ int seg_end(int it) const { return min(it1, (it / nch + 1) * nch); }
+  // Weights are stored tiled: tile (m, k) is 128 rows x 128 bytes, contiguous,
+  // at row (m * nch + k) * 128 of a [Mt * nch * 128, 128] byte matrix, so one
+  // TMA box is one contiguous 16 KB DRAM block.
+  __device__ int tile_row(int it) const { return (mt(it) * nch + kc(it)) * BM; }
+};
+}  // namespace fg
