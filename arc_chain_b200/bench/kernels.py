@@ -44,11 +44,11 @@ def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True, sub_box=None, ctas=No
     maps = [ops.TensorMap(w, 128) for w in Ws]
     S = torch.randint(1, 100, (M,), dtype=torch.int64, device=dev)
     bn = ops.fgemm_bn(B)
-    X = torch.randint(-127, 128, (max(8 * B, bn), K), dtype=torch.int8, device=dev)
+    X = torch.randint(-127, 128, (ops.limb_rows(B, bn), K), dtype=torch.int8, device=dev)
     xm = ops.TensorMap(X, bn, min(sub_box, bn) if sub_box else None)
     lmax = torch.tensor([limbs], dtype=torch.int32, device=dev)
     P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
-    tiles = torch.zeros(M // 128 + 2, dtype=torch.int32, device=dev)
+    tiles = torch.zeros(ops.tile_counters(M, B), dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     out = torch.zeros(B, M, dtype=torch.int64, device=dev)
     e = ops.epi(ops.STORE if mode == "store" else ops.PARTIAL, S, err, out=out, ldo=M)
@@ -71,7 +71,7 @@ def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True, sub_box=None, ctas=No
             "GB_s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak_gbs(), 3)}
 
 
-def bench_attn(T, n_heads=32, dh=128, B=1, iters=50):
+def bench_attn(T, n_heads=32, dh=128, B=1, iters=50, cluster=None):
     dev = torch.device("cuda")
     pages = (T + 15) // 16
     npg = pages * B
@@ -80,22 +80,22 @@ def bench_attn(T, n_heads=32, dh=128, B=1, iters=50):
     q = torch.randint(-(1 << 18), 1 << 18, (B, n_heads * dh), dtype=torch.int64, device=dev)
     pt = torch.arange(npg, dtype=torch.int32, device=dev).view(B, pages)
     pos = torch.full((B,), T - 1, dtype=torch.int32, device=dev)
-    X = torch.zeros(8 * B, n_heads * dh, dtype=torch.int8, device=dev)
+    X = torch.zeros(ops.limb_rows(B), n_heads * dh, dtype=torch.int8, device=dev)
     lm = torch.zeros(1, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     for _ in range(3):
-        ops.attn(q, K, V, pt, pos, n_heads, n_heads, dh, 5793, B, X, lm, pages * 16, err)
+        ops.attn(q, K, V, pt, pos, n_heads, n_heads, dh, 5793, B, X, lm, pages * 16, err, cluster=cluster)
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(iters):
-        ops.attn(q, K, V, pt, pos, n_heads, n_heads, dh, 5793, B, X, lm, pages * 16, err)
+        ops.attn(q, K, V, pt, pos, n_heads, n_heads, dh, 5793, B, X, lm, pages * 16, err, cluster=cluster)
     t1.record()
     torch.cuda.synchronize()
     us = t0.elapsed_time(t1) * 1000 / iters
     nbytes = 2 * B * T * n_heads * dh * 8
     return {"kernel": "attn_cluster", "T": T, "heads": n_heads, "B": B, "us": round(us, 2),
-            "GB_s": round(nbytes / us / 1e3, 1), "cluster": ops.attn_cluster_size(B, n_heads)}
+            "GB_s": round(nbytes / us / 1e3, 1), "cluster": cluster or ops.attn_cluster_size(B, n_heads)}
 
 
 def main():
@@ -103,10 +103,11 @@ def main():
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--only", default="")
-    ap.add_argument("--shape", default="", help="one of " + ",".join(SHAPES_7B))
+    ap.add_argument("--shape", default="", help="one of " + ",".join(SHAPES_7B) +
+                    "; with --only stream: comma-separated buffer sizes in MB")
     a = ap.parse_args()
     torch.cuda.set_device(0)
-    if a.shape:
+    if a.shape and a.only != "stream":
         M, K = SHAPES_7B[a.shape]
         r = bench_fgemm(M, K, a.B, a.iters)
         r["name"] = a.shape
@@ -118,6 +119,46 @@ def main():
                 r = bench_fgemm(M, K, a.B, a.iters, pdl=pdl)
                 r["name"] = name
                 print(json.dumps(r), flush=True)
+    if a.only == "stream":
+        # bulk-copy streaming probe: achievable weight-load bandwidth without MMA
+        sizes = [int(x) << 20 for x in a.shape.split(",")] if a.shape else [2048]
+        cap = max(sizes) << 20 if not a.shape else max(sizes)
+        cap = max(cap, 2 << 30)
+        buf = torch.randint(-127, 128, (cap // 128, 128), dtype=torch.int8, device="cuda")
+        tm = ops.TensorMap(buf, 128)
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        flush = torch.empty(256 << 20, dtype=torch.int8, device="cuda")
+        for nbytes in ([2 << 30] if not a.shape else sizes):
+          for mode in (0, 1):
+            for tile in (16384, 32768):
+                for stages in (4, 6, 8, 11):
+                    if stages * tile > 216 * 1024:
+                        continue
+                    for grid in (ops.num_sms(),):
+                        def run():
+                            ops.check(ops.lib().arcb_stream_probe(tm.addr, buf.data_ptr(), nbytes, tile, stages, mode,
+                                                                  grid, err.data_ptr(), ops._s()), "stream_probe")
+                        run()
+                        torch.cuda.synchronize()
+                        tot = 0.0
+                        for _ in range(5):
+                            flush.zero_()  # cold L2 for every timed launch
+                            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                            t0.record()
+                            run()
+                            t1.record()
+                            torch.cuda.synchronize()
+                            tot += t0.elapsed_time(t1) * 1000
+                        us = tot / 5
+                        print(json.dumps({"probe": "stream", "MB": nbytes >> 20, "mode": ["tma2d", "bulk1d"][mode],
+                                          "tile": tile, "stages": stages, "grid": grid, "us": round(us, 2),
+                                          "GB_s": round(nbytes / us / 1e3, 1), "err": int(err.item())}), flush=True)
+        return
+    if a.only == "attn_cs":
+        for T in (130, 386, 1024):
+            for cs in (1, 2, 4, 8):
+                print(json.dumps(bench_attn(T, B=a.B, iters=a.iters, cluster=cs)), flush=True)
+        return
     if a.only == "batch":
         # sub-box limb loads and CTA budget across batch sizes
         shapes = dict(SHAPES_7B, **SHAPES_MOE)
@@ -148,11 +189,11 @@ def timeline_fgemm(M, K, B=1, reps=5):
     wm = ops.TensorMap(W, 128)
     S = torch.randint(1, 100, (M,), dtype=torch.int64, device=dev)
     bn = ops.fgemm_bn(B)
-    X = torch.randint(-127, 128, (max(8 * B, bn), K), dtype=torch.int8, device=dev)
+    X = torch.randint(-127, 128, (ops.limb_rows(B, bn), K), dtype=torch.int8, device=dev)
     xm = ops.TensorMap(X, bn)
     lmax = torch.tensor([3], dtype=torch.int32, device=dev)
     P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
-    tiles = torch.zeros(M // 128 + 2, dtype=torch.int32, device=dev)
+    tiles = torch.zeros(ops.tile_counters(M, B), dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     out = torch.zeros(B, M, dtype=torch.int64, device=dev)
     prof = torch.zeros(ops.num_sms() * 8, dtype=torch.int64, device=dev)

@@ -188,7 +188,7 @@ class MlaBuffers:
         self.Q = torch.zeros(B, H, r + dr, dtype=I64, device=dev)
         self.oc = torch.zeros(B, H, r, dtype=I64, device=dev)
         self.bn = ops.fgemm_bn(B)
-        rows = max(8 * B, self.bn)
+        rows = ops.limb_rows(B, self.bn)
         self.Xd = torch.zeros(rows, d, dtype=I8, device=dev)
         self.Xo = torch.zeros(rows, H * dv, dtype=I8, device=dev)
         self.Xf = torch.zeros(rows, max(c.d_ff, 16), dtype=I8, device=dev)
@@ -203,7 +203,7 @@ class MlaBuffers:
                     ms.append(lin.M)
         mmax = max(ms)
         self.P = torch.zeros(8 * B * mmax, dtype=torch.int32, device=dev)
-        self.tiles = torch.zeros((mmax + 127) // 128 + 1, dtype=I32, device=dev)
+        self.tiles = torch.zeros(ops.tile_counters(mmax, B), dtype=I32, device=dev)
         self.cnt = torch.zeros(4 * c.n_layers + 4, dtype=I32, device=dev)
         self.ss = torch.zeros(1, B, dtype=I64, device=dev)
         self.err = torch.zeros(1, dtype=I32, device=dev)

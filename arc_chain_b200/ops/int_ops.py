@@ -328,14 +328,60 @@ def fgemm_q4(packed: torch.Tensor, xmap: TensorMap, M: int, K: int, B: int, lmax
 SPLIT_TABLE = [(2, 64), (8, 4), (32, 2), (1 << 30, 1)]
 
 
+def limb_slots(B: int) -> int:
+    """Slots per block of the limb-operand layout (csrc/kernels/common.cuh limb_row)."""
+    return min(B, 32)
+
+
+def n_tiles(B: int) -> int:
+    """N tiles of the fused GEMM for B slots (one per 32-slot block)."""
+    S = limb_slots(B)
+    return (B + S - 1) // S
+
+
+def limb_rows(B: int, bn: Optional[int] = None) -> int:
+    """Rows of a limb operand of B slots (every block's 8 planes, at least one TMA box)."""
+    return max(8 * n_tiles(B) * limb_slots(B), bn or fgemm_bn(B))
+
+
+def tile_counters(M: int, B: int) -> int:
+    """Entries of the fused GEMM's per-(M tile, N tile) arrival counters."""
+    return ((M + BM - 1) // BM) * n_tiles(B) + 1
+
+
+def limb_row(l: int, b: int, B: int) -> int:
+    S = limb_slots(B)
+    return (b // S) * 8 * S + l * S + b % S
+
+
+def limb_planes(x, rows: Optional[int] = None):
+    """Host limb operand of int64 values x [B, K]: (int8 [rows, K] in the
+    limb_row layout, limb count); signed radix-256 digits."""
+    import numpy as np
+
+    x = np.asarray(x, dtype=np.int64)
+    B, K = x.shape
+    rows = rows or limb_rows(B)
+    out = np.zeros((rows, K), dtype=np.int8)
+    r = x.copy()
+    need = 0
+    for l in range(8):
+        d = (r & 0xFF).astype(np.uint8).view(np.int8)
+        for b in range(B):
+            out[limb_row(l, b, B)] = d[b]
+        r = (r - d.astype(np.int64)) >> 8
+        if np.any(d != 0):
+            need = l + 1
+    return out, max(need, 1)
+
+
 def split_ctas(M: int, B: int, bn: int) -> int:
     """CTA budget of the stream-K GEMM: at decode batch 1-2 every SM streams
     (tiles split many ways; the partials are few); as the batch grows each
     split adds B x limbs partials per row, so tiles are shared by fewer CTAs."""
     splits = next(s for b, s in SPLIT_TABLE if B <= b)
     mt = (M + BM - 1) // BM
-    ntu = max(1, (3 * B + bn - 1) // bn)
-    return max(1, mt * ntu * splits)
+    return max(1, mt * n_tiles(B) * splits)
 
 
 def linear_gemm(lin, xmap: TensorMap, B: int, lmax, P, tile_cnt, epi: Epi) -> None:

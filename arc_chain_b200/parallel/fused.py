@@ -63,7 +63,7 @@ class FusedComm(NcclComm):
     def _site(self, bb, site: int, M: int) -> _Site:
         key = (id(bb), site)
         if key not in self._sites:
-            self._sites[key] = _Site(8 * bb.B * M, (M + 127) // 128 + 1, bb.P.device, self.group_name)
+            self._sites[key] = _Site(8 * bb.B * M, ops.tile_counters(M, bb.B), bb.P.device, self.group_name)
             torch.cuda.synchronize()
             dist.barrier(group=self.group)
         return self._sites[key]

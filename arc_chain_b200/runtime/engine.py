@@ -78,7 +78,7 @@ class StepBuffers:
         self.q = torch.zeros(B, dl, dtype=I64, device=dev)
         self.bn = ops.fgemm_bn(B)
         self.epis = None
-        rows = max(8 * B, self.bn)  # the TMA box never exceeds the tensor
+        rows = ops.limb_rows(B, self.bn)  # limb_row layout; the TMA box never exceeds the tensor
         self.Xd = torch.zeros(rows, d, dtype=I8, device=dev)
         self.Xo = torch.zeros(rows, dl, dtype=I8, device=dev)
         self.Xf = torch.zeros(rows, dffl, dtype=I8, device=dev)
@@ -102,7 +102,7 @@ class StepBuffers:
         self.eos = torch.zeros(8, dtype=I32, device=dev)
         self.n_eos = 0
         # per-M-tile arrival counters of the fused GEMM (zero between uses)
-        self.tiles = torch.zeros((mmax + 127) // 128 + 1, dtype=I32, device=dev)
+        self.tiles = torch.zeros(ops.tile_counters(mmax, B), dtype=I32, device=dev)
 
 
 class Engine:
@@ -125,6 +125,8 @@ class Engine:
         self.prefetch_tiles = 0
         # NVTX ranges per layer and phase (ARCB_NVTX=1), for timeline profilers
         self.nvtx = bool(os.environ.get("ARCB_NVTX"))
+        # optional op timeline of eager forwards: list of (label, CUDA event) appended after each op
+        self.op_events = None
         # single-stream decode steps as one persistent kernel (runtime/decode_step.py)
         self.use_step_kernel = os.environ.get("ARCB_STEP_KERNEL", "0") == "1"
         self._step_progs = {}
@@ -153,32 +155,48 @@ class Engine:
         E = self._epis(bb)
         reduce_in_kernel = cm.size == 1 or getattr(cm, "fused", False)
         nv = torch.cuda.nvtx if self.nvtx else None
+        ev = self.op_events
+
+        def mark(label):
+            if ev is not None:
+                e_ = torch.cuda.Event(enable_timing=True)
+                e_.record()
+                ev.append((label, e_))
+
+        mark("embed")
         for l, Ly in enumerate(m.layers):
             c0, c1, c2, c3 = (bb.cnt[4 * l + i:4 * l + i + 1] for i in range(4))
             e = E[l]
             if nv:
                 nv.range_push(f"layer {l} attention")
             ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
+            mark("norm")
             ops.linear_gemm(Ly.qkv, bb.mXd, B, c0, bb.P, bb.tiles, e["qkv"])
+            mark("qkv")
             ops.attn(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo, c1,
                      self.max_pages * PAGE, bb.err)
+            mark("attn")
             if reduce_in_kernel:
                 cm.fgemm_reduce(Ly.wo, bb.mXo, B, c1, bb, e["wo"], site=0)
             else:
                 ops.linear_gemm(Ly.wo, bb.mXo, B, c1, bb.P, bb.tiles, e["partial"])
                 cm.reduce_partials(bb.P, 8 * B, d, c1)
                 ops.finalize(bb.P, d, B, c1, Ly.wo.s, bb.h, d, 1, ss[2 * l + 1])
+            mark("wo")
             if nv:
                 nv.range_pop()
                 nv.range_push(f"layer {l} ffn")
             ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
+            mark("norm")
             ops.linear_gemm(Ly.gu, bb.mXd, B, c2, bb.P, bb.tiles, e["gu"])
+            mark("gate_up")
             if reduce_in_kernel:
                 cm.fgemm_reduce(Ly.down, bb.mXf, B, c3, bb, e["down"], site=1)
             else:
                 ops.linear_gemm(Ly.down, bb.mXf, B, c3, bb.P, bb.tiles, e["partial"])
                 cm.reduce_partials(bb.P, 8 * B, d, c3)
                 ops.finalize(bb.P, d, B, c3, Ly.down.s, bb.h, d, 1, ss[2 * l + 2])
+            mark("down")
             if nv:
                 nv.range_pop()
         if with_logits:

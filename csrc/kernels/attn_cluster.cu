@@ -188,9 +188,8 @@ __global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__
       int8_t dg[8];
       const int nl = limb_split8((int64_t)o, dg);
       need = nl > need ? nl : need;
-      const size_t ps = (size_t)B * d;
 #pragma unroll
-      for (int l = 0; l < 8; ++l) X[l * ps + off] = dg[l];
+      for (int l = 0; l < 8; ++l) X[limb_row(l, b, B) * d + hq * dv + e] = dg[l];
     }
   }
   need = __reduce_max_sync(0xffffffffu, need);

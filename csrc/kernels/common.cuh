@@ -196,6 +196,18 @@ __device__ __forceinline__ int64_t shfl_xor_i64(int64_t v, int m) {
   return (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, m);
 }
 
+// Limb-operand layout: the row of limb plane l of slot b when B slots are
+// split into limbs.  Slots are grouped in blocks of S = min(B, 32); a block
+// occupies 8 * S consecutive rows, limb-major inside (row l * S + slot), so
+// one 256-row N tile of the fused GEMM holds every limb of its 32 slots and
+// can recombine them from TMEM.  For B <= 32 this is the single block
+// row = l * B + b.
+__host__ __device__ __forceinline__ int limb_slots(int B) { return B < 32 ? B : 32; }
+__host__ __device__ __forceinline__ size_t limb_row(int l, int b, int B) {
+  if (B <= 32) return (size_t)l * B + b;  // one block: no division
+  return (size_t)(b >> 5) * 256 + (size_t)l * 32 + (size_t)(b & 31);
+}
+
 // Signed-digit limb split of one value into 8 int8 planes.
 __device__ __forceinline__ int limb_split8(int64_t x, int8_t* d) {
   int need = 0;

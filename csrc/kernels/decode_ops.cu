@@ -99,12 +99,13 @@ __device__ __forceinline__ int64_t block_max_i64(int64_t v, int64_t* sh) {
   return r;
 }
 
-__device__ __forceinline__ void store_limbs(int8_t* X, size_t plane_stride, size_t off, int64_t v, int& need) {
+// Limb digits of v (slot b, column j of a [rows, ld] limb operand of B slots).
+__device__ __forceinline__ void store_limbs(int8_t* X, int B, int ld, int b, int j, int64_t v, int& need) {
   int8_t d[8];
   int n = limb_split8(v, d);
   need = n > need ? n : need;
 #pragma unroll
-  for (int l = 0; l < 8; ++l) X[l * plane_stride + off] = d[l];
+  for (int l = 0; l < 8; ++l) X[limb_row(l, b, B) * ld + j] = d[l];
 }
 
 // Recombine one output element from its limb partials and zero them.
@@ -165,7 +166,7 @@ __global__ void k_norm_limbs(const int64_t* __restrict__ h, const uint64_t* __re
     const size_t off = (size_t)b * d + j;
     const int64_t y = rms_apply(h[off], inv, j < ngamma ? gamma[j] : ONE);
     if (y_out) y_out[off] = y;
-    if (X) store_limbs(X, (size_t)B * d, off, y, need);
+    if (X) store_limbs(X, B, d, b, j, y, need);
   }
   need = block_max_int(need, shi);
   if (threadIdx.x == 0 && lmax) atomicMax(lmax, need);
@@ -189,7 +190,7 @@ __global__ void k_rmsnorm_limbs(const int64_t* __restrict__ h, const int64_t* __
   for (int j = threadIdx.x; j < d; j += blockDim.x) {
     const int64_t y = rms_apply(x[j], inv, j < ngamma ? gamma[j] : ONE);
     if (y_out) y_out[(size_t)b * d + j] = y;
-    if (X) store_limbs(X, (size_t)B * d, (size_t)b * d + j, y, need);
+    if (X) store_limbs(X, B, d, b, j, y, need);
   }
   need = block_max_int(need, shi);
   if (threadIdx.x == 0 && lmax) atomicMax(lmax, need);
@@ -288,7 +289,7 @@ __global__ void k_finalize_swiglu(int* __restrict__ P, int dff, int B, const int
     const int64_t u = fin_elem(P, M, B, L, b, dff + j, scales[dff + j]);
     const int64_t y = swiglu(g, u, g_exp_lut.v);
     if (y_out) y_out[(size_t)b * dff + j] = y;
-    store_limbs(X, (size_t)B * dff, (size_t)b * dff + j, y, need);
+    store_limbs(X, B, dff, b, j, y, need);
   }
   need = block_max_int(need, shi);
   if (threadIdx.x == 0) atomicMax(lmax_out, need);
@@ -423,7 +424,7 @@ __global__ void k_attn_pv(const int64_t* __restrict__ Vc, const int* __restrict_
     O[bh * dh + e] = 0;
     const size_t off = (size_t)b * d + hq * dh + e;
     if (o_out) o_out[off] = o;
-    if (X) store_limbs(X, (size_t)B * d, off, o, need);
+    if (X) store_limbs(X, B, d, b, hq * dh + e, o, need);
   }
   need = block_max_int(need, shi);
   if (threadIdx.x == 0) {

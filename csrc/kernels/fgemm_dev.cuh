@@ -196,10 +196,8 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
         int8_t dg[8];
         const int n = limb_split8(y, dg);
         need = n > need ? n : need;
-        const size_t ps = (size_t)E.ldx * E.B;
-        const size_t off = (size_t)b * E.ldx + j;
 #pragma unroll
-        for (int l = 0; l < 8; ++l) E.X[l * ps + off] = dg[l];
+        for (int l = 0; l < 8; ++l) E.X[limb_row(l, b, E.B) * E.ldx + j] = dg[l];
       }
       break;
     }
@@ -231,24 +229,26 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
 // serialise 96 L2 round trips.  Called by all lanes of a warp together.
 template <int BN>
 __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int m, bool valid, int B, int L,
-                                                int& need) {
+                                                int& need, int bb0 = 0, int bb1 = -1) {
+  // slots [bb0, bb1) of the partial buffer (row l * B + b); the whole batch by default
+  if (bb1 < 0) bb1 = B;
   if (BN >= 64) {
     constexpr int FS = 4;  // slots per round: 4 x L loads in flight, no spills
-    for (int b0 = 0; b0 < B; b0 += FS) {
+    for (int b0 = bb0; b0 < bb1; b0 += FS) {
       int v[8][FS];
 #pragma unroll
       for (int l = 0; l < 8; ++l)
 #pragma unroll
         for (int j = 0; j < FS; ++j)
-          v[l][j] = (valid && l < L && b0 + j < B) ? __ldcg(P + (size_t)(l * B + b0 + j) * M + m) : 0;
+          v[l][j] = (valid && l < L && b0 + j < bb1) ? __ldcg(P + (size_t)(l * B + b0 + j) * M + m) : 0;
 #pragma unroll
       for (int l = 0; l < 8; ++l)
 #pragma unroll
         for (int j = 0; j < FS; ++j)
-          if (valid && l < L && b0 + j < B) __stcg(P + (size_t)(l * B + b0 + j) * M + m, 0);
+          if (valid && l < L && b0 + j < bb1) __stcg(P + (size_t)(l * B + b0 + j) * M + m, 0);
 #pragma unroll
       for (int j = 0; j < FS; ++j) {
-        if (b0 + j >= B) break;
+        if (b0 + j >= bb1) break;
         uint64_t acc = 0;
 #pragma unroll
         for (int l = 0; l < 8; ++l) acc += (uint64_t)(int64_t)v[l][j] << (8 * l);
@@ -257,7 +257,7 @@ __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int
     }
     return;
   }
-  for (int b = 0; b < B; ++b) {
+  for (int b = bb0; b < bb1; ++b) {
     uint64_t acc = 0;
     if (valid)
       for (int l = 0; l < L; ++l) {
@@ -292,16 +292,20 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Work item -> (n-tile, m-tile, chunk); CTA c owns items [it0, it1).
+// Work item -> (m-tile, n-tile, chunk), m-tile major: the n-tiles of one
+// weight tile are consecutive items, so CTAs working on them at the same time
+// share the weight tile through L2.  CTA c owns items [it0, it1).
 struct Work {
-  int Mt, nch, it0, it1;
-  __device__ void range(int ntu) {
+  int Mt, nch, it0, it1, ntu = 1;
+  __device__ void range(int ntu_) {
+    ntu = ntu_;
     const long long total = (long long)ntu * Mt * nch;
     it0 = (int)(total * blockIdx.x / gridDim.x);
     it1 = (int)(total * (blockIdx.x + 1) / gridDim.x);
   }
-  __device__ int nt(int it) const { return it / (Mt * nch); }
-  __device__ int mt(int it) const { return (it / nch) % Mt; }
+  __device__ int nt(int it) const { return (it / nch) % ntu; }
+  __device__ int mt(int it) const { return it / (nch * ntu); }
+  __device__ int tile(int it) const { return it / nch; }  // (mt, nt) index = mt * ntu + nt
   __device__ int kc(int it) const { return it % nch; }
   __device__ int seg_end(int it) const { return min(it1, (it / nch + 1) * nch); }
   // Weights are stored tiled: tile (m, k) is 128 rows x 128 bytes, contiguous,

@@ -31,7 +31,8 @@ using namespace q16;
 
 namespace fg {
 
-template <int BN, bool Q4>
+// MB: the launch has several 32-slot blocks (B > 32, 256-row tiles only).
+template <int BN, bool Q4, bool MB>
 __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
     k_gemm_fused(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
                  int B, int n_tiles_max, int prefetch_ok, const int* __restrict__ lmax, int* __restrict__ P,
@@ -110,9 +111,16 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
     }
   };
   // Weights do not depend on the previous kernel: start streaming them.
+  // The work list depends only on B (n-tiles = slot blocks), not on the limb
+  // count, so it is known before the dependency wait.
+  // Only launches with B > 32 (256-row tiles) have several 32-slot blocks;
+  // the others have one block of B slots, which the compiler is told.
+  constexpr bool MULTI = MB;
+  const int S = MULTI ? limb_slots(B) : B;
+  const int ntu = MULTI ? n_tiles_max : 1;  // = ceil(B / S)
   int pre = 0;
   if (warp == 0 && lane == 0 && prefetch_ok) {
-    W.range(1);
+    W.range(ntu);
     pre = min(C::STAGES, W.it1 - W.it0);
     for (int i = 0; i < pre; ++i) {
       const int it = W.it0 + i;
@@ -123,19 +131,13 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
   pdl_wait();
   if (E.prof && threadIdx.x == 0) E.prof[blockIdx.x * 8 + 1] = globaltimer_ns();
   const int L = max(1, *lmax);
-  const int nrows = L * B;
-  const int ntu = min(n_tiles_max, (nrows + BN - 1) / BN);
+  const int nrows = L * S;  // live rows of every n-tile: L limbs of S slots
   W.range(ntu);
   if (E.rp && warp == 2 && lane == 0) {
     // Publish this rank's limb count before any arrival (finalisers read the
-    // max over ranks), then count the n-tiles this rank has no rows for, so
-    // every rank contributes n_tiles_max * nch arrivals per tile.
+    // max over ranks).
     for (int p = 0; p < E.npeers; ++p) atomicMax_system(E.peer_lmax[p], L);
     __threadfence_system();
-    const int virt = (n_tiles_max - ntu) * W.nch;
-    if (blockIdx.x == 0 && virt > 0)
-      for (int mt = 0; mt < W.Mt; ++mt)
-        for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + mt, virt);
   }
 
   if (warp == 0) {
@@ -158,7 +160,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
           ok = false;
           break;
         }
-        const int live = BN >= 64 ? min(BN, (min(BN, nrows - W.nt(it) * BN) + bbox - 1) / bbox * bbox) : BN;
+        const int live = BN >= 64 ? min(BN, (min(BN, nrows) + bbox - 1) / bbox * bbox) : BN;
         mbar_arrive_expect_tx(full(s), (Q4 ? Q4_TILE : C::A_BYTES) + live * BK);
         load_a(s, it);
         load_b(s, it, kx, live);
@@ -191,8 +193,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
           break;
         }
         tc_fence_after();
-        const int n0 = W.nt(it) * BN;
-        const int n_mma = (min(BN, nrows - n0) + 15) & ~15;
+        const int n_mma = (min(BN, nrows) + 15) & ~15;
         const uint32_t idesc = idesc_i8(BM, n_mma);
         const uint32_t dst = tmem + (uint32_t)(tb * C::ACC_COLS);
         for (int j = it; j < se; ++j, ++i) {
@@ -262,7 +263,8 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
     int seg = 0;
     for (int it = W.it0; it < W.it1; ++seg) {
       const int se = W.seg_end(it), tb = seg & 1;
-      const int nt = W.nt(it), mt = W.mt(it);
+      const int nt = MULTI ? W.nt(it) : 0, mt = MULTI ? W.mt(it) : it / W.nch, tl = MULTI ? W.tile(it) : mt;
+      const int sb0 = nt * S, nb = min(S, B - sb0);  // slots of this n-tile
       // One thread waits (bounded); the four warps then branch together, since
       // the named barriers below have no timeout of their own.
       if (warp == 2 && lane == 0) *ok_ptr = mbar_wait(seg_full(tb), (uint32_t)(seg >> 1) & 1u) ? 1 : 0;
@@ -276,19 +278,18 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       tc_fence_after();
       const int m = mt * BM + q * 32 + lane;
       const bool valid = m < M;
-      const int n0 = nt * BN;
-      const int n_mma = (min(BN, nrows - n0) + 15) & ~15;
+      const int n_mma = (min(BN, nrows) + 15) & ~15;
       const bool whole = (W.kc(it) == 0) && (se - it == W.nch);
-      const bool direct = whole && ntu == 1 && E.mode != PARTIAL && !E.rp;
+      const bool direct = whole && E.mode != PARTIAL && !E.rp;
       const uint32_t taddr = tmem + (uint32_t)(tb * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
       int need = 0;
-      if (BN >= 64 && direct && (B & 7) == 0) {
-        // 8 slots x L limbs per TMEM read batch (columns l * B + b0 .. + 7)
-        for (int b0 = 0; b0 < B; b0 += 8) {
+      if (BN >= 64 && direct && (nb & 7) == 0) {
+        // 8 slots x L limbs per TMEM read batch (tile columns l * S + s0 .. + 7)
+        for (int s0 = 0; s0 < nb; s0 += 8) {
           uint32_t r[8][8];
 #pragma unroll
           for (int l = 0; l < 8; ++l)
-            if (l < L) tmem_ld8(taddr + (uint32_t)(l * B + b0), r[l]);
+            if (l < L) tmem_ld8(taddr + (uint32_t)(l * S + s0), r[l]);
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -296,19 +297,20 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
 #pragma unroll
             for (int l = 0; l < 8; ++l)
               if (l < L) acc += (uint64_t)(int64_t)(int)r[l][j] << (8 * l);
-            apply_row(E, M, m, valid, b0 + j, acc, need);
+            apply_row(E, M, m, valid, sb0 + s0 + j, acc, need);
           }
         }
       } else if (direct) {
-        for (int b = 0; b < B; ++b) {
+        for (int s = 0; s < nb; ++s) {
           uint32_t r[8];
-          for (int l = 0; l < L; ++l) tmem_ld1(taddr + (uint32_t)(l * B + b), r[l]);
+          for (int l = 0; l < L; ++l) tmem_ld1(taddr + (uint32_t)(l * S + s), r[l]);
           tmem_ld_wait();
           uint64_t acc = 0;
           for (int l = 0; l < L; ++l) acc += (uint64_t)(int64_t)(int)r[l] << (8 * l);
-          apply_row(E, M, m, valid, b, acc, need);
+          apply_row(E, M, m, valid, sb0 + s, acc, need);
         }
-      } else {
+      } else if (!MULTI || ntu == 1) {
+        // one slot block: tile column c is partial row c
         for (int c0 = 0; c0 < n_mma; c0 += 16) {
           uint32_t r[16];
           tmem_ld16(taddr + (uint32_t)c0, r);
@@ -316,8 +318,35 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
           if (valid) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const int n = n0 + c0 + j;
+              const int n = c0 + j;
               if (n < nrows && r[j] != 0) {
+                if (E.rp) {
+                  for (int p = 0; p < E.npeers; ++p) red_add_s32(E.peer_P[p] + (size_t)n * M + m, (int)r[j]);
+                } else {
+                  red_add_s32(P + (size_t)n * M + m, (int)r[j]);
+                }
+              }
+            }
+          }
+        }
+      } else {
+        // tile column c = l * S + s holds partial row l * B + sb0 + s = c + l * (B - S) + sb0;
+        // l is advanced column by column (no division on the tail's critical path)
+        int lc = 0, sc = 0;
+        for (int c0 = 0; c0 < n_mma; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + (uint32_t)c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int c = c0 + j, l = lc, s = sc;
+            if (++sc == S) {
+              sc = 0;
+              ++lc;
+            }
+            const int n = c + l * (B - S) + sb0;
+            if (valid) {
+              if (c < nrows && s < nb && r[j] != 0) {
                 if (E.rp) {
                   for (int p = 0; p < E.npeers; ++p) red_add_s32(E.peer_P[p] + (size_t)n * M + m, (int)r[j]);
                 } else {
@@ -335,21 +364,21 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         __threadfence_system();
         epi_bar();
         if (warp == 2 && lane == 0)
-          for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + mt, se - it);
+          for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + tl, se - it);
       } else if (!direct && E.mode != PARTIAL) {
         __threadfence();
         epi_bar();
         if (warp == 2 && lane == 0) {
           const int add = se - it;
-          const int old = atomicAdd(tile_cnt + mt, add);
-          *flag_ptr = (old + add == ntu * W.nch) ? 1 : 0;
+          const int old = atomicAdd(tile_cnt + tl, add);
+          *flag_ptr = (old + add == W.nch) ? 1 : 0;
         }
         epi_bar();
         const bool last = *flag_ptr != 0;
         if (last) {
           __threadfence();
-          finalize_from_P<BN>(E, P, M, m, valid, B, L, need);
-          if (warp == 2 && lane == 0) tile_cnt[mt] = 0;
+          finalize_from_P<BN>(E, P, M, m, valid, B, L, need, sb0, sb0 + nb);
+          if (warp == 2 && lane == 0) tile_cnt[tl] = 0;
         }
         epi_bar();
       }
@@ -367,10 +396,12 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_sig[p], 1ull);
     }
     if (E.rp && E.mode != PARTIAL) {
-      // ---- finaliser: tiles mt = blockIdx.x (mod grid) of this rank's copy
-      const int target = E.npeers * n_tiles_max * W.nch;
-      for (int mt = blockIdx.x; mt < W.Mt; mt += gridDim.x) {
-        if (warp == 2 && lane == 0) *ok_ptr = wait_counter_geq(E.cnt_local + mt, target) ? 1 : 0;
+      // ---- finaliser: (m-tile, n-tile) t = blockIdx.x (mod grid) of this rank's copy
+      const int target = E.npeers * W.nch;
+      for (int t = blockIdx.x; t < W.Mt * ntu; t += gridDim.x) {
+        const int mt = t / ntu, nt = t - mt * ntu;
+        const int sb0 = nt * S, nb = min(S, B - sb0);
+        if (warp == 2 && lane == 0) *ok_ptr = wait_counter_geq(E.cnt_local + t, target) ? 1 : 0;
         epi_bar();
         const bool ok = *ok_ptr != 0;
         epi_bar();
@@ -383,9 +414,9 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         const int m = mt * BM + q * 32 + lane;
         const bool valid = m < M;
         int need = 0;
-        finalize_from_P<BN>(E, P, M, m, valid, B, Lf, need);
+        finalize_from_P<BN>(E, P, M, m, valid, B, Lf, need, sb0, sb0 + nb);
         epi_bar();
-        if (warp == 2 && lane == 0) E.cnt_local[mt] = 0;
+        if (warp == 2 && lane == 0) E.cnt_local[t] = 0;
       }
       if (E.prof && warp == 2 && lane == 0) E.prof[blockIdx.x * 8 + 5] = globaltimer_ns();
     }
@@ -410,17 +441,17 @@ static int num_sms() {
   return n;
 }
 
-template <int BN, bool Q4>
+template <int BN, bool Q4, bool MB = false>
 int launch(const CUtensorMap* a, const CUtensorMap* b, int M, int K, int B, const int* lmax, int* P, int* cnt,
            const Epi& E, cudaStream_t st, int pdl, const uint8_t* q4w) {
   using C = Cfg<BN, Q4>;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_fused<BN, Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_fused<BN, Q4, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return (int)e;
     attr = true;
   }
-  const int n_tiles_max = (8 * B + BN - 1) / BN;
+  const int n_tiles_max = (B + limb_slots(B) - 1) / limb_slots(B);  // slot blocks = n-tiles
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(E.max_ctas > 0 && E.max_ctas < num_sms() ? E.max_ctas : num_sms());
   cfg.blockDim = dim3(C::THREADS);
@@ -431,8 +462,8 @@ int launch(const CUtensorMap* a, const CUtensorMap* b, int M, int K, int B, cons
   at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_fused<BN, Q4>, *a, *b, M, K, B, n_tiles_max,
-                                     (int)(n_tiles_max == 1), lmax, P, cnt, E, q4w);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_fused<BN, Q4, MB>, *a, *b, M, K, B, n_tiles_max, 1, lmax, P, cnt,
+                                     E, q4w);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
@@ -440,9 +471,9 @@ int launch(const CUtensorMap* a, const CUtensorMap* b, int M, int K, int B, cons
 
 extern "C" {
 
-// Box height for the fused GEMM's limb operand: all 8 planes of B slots fit
-// one N tile up to B = 32 (so the work list is known before the dependency
-// wait and weight prefetch is allowed); larger batches tile N by 256.
+// N-tile height of the fused GEMM's limb operand: all 8 planes of B <= 32
+// slots in one tile; larger batches use 256-row tiles of 32-slot blocks
+// (limb_row layout), one tile per block.
 int arcb_fgemm_bn(int B) {
   const int want = 8 * B;
   if (want <= 16) return 16;
@@ -453,7 +484,9 @@ int arcb_fgemm_bn(int B) {
 }
 
 // Fused GEMM + epilogue.  `epi` points to an fg::Epi in host memory (copied
-// into the launch).  tile_cnt: zeroed int array with one entry per M tile.
+// into the launch).  tile_cnt: zeroed int array with one entry per (M tile,
+// N tile), ceil(M / 128) * ceil(B / 32) + 1 entries.  The limb operand uses
+// the limb_row layout (common.cuh); the partial buffer P has rows l * B + b.
 int arcb_fgemm(const void* tmA, const void* tmB, int M, int K, int B, int bn, const int* lmax, int* P,
                int* tile_cnt, const void* epi, int pdl, void* stream) {
   const CUtensorMap* a = (const CUtensorMap*)tmA;
@@ -467,7 +500,9 @@ int arcb_fgemm(const void* tmA, const void* tmB, int M, int K, int B, int bn, co
     case 32: return fg::launch<32, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
     case 64: return fg::launch<64, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
     case 128: return fg::launch<128, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
-    case 256: return fg::launch<256, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
+    case 256:
+      return B > 32 ? fg::launch<256, false, true>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr)
+                    : fg::launch<256, false, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
   }
   return -3;
 }
@@ -491,7 +526,9 @@ int arcb_fgemm_q4(const uint8_t* q4w, const void* tmB, int M, int K, int B, int 
     case 32: return fg::launch<32, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
     case 64: return fg::launch<64, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
     case 128: return fg::launch<128, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
-    case 256: return fg::launch<256, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
+    case 256:
+      return B > 32 ? fg::launch<256, true, true>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w)
+                    : fg::launch<256, true, false>(b, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, q4w);
   }
   return -3;
 }

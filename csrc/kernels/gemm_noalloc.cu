@@ -3,6 +3,8 @@
 // the reference.
 #include "gemm_noalloc.h"
 
+#include "common.cuh"
+
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -49,7 +51,7 @@ extern "C" int arcb_fgemm_noalloc(const void* tmA, const void* tmB, int M, int K
   // The epilogue descriptor starts with its mode; 0 is the partial-only mode.
   const int mode = *(const int*)epi;
   if (mode == 0) return ARCB_NOALLOC_ERR_MODE;
-  const long long tiles = (M + 127) / 128 + 1;
+  const long long tiles = (long long)((M + 127) / 128) * ((B + limb_slots(B) - 1) / limb_slots(B)) + 1;
   if (tiles > ARCB_NOALLOC_MAX_TILES + 1) return ARCB_NOALLOC_ERR_TOO_MANY_TILES;
   const long long partials = 8ll * B * (long long)M;
   if (partials > (long long)ARCB_NOALLOC_MAX_PARTIALS) return ARCB_NOALLOC_ERR_PARTIALS;

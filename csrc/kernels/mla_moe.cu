@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(HL_THREADS) k_mla_out(const int64_t* __restric
       const int n = limb_split8(v, dg);
       need = n > need ? n : need;
 #pragma unroll
-      for (int l = 0; l < 8; ++l) X[(size_t)l * B * d_out + off] = dg[l];
+      for (int l = 0; l < 8; ++l) X[limb_row(l, b0 + sl, B) * d_out + (size_t)h * dv + i] = dg[l];
     }
   }
   need = __reduce_max_sync(0xffffffffu, need);

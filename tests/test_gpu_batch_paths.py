@@ -15,23 +15,6 @@ from arc_chain_b200.oracle import arcref
 pytestmark = pytest.mark.gpu
 
 
-def _planes(x: np.ndarray, rows: int):
-    B, K = x.shape
-    planes = np.zeros((8, B, K), dtype=np.int8)
-    r = x.astype(np.int64).copy()
-    need = 0
-    for l in range(8):
-        d = (r & 0xFF).astype(np.uint8).view(np.int8)
-        planes[l] = d
-        r = (r - d.astype(np.int64)) >> 8
-        if np.any(planes[l] != 0):
-            need = l + 1
-    p = planes.reshape(8 * B, K)
-    if p.shape[0] < rows:
-        p = np.concatenate([p, np.zeros((rows - p.shape[0], K), np.int8)])
-    return p, max(need, 1)
-
-
 @pytest.mark.parametrize("B,mag", [(8, 1 << 17), (16, 1 << 40), (24, 1 << 12), (32, 1 << 20), (40, 1 << 17),
                                    (64, 1 << 23)])
 @pytest.mark.parametrize("ctas", ["tiles", "heuristic", 7, 0])
@@ -44,18 +27,18 @@ def test_fused_gemm_sub_box_and_cta_budget(B, mag, ctas):
     s = rng.integers(1, 5000, size=M).astype(np.int64)
     x = rng.integers(-mag, mag, size=(B, K), dtype=np.int64)
     bn = ops.fgemm_bn(B)
-    planes, need = _planes(x, max(8 * B, bn))
+    planes, need = ops.limb_planes(x, ops.limb_rows(B, bn))
     dev = torch.device("cuda")
     W, X, S = (torch.from_numpy(a).to(dev) for a in (w, planes, s))
     wm, xm = ops.TensorMap(ops.tile_weight(W), 128), ops.TensorMap(X, bn, min(bn, 32))
     lmax = torch.tensor([need], dtype=torch.int32, device=dev)
     P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
-    tiles = torch.zeros(M // 128 + 1, dtype=torch.int32, device=dev)
+    tiles = torch.zeros(ops.tile_counters(M, B), dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     out = torch.zeros(B, M, dtype=torch.int64, device=dev)
     ref = np.stack([arcref.matmul_i8(w, s, x[b]) for b in range(B)])
     e = ops.epi(ops.STORE, S, err, out=out, ldo=M)
-    e.max_ctas = {"tiles": M // 128, "heuristic": ops.split_ctas(M, B, bn)}.get(ctas, ctas)
+    e.max_ctas = {"tiles": (M // 128) * ops.n_tiles(B), "heuristic": ops.split_ctas(M, B, bn)}.get(ctas, ctas)
     for _ in range(2):
         out.zero_()
         ops.fgemm(wm, xm, M, K, B, lmax, P, tiles, e)

@@ -79,10 +79,8 @@ def test_fused_gemm_store_and_partial(M, K, B, mag):
     w = rng.integers(-127, 128, size=(M, K), dtype=np.int64).astype(np.int8)
     s = rng.integers(1, 5000, size=M).astype(np.int64)
     x = rng.integers(-mag, mag, size=(B, K), dtype=np.int64)
-    planes, need = _limbs(x, B, K)
     bn = ops.fgemm_bn(B)
-    if planes.shape[0] < bn:
-        planes = np.concatenate([planes, np.zeros((bn - planes.shape[0], K), np.int8)])
+    planes, need = ops.limb_planes(x, ops.limb_rows(B, bn))  # blocked limb layout for B > 32
     dev = torch.device("cuda")
     W, X, S = (torch.from_numpy(a).to(dev) for a in (w, planes, s))
     Wt = ops.tile_weight(W)
@@ -90,7 +88,7 @@ def test_fused_gemm_store_and_partial(M, K, B, mag):
     wm, xm = ops.TensorMap(Wt, 128), ops.TensorMap(X, bn)
     lmax = torch.tensor([need], dtype=torch.int32, device=dev)
     P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
-    tiles = torch.zeros((M + 127) // 128 + 1, dtype=torch.int32, device=dev)
+    tiles = torch.zeros(ops.tile_counters(M, B), dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     out = torch.zeros(B, M, dtype=torch.int64, device=dev)
     ref = np.stack([arcref.matmul_i8(w, s, x[b]) for b in range(B)])
@@ -218,17 +216,15 @@ def test_q4_gemm_exact(M, K, B):
     s = rng.integers(1, 5000, size=M).astype(np.int64)
     x = rng.integers(-(1 << 30), 1 << 30, size=(B, K), dtype=np.int64)
     weff = spec.q4g_effective(q, m)
-    planes, need = _limbs(x, B, K)
     bn = ops.fgemm_bn(B)
-    if planes.shape[0] < bn:
-        planes = np.concatenate([planes, np.zeros((bn - planes.shape[0], K), np.int8)])
+    planes, need = ops.limb_planes(x, ops.limb_rows(B, bn))
     dev = torch.device("cuda")
     packed = ops.pack_q4(torch.from_numpy(q).to(dev), torch.from_numpy(m).to(dev))
     X, S = torch.from_numpy(planes).to(dev), torch.from_numpy(s).to(dev)
     xm = ops.TensorMap(X, bn)
     lmax = torch.tensor([need], dtype=torch.int32, device=dev)
     P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
-    tiles = torch.zeros((M + 127) // 128 + 1, dtype=torch.int32, device=dev)
+    tiles = torch.zeros(ops.tile_counters(M, B), dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     out = torch.zeros(B, M, dtype=torch.int64, device=dev)
     ops.fgemm_q4(packed, xm, M, K, B, lmax, P, tiles, ops.epi(ops.STORE, S, err, out=out, ldo=M))
