@@ -119,6 +119,17 @@ def main():
                 r = bench_fgemm(M, K, a.B, a.iters, pdl=pdl)
                 r["name"] = name
                 print(json.dumps(r), flush=True)
+    if a.only == "large":
+        # 70B-architecture shapes at prefill / batched sizes: time and int8 tensor rate
+        shapes = {"70b_qkv": (10240, 8192), "70b_wo": (8192, 8192), "70b_gate_up": (57344, 8192),
+                  "70b_down": (8192, 28672)}
+        for B in (64, 256, 1024):
+            for name, (M, K) in shapes.items():
+                r = bench_fgemm(M, K, B, max(3, a.iters // 5), limbs=4)
+                r["name"] = name
+                r["int8_TOPS"] = round(2 * M * K * 4 * B / (r["us"] * 1e-6) / 1e12, 1)
+                print(json.dumps(r), flush=True)
+        return
     if a.only == "stream":
         # bulk-copy streaming probe: achievable weight-load bandwidth without MMA
         sizes = [int(x) << 20 for x in a.shape.split(",")] if a.shape else [2048]
