@@ -33,10 +33,12 @@ def hbm_peak_gbs() -> float:
         return 6650.0
 
 
-def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True, sub_box=None, ctas=None, limbs=3):
+def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True, sub_box=None, ctas=None, limbs=3, sched=0):
     """One fused GEMM alone.  sub_box: rows per TMA box of the limb operand
     (None = the whole BN tile); ctas: persistent CTA budget (None = the
-    split_ctas heuristic, 0 = one per SM); limbs: device limb count."""
+    split_ctas heuristic, 0 = one per SM); limbs: device limb count; sched:
+    work schedule of multi-n-tile launches (0 = round-robin / grouped, 1 =
+    plain stream-K)."""
     dev = torch.device("cuda")
     nbytes = M * K
     copies = max(2, -(-300_000_000 // nbytes))
@@ -53,6 +55,7 @@ def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True, sub_box=None, ctas=No
     out = torch.zeros(B, M, dtype=torch.int64, device=dev)
     e = ops.epi(ops.STORE if mode == "store" else ops.PARTIAL, S, err, out=out, ldo=M)
     e.max_ctas = ops.split_ctas(M, B, bn) if ctas is None else ctas
+    e.sched = sched
     ops.set_pdl(pdl)
     for i in range(5):
         ops.fgemm(maps[i % copies], xm, M, K, B, lmax, P, tiles, e)
@@ -67,12 +70,15 @@ def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True, sub_box=None, ctas=No
     gbs = nbytes / us / 1e3
     assert int(err.item()) == 0
     return {"kernel": "fgemm", "M": M, "K": K, "B": B, "mode": mode, "pdl": pdl, "sub_box": sub_box,
-            "ctas": e.max_ctas, "limbs": limbs, "us": round(us, 2),
+            "ctas": e.max_ctas, "limbs": limbs, "sched": sched, "us": round(us, 2),
             "GB_s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak_gbs(), 3)}
 
 
-def bench_attn(T, n_heads=32, dh=128, B=1, iters=50, cluster=None):
+def bench_attn(T, n_heads=32, dh=128, B=1, iters=50, cluster=None, paged=True):
+    """Decode attention over T cached tokens; paged selects the TMA-fed
+    page-ring form (else per-thread loads)."""
     dev = torch.device("cuda")
+    ops.set_attn_paged(paged)
     pages = (T + 15) // 16
     npg = pages * B
     K = torch.randint(-(1 << 18), 1 << 18, (npg, n_heads, 16, dh), dtype=torch.int64, device=dev)
@@ -94,7 +100,9 @@ def bench_attn(T, n_heads=32, dh=128, B=1, iters=50, cluster=None):
     torch.cuda.synchronize()
     us = t0.elapsed_time(t1) * 1000 / iters
     nbytes = 2 * B * T * n_heads * dh * 8
-    return {"kernel": "attn_cluster", "T": T, "heads": n_heads, "B": B, "us": round(us, 2),
+    ops.set_attn_paged(True)
+    return {"kernel": "attn_paged" if paged else "attn_cluster", "T": T, "heads": n_heads, "B": B, "us": round(us, 2),
+            "frac_of_measured_hbm": round(nbytes / us / 1e3 / hbm_peak_gbs(), 3),
             "GB_s": round(nbytes / us / 1e3, 1), "cluster": cluster or ops.attn_cluster_size(B, n_heads)}
 
 
@@ -125,10 +133,11 @@ def main():
                   "70b_down": (8192, 28672)}
         for B in (64, 256, 1024):
             for name, (M, K) in shapes.items():
-                r = bench_fgemm(M, K, B, max(3, a.iters // 5), limbs=4)
-                r["name"] = name
-                r["int8_TOPS"] = round(2 * M * K * 4 * B / (r["us"] * 1e-6) / 1e12, 1)
-                print(json.dumps(r), flush=True)
+                for sched in (0, 1):
+                    r = bench_fgemm(M, K, B, max(3, a.iters // 5), limbs=4, sched=sched)
+                    r["name"] = name
+                    r["int8_TOPS"] = round(2 * M * K * 4 * B / (r["us"] * 1e-6) / 1e12, 1)
+                    print(json.dumps(r), flush=True)
         return
     if a.only == "stream":
         # bulk-copy streaming probe: achievable weight-load bandwidth without MMA
@@ -168,7 +177,8 @@ def main():
     if a.only == "attn_cs":
         for T in (130, 386, 1024):
             for cs in (1, 2, 4, 8):
-                print(json.dumps(bench_attn(T, B=a.B, iters=a.iters, cluster=cs)), flush=True)
+                for paged in (True, False):
+                    print(json.dumps(bench_attn(T, B=a.B, iters=a.iters, cluster=cs, paged=paged)), flush=True)
         return
     if a.only == "batch":
         # sub-box limb loads and CTA budget across batch sizes
@@ -187,7 +197,8 @@ def main():
         return
     if a.only in ("", "attn"):
         for T in (130, 386, 1024, 2048):
-            print(json.dumps(bench_attn(T, B=a.B, iters=a.iters)), flush=True)
+            for paged in (True, False):
+                print(json.dumps(bench_attn(T, B=a.B, iters=a.iters, paged=paged)), flush=True)
 
 
 

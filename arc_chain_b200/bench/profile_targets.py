@@ -5,7 +5,7 @@ handful of times (a warm-up, then the launches to capture).
     python -m arc_chain_b200.bench.profile_targets <target>
 
 targets (kernel name to select, launches before the first timed one):
-  attn        k_attn_cluster   7B decode attention, T = 386, 32 heads    (3)
+  attn        k_attn_paged     7B decode attention, T = 386, 32 heads    (3)
   gemm_b1     k_gemm_fused     7B gate/up 22016 x 4096 at B = 1          (5)
   gemm_b256   k_gemm_fused     70B gate/up 57344 x 8192 at B = 256       (5)
   commit      k_batch_commit   BLAKE3 derive-key commit, 1M x 256 B      (1)

@@ -54,6 +54,7 @@ _SIGS = {
     "arcb_attn_mla": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, i64, i32, i32, i32, vp, vp, vp]),
     "arcb_moe_route": (i32, [vp, i32, i32, i32, i32, i32, vp, vp]),
     "arcb_set_pdl": (None, [i32]),
+    "arcb_set_attn_paged": (None, [i32]),
     "arcb_get_pdl": (i32, []),
 }
 

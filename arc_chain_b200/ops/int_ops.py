@@ -185,12 +185,12 @@ class Epi(C.Structure):
                 ("pt_stride", C.c_int), ("pos", C.c_void_p), ("rcos", C.c_void_p), ("rsin", C.c_void_p),
                 ("max_seq", C.c_int), ("X", C.c_void_p), ("ldx", C.c_int), ("lmax_out", C.c_void_p),
                 ("err", C.c_void_p), ("B", C.c_int),
-                ("rp", C.c_int), ("npeers", C.c_int), ("peer_P", C.c_void_p), ("peer_cnt", C.c_void_p),
-                ("peer_lmax", C.c_void_p), ("cnt_local", C.c_void_p), ("lmax_fin", C.c_void_p), ("prof", C.c_void_p),
+                ("rp", C.c_int), ("npeers", C.c_int), ("rank", C.c_int), ("peer_R", C.c_void_p),
+                ("peer_cnt", C.c_void_p), ("cnt_local", C.c_void_p), ("prof", C.c_void_p),
                 ("grp_rows", C.c_int), ("grp_koff", C.c_int), ("route", C.c_void_p), ("route_ld", C.c_int),
                 ("max_ctas", C.c_int), ("b_box", C.c_int), ("route_gs", C.c_int), ("peer_h", C.c_void_p),
                 ("peer_sig", C.c_void_p), ("pf_w", C.c_void_p), ("pf_M", C.c_int), ("pf_K", C.c_int),
-                ("pf_tiles", C.c_int)]
+                ("pf_tiles", C.c_int), ("sched", C.c_int)]
 
 
 PARTIAL, STORE, RESID, QKV, SWIGLU, MOE_COMBINE = 0, 1, 2, 3, 4, 5
@@ -221,6 +221,12 @@ def epi(mode, scales, err, **kw) -> Epi:
 
 def set_pdl(on: bool) -> None:
     lib().arcb_set_pdl(int(on))
+
+
+def set_attn_paged(on: bool) -> None:
+    """Decode attention for standard heads: TMA-fed page ring (True, the
+    default) or per-thread loads (False); identical results."""
+    lib().arcb_set_attn_paged(int(on))
 
 
 def tile_weight(w: torch.Tensor) -> torch.Tensor:
@@ -386,7 +392,7 @@ def split_ctas(M: int, B: int, bn: int) -> int:
 
 def linear_gemm(lin, xmap: TensorMap, B: int, lmax, P, tile_cnt, epi: Epi) -> None:
     """Dispatch a Linear (int8 tiles or Q4 tiles) to its fused GEMM."""
-    if epi.rp == 0 and not epi.peer_sig:  # cross-rank arrival counts assume the full grid
+    if not epi.peer_sig:  # expert-parallel arrival counts assume the full grid
         epi.max_ctas = min(num_sms(), split_ctas(lin.M, B, xmap.box_rows))
     if getattr(lin, "q4", None) is not None:
         fgemm_q4(lin.q4, xmap, lin.M, lin.K, B, lmax, P, tile_cnt, epi)

@@ -1,21 +1,24 @@
-"""Fused tensor-parallel communication: GEMM -> int32 limb-partial all-reduce
-inside the GEMM kernel, over NVLink peer memory.
+"""Fused tensor-parallel communication: GEMM -> all-reduce inside the GEMM
+kernel, over NVLink peer memory.
 
 For the row-parallel projections (W_o, W_down) every rank holds a K shard,
-so each output row needs the sum over ranks of the int32 per-limb partials
-before the limb recombination, scale and residual.  Instead of a separate
-collective, the fused GEMM (csrc/kernels/gemm_fused.cu, ``rp`` mode) adds
-each partial tile straight into every rank's P buffer with ``red.add`` on
-peer pointers of a symmetric allocation, then bumps every rank's per-tile
-arrival counter.  On each rank a designated CTA per tile waits (bounded; a
-timeout sets ARCB_ERR_COMM_TIMEOUT) until all ranks' chunks have arrived and
-finalises its own copy (residual add + next norm's sum of squares).  Integer
-sums are exact and order free, so every rank ends with the identical,
-reference-exact hidden state, and the transfer overlaps the MMA tile by tile.
+so each output row needs the sum over ranks of the partial dot products
+before the scale and residual.  Instead of a separate collective, the fused
+GEMM (csrc/kernels/gemm_fused.cu, ``rp`` mode) first sums the split-K limb
+partials of a tile in this GPU's own partial buffer, exactly as on one GPU.
+The CTA that completes the tile recombines its limbs and stores the wrapping
+int64 row sums (128 rows x slots: 1 KB per tile at batch 1) into this rank's
+slot of every rank's receive buffer with plain stores to peer memory, fences
+and adds 1 to every rank's arrival counter for the tile.  On each rank a
+designated CTA per tile waits (bounded; a timeout sets ARCB_ERR_COMM_TIMEOUT)
+for all ranks' arrivals, sums the slots and finalises its own copy (residual
+add + next norm's sum of squares).  Integer sums are exact and order free,
+so every rank ends with the identical, reference-exact hidden state; each
+tile crosses NVLink once per peer, as soon as it is complete.
 
 Two buffer sets (one for W_o, one for W_down) make reuse safe: a rank can be
 at most one row-parallel GEMM ahead of a peer.  Multicast is not used (only
-plain peer loads/stores/atomics), and no TMA reads peer memory.
+plain peer stores and atomics), and no TMA reads peer memory.
 
 Symmetric memory and peer mappings come from torch.distributed's
 symmetric-memory allocator; the logits all-gather stays on NCCL.
@@ -34,21 +37,19 @@ os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
 
 
 class _Site:
-    def __init__(self, n_p: int, n_cnt: int, device, group_name):
+    def __init__(self, n_slots: int, B: int, M: int, n_cnt: int, device, group_name):
         import torch.distributed._symmetric_memory as symm_mem
 
-        self.P = symm_mem.empty(n_p, dtype=torch.int32, device=device)
+        self.P = torch.zeros(8 * B * M, dtype=torch.int32, device=device)  # local split-K partials
+        self.R = symm_mem.empty(n_slots * B * M, dtype=torch.int64, device=device)
         self.cnt = symm_mem.empty(n_cnt, dtype=torch.int32, device=device)
-        self.lmax = symm_mem.empty(1, dtype=torch.int32, device=device)
-        for t in (self.P, self.cnt, self.lmax):
-            t.zero_()
-        hp = symm_mem.rendezvous(self.P, group_name)
+        self.R.zero_()
+        self.cnt.zero_()
+        hr = symm_mem.rendezvous(self.R, group_name)
         hc = symm_mem.rendezvous(self.cnt, group_name)
-        hl = symm_mem.rendezvous(self.lmax, group_name)
-        self._h = (hp, hc, hl)
-        self.peer_P = torch.tensor(list(hp.buffer_ptrs), dtype=torch.int64, device=device)
+        self._h = (hr, hc)
+        self.peer_R = torch.tensor(list(hr.buffer_ptrs), dtype=torch.int64, device=device)
         self.peer_cnt = torch.tensor(list(hc.buffer_ptrs), dtype=torch.int64, device=device)
-        self.peer_lmax = torch.tensor(list(hl.buffer_ptrs), dtype=torch.int64, device=device)
 
 
 class FusedComm(NcclComm):
@@ -63,7 +64,7 @@ class FusedComm(NcclComm):
     def _site(self, bb, site: int, M: int) -> _Site:
         key = (id(bb), site)
         if key not in self._sites:
-            self._sites[key] = _Site(8 * bb.B * M, ops.tile_counters(M, bb.B), bb.P.device, self.group_name)
+            self._sites[key] = _Site(self.size, bb.B, M, ops.tile_counters(M, bb.B), bb.P.device, self.group_name)
             torch.cuda.synchronize()
             dist.barrier(group=self.group)
         return self._sites[key]
@@ -76,11 +77,10 @@ class FusedComm(NcclComm):
             e = ops.Epi.from_buffer_copy(epi)
             e.rp = 1
             e.npeers = self.size
-            e.peer_P = s.peer_P.data_ptr()
+            e.rank = self.rank
+            e.peer_R = s.peer_R.data_ptr()
             e.peer_cnt = s.peer_cnt.data_ptr()
-            e.peer_lmax = s.peer_lmax.data_ptr()
             e.cnt_local = s.cnt.data_ptr()
-            e.lmax_fin = s.lmax.data_ptr()
             self._epis[key] = (e, epi)  # keep the source alive: its id is the key
         else:
             e = e[0]

@@ -47,17 +47,20 @@ struct Epi {
   int* lmax_out;
   int* err;
   int B;  // slots in the step (plane stride of X = B * ldx)
-  // Tensor-parallel push mode (rp = 1): partials go to every rank's P over
-  // NVLink (peer pointers of a symmetric allocation), arrivals to every
-  // rank's per-tile counters; tile mt is finalised on each rank by its CTA
-  // mt % gridDim.x once all ranks' chunks have arrived.
+  // Tensor-parallel reduce mode (rp = 1, row-parallel GEMMs): the split-K
+  // partials of a tile are summed in this GPU's P as in the one-GPU path;
+  // the CTA that completes the tile recombines its limbs and stores the
+  // wrapping int64 row sums into slot `rank` of every rank's receive buffer
+  // peer_R[p] ([npeers][B][M], peer pointers of a symmetric allocation),
+  // then adds 1 to every rank's arrival counter peer_cnt[p][tile].  Tile t
+  // is finalised on each rank by its CTA t % gridDim.x once cnt_local[t]
+  // reaches npeers: it sums the npeers slots and applies the epilogue.
   int rp;
   int npeers;
-  int* const* peer_P;
+  int rank;
+  int64_t* const* peer_R;
   int* const* peer_cnt;
-  int* const* peer_lmax;
   int* cnt_local;
-  int* lmax_fin;
   // optional per-CTA %globaltimer stamps [grid][8]: 0 entry, 1 after the
   // dependency wait, 2 first stage consumed, 3 last MMA issued, 4 epilogue
   // done, 5 finaliser done, 6 exit
@@ -94,6 +97,9 @@ struct Epi {
   // and the next GEMM's first stages hit L2.  null = off.
   const uint8_t* pf_w;
   int pf_M, pf_K, pf_tiles;
+  // Work schedule of launches with several n-tiles: 0 = round-robin whole
+  // tiles / n-tile groups (struct Work), 1 = plain stream-K.
+  int sched;
 };
 
 // Ring depth for decode-sized tiles (BN <= 32).  A 5-stage ring (two CTAs
@@ -221,9 +227,41 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
   }
 }
 
+// Tensor-parallel reduce mode: stores this rank's recombined sum of row m,
+// slot b into slot `rank` of every rank's receive buffer (plain stores to
+// peer memory; the caller fences and signals once the tile is complete).
+__device__ __forceinline__ void push_row(const Epi& E, int M, int B, int m, bool valid, int b, uint64_t acc) {
+  if (!valid) return;
+  const size_t off = ((size_t)E.rank * B + b) * M + m;
+  for (int p = 0; p < E.npeers; ++p) __stcg((long long*)(E.peer_R[p] + off), (long long)acc);
+}
+
+// The row's destination: every rank's receive buffer (rp) or the epilogue.
+__device__ __forceinline__ void emit_row(const Epi& E, int M, int B, int m, bool valid, int b, uint64_t acc,
+                                         int& need) {
+  if (E.rp) push_row(E, M, B, m, valid, b, acc);
+  else apply_row(E, M, m, valid, b, acc, need);
+}
+
+// Tensor-parallel finaliser: row m of slots [bb0, bb1) is the wrapping sum
+// of the npeers ranks' slots of this rank's receive buffer (exact, so the
+// order does not matter and every rank computes the same value).
+__device__ __forceinline__ void finalize_from_R(const Epi& E, int M, int m, bool valid, int B, int& need, int bb0,
+                                                int bb1) {
+  const int64_t* R = E.peer_R[E.rank];
+  for (int b = bb0; b < bb1; ++b) {
+    uint64_t acc = 0;
+    if (valid) {
+#pragma unroll 8
+      for (int r = 0; r < E.npeers; ++r) acc += (uint64_t)__ldcg((const long long*)(R + ((size_t)r * B + b) * M + m));
+    }
+    apply_row(E, M, m, valid, b, acc, need);
+  }
+}
+
 // Finalises row m of a split tile from the partial buffer P: reads and
 // clears its L x B int32 partials, recombines the limbs and applies the
-// epilogue.  Wide tiles (BN >= 64, i.e. batches of 8 or more) read 8 slots x
+// epilogue (or, in tensor-parallel reduce mode, pushes the sums).  Wide tiles (BN >= 64, i.e. batches of 8 or more) read 8 slots x
 // L limbs per round with every load in flight together; each load otherwise
 // waits for the previous clear, and a batch of 32 slots at 3 limbs would
 // serialise 96 L2 round trips.  Called by all lanes of a warp together.
@@ -252,7 +290,7 @@ __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int
         uint64_t acc = 0;
 #pragma unroll
         for (int l = 0; l < 8; ++l) acc += (uint64_t)(int64_t)v[l][j] << (8 * l);
-        apply_row(E, M, m, valid, b0 + j, acc, need);
+        emit_row(E, M, B, m, valid, b0 + j, acc, need);
       }
     }
     return;
@@ -265,7 +303,7 @@ __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int
         acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
         *p = 0;
       }
-    apply_row(E, M, m, valid, b, acc, need);
+    emit_row(E, M, B, m, valid, b, acc, need);
   }
 }
 
@@ -292,22 +330,83 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Work item -> (m-tile, n-tile, chunk), m-tile major: the n-tiles of one
-// weight tile are consecutive items, so CTAs working on them at the same time
-// share the weight tile through L2.  CTA c owns items [it0, it1).
+// Work item -> (m-tile, n-tile, chunk).  Three schedules:
+//
+// Stream-K (one n-tile): items are numbered tile by tile, chunk innermost,
+// and CTA c takes one balanced contiguous range.
+//
+// Several n-tiles, at least two waves of tiles (hybrid): the first `waves`
+// full waves are handed out whole and round-robin (CTA c runs tiles c,
+// c + grid, ..., tile = mt * ntu + nt), so at any moment the grid works on
+// about grid / ntu weight tiles, each shared through L2 by the CTAs on its
+// n-tiles; a contiguous range would walk the n-tiles of one weight tile on
+// a single CTA, re-reading it from DRAM once per n-tile.  The remaining
+// tiles (between one and two waves) are split stream-K.  Item numbers of
+// the round-robin part are [c * dpn, (c + 1) * dpn) for CTA c; the
+// stream-K part starts at dp_end = waves * grid * nch.
+//
+// Several n-tiles, fewer than two waves (grouped): the grid is cut into ntu
+// equal groups (grid / ntu CTAs each; the few CTAs left over get no items);
+// group g = c % ntu runs stream-K over the m-tiles of n-tile g, numbered
+// it = g * Mt * nch + mt * nch + chunk.  The CTAs of equal rank in different
+// groups walk the same (m-tile, chunk) sequence at the same time, so each
+// weight tile comes from DRAM once and is shared through L2.
+//
+// A round-robin tile starts at a CTA-dependent chunk `rot` and wraps (the
+// chunks' partial sums are exact, so their order does not matter): the
+// ntu CTAs on one weight tile, and the CTAs on one n-tile, then read any
+// given chunk at different moments within the tile's window instead of all
+// at once from one L2 location.  kpos(it) is the item's position in its
+// tile, kc(it) the chunk it loads.
 struct Work {
   int Mt, nch, it0, it1, ntu = 1;
-  __device__ void range(int ntu_) {
+  int dpn = 0, dp_end = 0, sk0 = 0, per = 0;  // per > 0: grouped (items per group)
+  int rot = 0;
+  __device__ void range(int ntu_, bool multi = false) {
     ntu = ntu_;
-    const long long total = (long long)ntu * Mt * nch;
-    it0 = (int)(total * blockIdx.x / gridDim.x);
-    it1 = (int)(total * (blockIdx.x + 1) / gridDim.x);
+    const long long T = (long long)ntu * Mt;
+    const int G = (int)gridDim.x, c = (int)blockIdx.x;
+    if (multi && ntu > 1 && T < 2LL * G && G >= ntu) {
+      const int Gg = G / ntu;  // CTAs per group
+      per = Mt * nch;
+      if (c >= Gg * ntu) {
+        it0 = it1 = sk0 = 0;
+        return;
+      }
+      const int g = c % ntu, r = c / ntu;
+      it0 = sk0 = g * per + (int)((long long)per * r / Gg);
+      it1 = g * per + (int)((long long)per * (r + 1) / Gg);
+      return;
+    }
+    int waves = multi && ntu > 1 ? (int)(T / G) - 1 : 0;
+    if (waves < 0) waves = 0;
+    dpn = waves * nch;
+    dp_end = waves * G * nch;
+    rot = (int)(((long long)(c % ntu) * max(1, nch / ntu) + (long long)(c / ntu) * 3) % nch);
+    const long long total = (T - (long long)waves * G) * nch;
+    sk0 = dp_end + (int)(total * c / G);
+    it1 = dp_end + (int)(total * (c + 1) / G);
+    it0 = dpn ? c * dpn : sk0;
   }
-  __device__ int nt(int it) const { return (it / nch) % ntu; }
-  __device__ int mt(int it) const { return it / (nch * ntu); }
-  __device__ int tile(int it) const { return it / nch; }  // (mt, nt) index = mt * ntu + nt
-  __device__ int kc(int it) const { return it % nch; }
-  __device__ int seg_end(int it) const { return min(it1, (it / nch + 1) * nch); }
+  // number of items of this CTA, and its i-th item
+  __device__ int count() const { return dpn + (it1 - sk0); }
+  __device__ int item(int i) const { return i < dpn ? it0 + i : sk0 + (i - dpn); }
+  // the item after a segment that ended at se
+  __device__ int next(int se) const { return (dpn && se == it0 + dpn) ? sk0 : se; }
+  __device__ int tile(int it) const {  // (mt, nt) index = mt * ntu + nt
+    if (per) return ((it % per) / nch) * ntu + it / per;
+    return it < dp_end ? (int)blockIdx.x + ((it - it0) / nch) * (int)gridDim.x : it / nch;
+  }
+  __device__ int nt(int it) const { return per ? it / per : tile(it) % ntu; }
+  __device__ int mt(int it) const { return per ? (it % per) / nch : tile(it) / ntu; }
+  __device__ int kpos(int it) const { return it % nch; }
+  __device__ int kc(int it) const {
+    const int k = it % nch;
+    return it < dp_end ? (k + rot < nch ? k + rot : k + rot - nch) : k;
+  }
+  __device__ int seg_end(int it) const {
+    return it < dp_end ? (it / nch + 1) * nch : min(it1, (it / nch + 1) * nch);
+  }
   // Weights are stored tiled: tile (m, k) is 128 rows x 128 bytes, contiguous,
   // at row (m * nch + k) * 128 of a [Mt * nch * 128, 128] byte matrix, so one
   // TMA box is one contiguous 16 KB DRAM block.

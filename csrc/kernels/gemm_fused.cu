@@ -120,10 +120,10 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
   const int ntu = MULTI ? n_tiles_max : 1;  // = ceil(B / S)
   int pre = 0;
   if (warp == 0 && lane == 0 && prefetch_ok) {
-    W.range(ntu);
-    pre = min(C::STAGES, W.it1 - W.it0);
+    W.range(ntu, MULTI && E.sched == 0);
+    pre = min(C::STAGES, W.count());
     for (int i = 0; i < pre; ++i) {
-      const int it = W.it0 + i;
+      const int it = W.item(i);
       mbar_arrive_expect_tx(full(i), C::STAGE_BYTES);
       load_a(i, it);
     }
@@ -132,22 +132,16 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
   if (E.prof && threadIdx.x == 0) E.prof[blockIdx.x * 8 + 1] = globaltimer_ns();
   const int L = max(1, *lmax);
   const int nrows = L * S;  // live rows of every n-tile: L limbs of S slots
-  W.range(ntu);
-  if (E.rp && warp == 2 && lane == 0) {
-    // Publish this rank's limb count before any arrival (finalisers read the
-    // max over ranks).
-    for (int p = 0; p < E.npeers; ++p) atomicMax_system(E.peer_lmax[p], L);
-    __threadfence_system();
-  }
+  W.range(ntu, MULTI && E.sched == 0);
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      const int n = W.it1 - W.it0;
+      const int n = W.count();
       int issued = 0;
       bool ok = true;
       for (int i = 0; i < n; ++i) {
-        const int it = W.it0 + i, s = i % C::STAGES;
+        const int it = W.item(i), s = i % C::STAGES;
         const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
         const int kx = W.kc(it) * BK + (E.grp_koff ? (W.mt(it) * BM / E.grp_rows) * E.grp_koff : 0);
         if (i < pre) {  // its transaction count (full box) was set before the dependency wait
@@ -186,7 +180,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       // ---------------- MMA issuer
       int i = 0, seg = 0;
       bool ok = true;
-      for (int it = W.it0; it < W.it1 && ok; ++seg) {
+      for (int it = W.item(0); it < W.it1 && ok; ++seg) {
         const int se = W.seg_end(it), tb = seg & 1;
         if (seg >= 2 && !mbar_wait(seg_free(tb), (uint32_t)((seg >> 1) - 1) & 1u)) {
           set_error(E.err, ARCB_ERR_TIMEOUT_DONE);
@@ -215,13 +209,13 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         }
         mma_commit(seg_full(tb));
         if (E.prof) E.prof[blockIdx.x * 8 + 3] = globaltimer_ns();
-        it = se;
+        it = W.next(se);
       }
     }
   } else if (Q4 && warp >= 6) {
     // ---------------- Q4 converter warps 6..9: packed tile -> swizzled int8 A
     const int r = threadIdx.x - 192;  // tile row
-    const int n = W.it1 - W.it0;
+    const int n = W.count();
     for (int i = 0; i < n; ++i) {
       const int s = i % C::STAGES;
       if (!mbar_wait(full(s), (uint32_t)(i / C::STAGES) & 1u)) {
@@ -261,7 +255,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
     // ---------------- epilogue warps 2..5
     const int q = warp & 3;
     int seg = 0;
-    for (int it = W.it0; it < W.it1; ++seg) {
+    for (int it = W.item(0); it < W.it1; ++seg) {
       const int se = W.seg_end(it), tb = seg & 1;
       const int nt = MULTI ? W.nt(it) : 0, mt = MULTI ? W.mt(it) : it / W.nch, tl = MULTI ? W.tile(it) : mt;
       const int sb0 = nt * S, nb = min(S, B - sb0);  // slots of this n-tile
@@ -279,8 +273,8 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       const int m = mt * BM + q * 32 + lane;
       const bool valid = m < M;
       const int n_mma = (min(BN, nrows) + 15) & ~15;
-      const bool whole = (W.kc(it) == 0) && (se - it == W.nch);
-      const bool direct = whole && E.mode != PARTIAL && !E.rp;
+      const bool whole = (W.kpos(it) == 0) && (se - it == W.nch);
+      const bool direct = whole && E.mode != PARTIAL;
       const uint32_t taddr = tmem + (uint32_t)(tb * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
       int need = 0;
       if (BN >= 64 && direct && (nb & 7) == 0) {
@@ -297,7 +291,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
 #pragma unroll
             for (int l = 0; l < 8; ++l)
               if (l < L) acc += (uint64_t)(int64_t)(int)r[l][j] << (8 * l);
-            apply_row(E, M, m, valid, sb0 + s0 + j, acc, need);
+            emit_row(E, M, B, m, valid, sb0 + s0 + j, acc, need);
           }
         }
       } else if (direct) {
@@ -307,7 +301,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
           tmem_ld_wait();
           uint64_t acc = 0;
           for (int l = 0; l < L; ++l) acc += (uint64_t)(int64_t)(int)r[l] << (8 * l);
-          apply_row(E, M, m, valid, sb0 + s, acc, need);
+          emit_row(E, M, B, m, valid, sb0 + s, acc, need);
         }
       } else if (!MULTI || ntu == 1) {
         // one slot block: tile column c is partial row c
@@ -319,13 +313,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int n = c0 + j;
-              if (n < nrows && r[j] != 0) {
-                if (E.rp) {
-                  for (int p = 0; p < E.npeers; ++p) red_add_s32(E.peer_P[p] + (size_t)n * M + m, (int)r[j]);
-                } else {
-                  red_add_s32(P + (size_t)n * M + m, (int)r[j]);
-                }
-              }
+              if (n < nrows && r[j] != 0) red_add_s32(P + (size_t)n * M + m, (int)r[j]);
             }
           }
         }
@@ -346,13 +334,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
             }
             const int n = c + l * (B - S) + sb0;
             if (valid) {
-              if (c < nrows && s < nb && r[j] != 0) {
-                if (E.rp) {
-                  for (int p = 0; p < E.npeers; ++p) red_add_s32(E.peer_P[p] + (size_t)n * M + m, (int)r[j]);
-                } else {
-                  red_add_s32(P + (size_t)n * M + m, (int)r[j]);
-                }
-              }
+              if (c < nrows && s < nb && r[j] != 0) red_add_s32(P + (size_t)n * M + m, (int)r[j]);
             }
           }
         }
@@ -360,12 +342,8 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(seg_free(tb));
-      if (E.rp) {
-        __threadfence_system();
-        epi_bar();
-        if (warp == 2 && lane == 0)
-          for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + tl, se - it);
-      } else if (!direct && E.mode != PARTIAL) {
+      bool pushed = direct;  // rp: this CTA completed the tile and stored its sums
+      if (!direct && E.mode != PARTIAL) {
         __threadfence();
         epi_bar();
         if (warp == 2 && lane == 0) {
@@ -380,13 +358,21 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
           finalize_from_P<BN>(E, P, M, m, valid, B, L, need, sb0, sb0 + nb);
           if (warp == 2 && lane == 0) tile_cnt[tl] = 0;
         }
+        pushed = last;
         epi_bar();
+      }
+      if (E.rp && pushed) {
+        // the tile's sums are in every rank's receive buffer: signal each rank once
+        __threadfence_system();
+        epi_bar();
+        if (warp == 2 && lane == 0)
+          for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + tl, 1);
       }
       if (E.mode == SWIGLU && E.lmax_out) {
         need = __reduce_max_sync(0xffffffffu, need);
         if (lane == 0 && need > 0) atomicMax(E.lmax_out, need);
       }
-      it = se;
+      it = W.next(se);
     }
     if (E.prof && warp == 2 && lane == 0) E.prof[blockIdx.x * 8 + 4] = globaltimer_ns();
     if (E.peer_sig) {
@@ -397,7 +383,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
     }
     if (E.rp && E.mode != PARTIAL) {
       // ---- finaliser: (m-tile, n-tile) t = blockIdx.x (mod grid) of this rank's copy
-      const int target = E.npeers * W.nch;
+      const int target = E.npeers;  // one arrival per rank per tile
       for (int t = blockIdx.x; t < W.Mt * ntu; t += gridDim.x) {
         const int mt = t / ntu, nt = t - mt * ntu;
         const int sb0 = nt * S, nb = min(S, B - sb0);
@@ -410,11 +396,10 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
           continue;
         }
         __threadfence_system();
-        const int Lf = min(8, max(L, ld_acquire_sys(E.lmax_fin)));
         const int m = mt * BM + q * 32 + lane;
         const bool valid = m < M;
         int need = 0;
-        finalize_from_P<BN>(E, P, M, m, valid, B, Lf, need, sb0, sb0 + nb);
+        finalize_from_R(E, M, m, valid, B, need, sb0, sb0 + nb);
         epi_bar();
         if (warp == 2 && lane == 0) E.cnt_local[t] = 0;
       }

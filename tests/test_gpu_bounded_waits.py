@@ -31,20 +31,17 @@ def test_cross_rank_wait_times_out_cleanly():
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     h = torch.zeros(B, M, dtype=torch.int64, device=dev)
     P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
+    R = torch.zeros(2 * B * M, dtype=torch.int64, device=dev)
     cnt = torch.zeros(4, dtype=torch.int32, device=dev)
-    P_lost = torch.zeros_like(P)
+    R_lost = torch.zeros_like(R)
     cnt_lost = torch.zeros_like(cnt)  # a "peer" that never reports back
-    lm = torch.zeros(1, dtype=torch.int32, device=dev)
-    lm2 = torch.zeros(1, dtype=torch.int32, device=dev)
     tiles = torch.zeros(4, dtype=torch.int32, device=dev)
-    peerP = torch.tensor([P.data_ptr(), P_lost.data_ptr()], dtype=torch.int64, device=dev)
+    peerR = torch.tensor([R.data_ptr(), R_lost.data_ptr()], dtype=torch.int64, device=dev)
     peerC = torch.tensor([cnt.data_ptr(), cnt_lost.data_ptr()], dtype=torch.int64, device=dev)
-    peerL = torch.tensor([lm.data_ptr(), lm2.data_ptr()], dtype=torch.int64, device=dev)
     e = ops.epi(ops.RESID, S, err, out=h, ldo=M)
-    e.rp, e.npeers = 1, 2
-    e.peer_P, e.peer_cnt, e.peer_lmax = peerP.data_ptr(), peerC.data_ptr(), peerL.data_ptr()
-    e.cnt_local, e.lmax_fin = cnt.data_ptr(), lm.data_ptr()
-    # the local counter only ever sees this rank's half of the arrivals
+    e.rp, e.npeers, e.rank = 1, 2, 0
+    e.peer_R, e.peer_cnt, e.cnt_local = peerR.data_ptr(), peerC.data_ptr(), cnt.data_ptr()
+    # the local counter only ever sees this rank's own arrival, never the peer's
     t0 = time.time()
     ops.fgemm(wm, xm, M, K, B, lmax, P, tiles, e)
     torch.cuda.synchronize()
