@@ -50,7 +50,7 @@ def _run(cmd):
 
 def build_arcref(verbose=False) -> str:
     os.makedirs(LIBDIR, exist_ok=True)
-    srcs = [os.path.join(CSRC, "ref", f) for f in ("arcref.cpp", "blake3.cpp", "toy_engine.cpp")]
+    srcs = [os.path.join(CSRC, "ref", f) for f in ("arcref.cpp", "blake3.cpp", "toy_engine.cpp", "wgsl_forward.cpp")]
     out = os.path.join(LIBDIR, "libarcref.so")
     if _stale(out, srcs + _headers()):
         _run([CXX, *CXX_FLAGS, "-shared", "-o", out + ".tmp", *srcs])

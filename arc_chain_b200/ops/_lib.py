@@ -55,6 +55,14 @@ _SIGS = {
     "arcb_moe_route": (i32, [vp, i32, i32, i32, i32, i32, vp, vp]),
     "arcb_set_pdl": (None, [i32]),
     "arcb_set_attn_paged": (None, [i32]),
+    "arcb_wg_layernorm": (i32, [vp, i64, vp, i64, vp, i64, i32, vp]),
+    "arcb_wg_quantize": (i32, [vp, i64, vp, i64, vp, vp]),
+    "arcb_wg_matmul": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, vp, i64, vp]),
+    "arcb_wg_rope": (i32, [vp, i64, vp, vp, i64, i32, i32, i32, vp]),
+    "arcb_wg_attention": (i32, [vp, i64, vp, vp, i64, vp, vp, i64, vp, i64, i32, i32, i32, i32, i32, i32, vp]),
+    "arcb_wg_silu": (i32, [vp, vp, i64, vp]),
+    "arcb_wg_residual": (i32, [vp, vp, i64, vp]),
+    "arcb_wg_argmax": (i32, [vp, i64, vp, vp]),
     "arcb_get_pdl": (i32, []),
 }
 

@@ -67,6 +67,11 @@ def lib():
                 "arcref_merkle_root": (None, [vp, C.c_int64, C.c_char_p, C.c_size_t, vp]),
                 "arcref_rng_fill_i8": (None, [u64, u64, vp, i64]),
                 "arcref_rng_u64": (None, [u64, u64, vp, i64]),
+                "arcwg_new": (vp, [C.c_int] * 7 + [C.c_int32]),
+                "arcwg_free": (None, [vp]),
+                "arcwg_set_layer": (C.c_int, [vp, C.c_int, C.POINTER(vp), C.POINTER(vp), vp, vp]),
+                "arcwg_set_head": (C.c_int, [vp, vp, vp, vp, vp, vp, C.c_int]),
+                "arcwg_forward": (C.c_int, [vp, vp, C.c_int, vp]),
                 "arcref_num_threads": (C.c_int, []),
                 "arcref_set_threads": (None, [C.c_int]),
             }
