@@ -36,3 +36,44 @@ def quantize_f32(values: np.ndarray, n_rows: int, n_cols: int):
 def dequantize(data: np.ndarray, scales: np.ndarray) -> np.ndarray:
     """Approximate float view (value ~= data * scale / ONE), for inspection."""
     return data.astype(np.float64) * scales[:, None] / ONE
+
+
+def q4_engine_from_i8(data: np.ndarray, scales: np.ndarray):
+    """The reference's second Q4 format (crates/arc-inference/src/q4_engine.rs:
+    27-62, ``Q4Weights::from_i8``): per row q = ceil(absmax / 7), values
+    trunc(w / q) clamped to [-7, 7], packed two per byte (low nibble = even
+    column, stored biased by 8), scale s * max(q, 1).
+
+    Returns (packed uint8 [rows, cols / 2], scales int64).  Since
+    |trunc(w / ceil(absmax / 7))| <= 7 for every w of the row, the values
+    equal those of the per-row Q4 that the engine runs (``enable_q4``, clamp
+    [-8, 7]): the two formats differ only in the container."""
+    w = np.asarray(data, dtype=np.int8)
+    rows, cols = w.shape
+    if cols % 2:
+        raise ValueError("Q4 requires an even column count")
+    amax = np.maximum(np.abs(w.astype(np.int16)).max(axis=1), 1).astype(np.int64)
+    qpu = (amax + 6) // 7
+    v = w.astype(np.int64)
+    q = np.clip(np.sign(v) * (np.abs(v) // qpu[:, None]), -7, 7)
+    nib = (q + 8).astype(np.uint8)
+    packed = nib[:, 0::2] | (nib[:, 1::2] << 4)
+    return packed, np.asarray(scales, dtype=np.int64) * np.maximum(qpu, 1)
+
+
+def q4_engine_values(packed: np.ndarray) -> np.ndarray:
+    """Signed values [rows, 2 * packed cols] of a ``q4_engine_from_i8`` matrix."""
+    p = np.asarray(packed, dtype=np.uint8)
+    out = np.empty((p.shape[0], 2 * p.shape[1]), dtype=np.int8)
+    out[:, 0::2] = (p & 0x0F).astype(np.int8) - 8
+    out[:, 1::2] = (p >> 4).astype(np.int8) - 8
+    return out
+
+
+def matmul_q4_engine(packed: np.ndarray, scales: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """``matmul_q4`` (q4_engine.rs:71-97): (sum_j q_j x_j) * s >> 16 with
+    wrapping i64 arithmetic."""
+    q = q4_engine_values(packed).astype(np.int64)
+    with np.errstate(over="ignore"):
+        acc = (q * np.asarray(x, dtype=np.int64)[None, :]).sum(axis=1, dtype=np.int64)
+        return (acc * np.asarray(scales, dtype=np.int64)) >> 16

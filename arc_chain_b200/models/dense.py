@@ -194,17 +194,21 @@ def q4_row_host(m: Int8Model) -> Int8Model:
     return out
 
 
-def from_host(m: Int8Model, device, tp_rank: int = 0, tp_size: int = 1, q4: Optional[str] = None) -> DenseModel:
+def from_host(m: Int8Model, device, tp_rank: int = 0, tp_size: int = 1, q4: Optional[str] = None,
+              presharded: bool = False) -> DenseModel:
     """Upload an Int8Model (numpy) to the device, sharded for TP.
 
     q4=None keeps INT8; "row" applies the reference's per-row Q4 (every
     matrix including the LM head, as enable_q4 does); "group" the group-32
-    Q4 extension."""
+    Q4 extension.  presharded: `m` already holds rank tp_rank's slices
+    (formats/sharded.py), so nothing is sliced again."""
     if q4 == "row":
+        if presharded:
+            raise ValueError("per-row Q4 is applied before sharding: shard a q4_row_host model instead")
         dm = from_host(q4_row_host(m), device, tp_rank, tp_size)
         return to_q4(dm, "values")
     if q4 == "group":
-        return to_q4(from_host(m, device, tp_rank, tp_size), "group")
+        return to_q4(from_host(m, device, tp_rank, tp_size, presharded=presharded), "group")
     c = m.cfg
     check_tp(c, tp_size)
     dev = torch.device(device)
@@ -212,8 +216,8 @@ def from_host(m: Int8Model, device, tp_rank: int = 0, tp_size: int = 1, q4: Opti
     dh = c.d_head
     layers = []
     for L in m.layers:
-        r, s_ = tp_rank, tp_size
-        nhl, nkl = c.n_heads // s_, c.n_kv_heads // s_
+        r, s_ = (0, 1) if presharded else (tp_rank, tp_size)
+        nhl, nkl = c.n_heads // tp_size, c.n_kv_heads // tp_size
         wq, wk, wv = (_shard_rows(L[n], r, s_) for n in ("wq", "wk", "wv"))
         sq, sk, sv = (_shard_rows(L[n + "_s"], r, s_) for n in ("wq", "wk", "wv"))
         qkv = Linear(T(np.concatenate([interleave_heads(wq, nhl, dh), interleave_heads(wk, nkl, dh), wv])),
@@ -225,7 +229,7 @@ def from_host(m: Int8Model, device, tp_rank: int = 0, tp_size: int = 1, q4: Opti
         layers.append(DenseLayer(qkv.build_map(), wo.build_map(), gu.build_map(), down.build_map(),
                                  T(L["attn_norm"]), T(L["ffn_norm"])))
     lo, hi = _vocab_range(c.vocab, tp_rank, tp_size)
-    lm = Linear(T(m.out[lo:hi]), T(m.out_s[lo:hi])).build_map()
+    lm = Linear(T(m.out if presharded else m.out[lo:hi]), T(m.out_s if presharded else m.out_s[lo:hi])).build_map()
     q16 = getattr(m, "emb_q16", None)
     return DenseModel(c, int(m.attn_scale), T(m.emb), T(m.emb_s), lm, T(m.final_norm), T(m.rope_cos),
                       T(m.rope_sin), layers, tp_rank, tp_size, lo, emb_q16=None if q16 is None else T(q16))

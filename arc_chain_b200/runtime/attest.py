@@ -139,3 +139,71 @@ def tier_for_params(n_params: float) -> int:
 
 def needs_committee(tier: int) -> bool:
     return tier >= 2
+
+
+# Minimum stake per tier in base units (crates/arc-inference/src/lib.rs:61-68).
+TIER_MIN_STAKE = {1: 1_000, 2: 5_000, 3: 10_000, 4: 25_000}
+
+
+def tier_min_stake(tier: int) -> int:
+    return TIER_MIN_STAKE[int(tier)]
+
+
+def tier_max_params_b(tier: int) -> Optional[int]:
+    """Largest model (billions of parameters) a tier runs; None = unlimited."""
+    return {1: 20, 2: 50, 3: 100, 4: None}[int(tier)]
+
+
+def tier_from_u8(v: int) -> Optional[int]:
+    return int(v) if int(v) in TIER_MIN_STAKE else None
+
+
+# ------------------------------------------------------------------ errors
+# The reference's InferenceError variants (crates/arc-inference/src/lib.rs:22-42),
+# as exception classes with the same fields and messages.
+class InferenceError(Exception):
+    pass
+
+
+class ModelNotFound(InferenceError):
+    def __init__(self, model: str):
+        super().__init__(f"model not found: {model}")
+        self.model = model
+
+
+class ModelTooLarge(InferenceError):
+    def __init__(self, tier: int, size: int, max: int):
+        super().__init__(f"model too large for tier {tier}: {size} params, max {max}")
+        self.tier, self.size, self.max = tier, size, max
+
+
+class InferenceTimeout(InferenceError):
+    def __init__(self, elapsed_ms: int, limit_ms: int):
+        super().__init__(f"execution timeout: {elapsed_ms}ms > {limit_ms}ms")
+        self.elapsed_ms, self.limit_ms = elapsed_ms, limit_ms
+
+
+class DeterminismViolation(InferenceError):
+    def __init__(self):
+        super().__init__("determinism violation: output mismatch")
+
+
+class InsufficientStake(InferenceError):
+    def __init__(self, tier: int, have: int, need: int):
+        super().__init__(f"insufficient stake for tier {tier}: have {have}, need {need}")
+        self.tier, self.have, self.need = tier, have, need
+
+
+class RuntimeFailure(InferenceError):
+    def __init__(self, msg: str):
+        super().__init__(f"inference error: {msg}")
+
+
+def check_eligibility(tier: int, n_params: int, stake: int) -> None:
+    """Raises ModelTooLarge / InsufficientStake like the reference's tier checks."""
+    mx = tier_max_params_b(tier)
+    if mx is not None and n_params > mx * 1_000_000_000:
+        raise ModelTooLarge(tier, n_params, mx * 1_000_000_000)
+    need = tier_min_stake(tier)
+    if stake < need:
+        raise InsufficientStake(tier, stake, need)

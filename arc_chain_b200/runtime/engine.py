@@ -292,8 +292,11 @@ class Engine:
             self._scratch = self.new_request(1)
         return self._scratch
 
-    def prefill(self, rid: int, tokens: Sequence[int], start_pos: int = 0, chunk: int = 1024) -> None:
-        """Write KV for `tokens` at positions start_pos.. (logits discarded).
+    def prefill(self, rid: int, tokens: Sequence[int], start_pos: int = 0, chunk: int = 1024,
+                logits_sink=None) -> None:
+        """Write KV for `tokens` at positions start_pos.. .  Logits are
+        discarded unless `logits_sink` is given: it then receives, chunk by
+        chunk, the int64 Q16 logits [n, vocab] after each token (host copy).
 
         Chunks are padded to a power-of-two slot count; padding slots feed
         token 0 at position 0 of the scratch page, which no request reads."""
@@ -308,7 +311,23 @@ class Engine:
             bb.tokens.copy_(torch.tensor(part + [0] * pad, dtype=I32))
             bb.pos.copy_(torch.tensor(list(range(start_pos + s, start_pos + s + n)) + [0] * pad, dtype=I32))
             bb.pt.copy_(torch.tensor([row] * n + [srow] * pad, dtype=I32))
-            self.forward(bb, B, with_logits=False)
+            self.forward(bb, B, with_logits=logits_sink is not None)
+            if logits_sink is not None:
+                logits_sink(bb.logits[:n].cpu().numpy())
+
+    def score(self, tokens: Sequence[int], chunk: int = 256):
+        """Q16 logits [len(tokens), vocab] after each of `tokens`, fed from
+        position 0 as given (include the BOS yourself), as the reference's
+        forward_one_token returns them one by one; for perplexity."""
+        import numpy as np
+
+        out = []
+        rid = self.new_request(len(tokens) + 1)
+        try:
+            self.prefill(rid, tokens, chunk=chunk, logits_sink=out.append)
+        finally:
+            self.kv.release(rid)
+        return np.concatenate(out) if out else np.zeros((0, self.m.cfg.vocab), np.int64)
 
     def generate(self, prompt: Sequence[int], max_tokens: int, eos: Sequence[int] = (),
                  use_graph: bool = True) -> Tuple[List[int], bytes]:

@@ -32,7 +32,7 @@ import collections
 import json
 import time
 from dataclasses import dataclass, field
-from typing import Deque, Dict, List, Optional, Sequence
+from typing import Callable, Deque, Dict, List, Optional, Sequence
 
 import numpy as np
 import torch
@@ -61,7 +61,8 @@ class Request:
 
 class Scheduler:
     def __init__(self, engine: Engine, max_batch: int = 32, prefill_chunk: int = 1024,
-                 eos: Sequence[int] = (), gen_cap: Optional[int] = None, use_graph: bool = True):
+                 eos: Sequence[int] = (), gen_cap: Optional[int] = None, use_graph: bool = True,
+                 metrics_sink: Optional[Callable[[dict], None]] = None, keep_metrics: int = 10000):
         self.e = engine
         self.max_batch = max_batch
         self.prefill_chunk = prefill_chunk
@@ -76,7 +77,12 @@ class Scheduler:
         self._init_lanes()
         self.steps = 0
         self.tokens_out = 0
-        self.metrics: List[dict] = []
+        # per-step metrics: the last keep_metrics records, and every record
+        # to metrics_sink (e.g. a JSON-lines writer) when given
+        self.metrics: Deque[dict] = collections.deque(maxlen=keep_metrics)
+        self.metrics_sink = metrics_sink
+        self.finished = 0
+        self._t0 = None
         self.recoveries = 0
         self.max_recoveries = 3
 
@@ -156,10 +162,38 @@ class Scheduler:
 
     def step(self) -> int:
         """Admit, then one decode step over all lanes; returns active lanes."""
-        self._admit()
+        t0 = time.perf_counter()
+        if self._t0 is None:
+            self._t0 = t0
+        admitted = self._admit()
         active = sum(1 for x in self.lanes if x is not None)
         if active == 0:
             return 0
+        fin0 = self.finished
+        try:
+            return self._decode(active)
+        finally:
+            self._record(t0, admitted, active, self.finished - fin0)
+
+    def _record(self, t0: float, admitted: int, active: int, finished: int) -> None:
+        pool = self.e.kv.pool
+        m = {"step": self.steps, "active_lanes": active, "admitted": admitted, "finished": finished,
+             "waiting": len(self.waiting), "tokens_out": self.tokens_out, "kv_pages_used": pool.used,
+             "kv_pages_free": len(pool.free), "step_ms": round((time.perf_counter() - t0) * 1000, 3),
+             "recoveries": self.recoveries}
+        self.metrics.append(m)
+        if self.metrics_sink is not None:
+            self.metrics_sink(m)
+
+    def stats(self) -> dict:
+        """Totals since the first step (host clock)."""
+        el = time.perf_counter() - self._t0 if self._t0 else 0.0
+        return {"steps": self.steps, "tokens_out": self.tokens_out, "finished": self.finished,
+                "waiting": len(self.waiting), "active_lanes": sum(1 for x in self.lanes if x is not None),
+                "kv_pages_used": self.e.kv.pool.used, "recoveries": self.recoveries, "seconds": round(el, 3),
+                "tokens_per_s": round(self.tokens_out / el, 2) if el > 0 else 0.0}
+
+    def _decode(self, active: int) -> int:
         before = self.bb.count.cpu().numpy().copy()
         if self.use_graph:
             self.e._graph_for(self.bb).replay()
@@ -187,6 +221,7 @@ class Scheduler:
         r.t_done = time.perf_counter()
         self.e.kv.release(r.rid)
         self._close_lane(lane)
+        self.finished += 1
 
     # ------------------------------------------------------------ recovery and resume
     def _recover(self, counts_before) -> None:
