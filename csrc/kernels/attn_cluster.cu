@@ -211,7 +211,10 @@ __global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__
 // in flight from the start up to the ring depth, and the V pages arrive
 // while the cluster exchanges the max and the sum; the per-thread loops of
 // the plain form wait one DRAM round trip per key pair instead.
-constexpr int RING = 4;
+#ifndef ARCB_ATTN_RING
+#define ARCB_ATTN_RING 4
+#endif
+constexpr int RING = ARCB_ATTN_RING;
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
