@@ -442,8 +442,8 @@ def ep_wait_apply(cnt, epoch, per_call: int, h, delta, done, err) -> None:
     """Expert-parallel combine: bounded wait for this call's arrivals, then
     h += delta (wrapping) and delta = 0 (csrc/kernels/ep_ops.cu)."""
     _count()
-    check(lib().arcb_ep_wait_apply(_p(cnt), _p(epoch), per_call, _p(h), _p(delta), h.numel(), _p(done), _p(err),
-                                   _s()), "ep_wait_apply")
+    check(lib().arcb_ep_wait_apply(_p(cnt), _p(epoch), per_call, _p(h), _p(delta), 0 if h is None else h.numel(),
+                                   _p(done), _p(err), _s()), "ep_wait_apply")
 
 
 def set_prefetch(epi: Epi, next_lin, tiles: int) -> None:

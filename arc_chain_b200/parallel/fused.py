@@ -52,14 +52,72 @@ class _Site:
         self.peer_cnt = torch.tensor(list(hc.buffer_ptrs), dtype=torch.int64, device=device)
 
 
+class _Logits:
+    """Symmetric [B, vocab] logits buffer, every rank's pointer offset to
+    this rank's vocab columns, and the arrival counter of the gather."""
+
+    def __init__(self, B: int, V: int, lo: int, device, group_name):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.buf = symm_mem.empty(B * V, dtype=torch.int64, device=device)
+        self.cnt = symm_mem.empty(1, dtype=torch.int64, device=device)
+        self.buf.zero_()
+        self.cnt.zero_()
+        hb = symm_mem.rendezvous(self.buf, group_name)
+        hc = symm_mem.rendezvous(self.cnt, group_name)
+        self._h = (hb, hc)
+        self.peer = torch.tensor([p + lo * 8 for p in hb.buffer_ptrs], dtype=torch.int64, device=device)
+        self.peer_cnt = torch.tensor(list(hc.buffer_ptrs), dtype=torch.int64, device=device)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=device)
+        self.done = torch.zeros(1, dtype=torch.int32, device=device)
+        self.view = self.buf.view(B, V)
+        self.epi = None
+
+
 class FusedComm(NcclComm):
+    """fuse_logits: the LM head GEMM also stores its vocab slice into every
+    rank's logits buffer over NVLink (STORE epilogue with peer targets) and
+    a bounded arrival wait replaces the NCCL all-gather."""
+
     fused = True
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, fuse_logits: bool = False):
         super().__init__(group)
         self.group_name = (group or dist.group.WORLD).group_name
         self._sites = {}
         self._epis = {}
+        self.fuse_logits = fuse_logits
+        self._logits = {}
+
+    def _logit_state(self, bb, V: int, lo: int) -> _Logits:
+        key = id(bb)
+        if key not in self._logits:
+            self._logits[key] = _Logits(bb.B, V, lo, bb.P.device, self.group_name)
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+        return self._logits[key]
+
+    def lm_epi(self, epi, bb, V: int, lo: int):
+        """The LM head's epilogue descriptor (pushes into every rank when fused)."""
+        if not self.fuse_logits:
+            return epi
+        st = self._logit_state(bb, V, lo)
+        if st.epi is None:
+            e = ops.Epi.from_buffer_copy(epi)
+            e.ldo = V
+            e.npeers = self.size
+            e.peer_h = st.peer.data_ptr()
+            e.peer_sig = st.peer_cnt.data_ptr()
+            e.max_ctas = 0
+            st.epi = (e, epi)
+        return st.epi[0]
+
+    def gather_logits(self, local, full, B, vocab_offset, bb=None):
+        if not self.fuse_logits or bb is None or id(bb) not in self._logits:
+            return super().gather_logits(local, full, B, vocab_offset)
+        st = self._logits[id(bb)]
+        ops.ep_wait_apply(st.cnt, st.epoch, self.size * ops.num_sms(), None, None, st.done, bb.err)
+        full[:B].copy_(st.view[:B])
 
     def _site(self, bb, site: int, M: int) -> _Site:
         key = (id(bb), site)

@@ -46,7 +46,7 @@ class NcclComm(Comm):
         dist.all_reduce(P[:rows * M], op=dist.ReduceOp.SUM, group=self.group)
         dist.all_reduce(lmax, op=dist.ReduceOp.MAX, group=self.group)
 
-    def gather_logits(self, local, full, B, vocab_offset):
+    def gather_logits(self, local, full, B, vocab_offset, bb=None):
         Vl = local.shape[1]
         key = (B, Vl)
         if key not in self._gbuf:

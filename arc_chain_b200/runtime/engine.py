@@ -48,7 +48,7 @@ class Comm:
     def reduce_partials(self, P: torch.Tensor, rows: int, M: int, lmax: torch.Tensor) -> None:
         pass
 
-    def gather_logits(self, local: torch.Tensor, full: torch.Tensor, B: int, vocab_offset: int) -> None:
+    def gather_logits(self, local: torch.Tensor, full: torch.Tensor, B: int, vocab_offset: int, bb=None) -> None:
         pass
 
     def fgemm_reduce(self, lin, xmap, B: int, lmax: torch.Tensor, bb: "StepBuffers", epi, site: int = 0) -> None:
@@ -202,8 +202,9 @@ class Engine:
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
             ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
-            ops.linear_gemm(m.lm, bb.mXd, B, cf, bb.P, bb.tiles, E[-1]["lm"])
-            cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset)
+            lm_e = cm.lm_epi(E[-1]["lm"], bb, c.vocab, m.vocab_offset) if hasattr(cm, "lm_epi") else E[-1]["lm"]
+            ops.linear_gemm(m.lm, bb.mXd, B, cf, bb.P, bb.tiles, lm_e)
+            cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset, bb=bb)
 
     def _epis(self, bb: StepBuffers):
         """Epilogue descriptors of every fused GEMM of a forward over `bb`."""

@@ -58,6 +58,8 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--gen-len", type=int, default=256)
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
+    ap.add_argument("--fuse-logits", type=int, default=0,
+                    help="with --comm fused: the LM head also all-gathers its logits in-kernel")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", default="decode", choices=["decode", "batched", "moe", "specdec"],
                     help="decode: the headline 7B single-stream ms/token; batched: 70B-architecture continuous "
@@ -95,7 +97,7 @@ def main():
         if args.comm == "fused":
             from arc_chain_b200.parallel.fused import FusedComm
 
-            comm = FusedComm()
+            comm = FusedComm(fuse_logits=bool(args.fuse_logits))
     else:
         torch.cuda.set_device(0)
     local = int(os.environ.get("LOCAL_RANK", "0"))

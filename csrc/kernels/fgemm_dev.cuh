@@ -84,9 +84,11 @@ struct Epi {
   // Expert parallelism: MOE_COMBINE reads route column g * route_gs of
   // local group g (route points at this rank's first expert column;
   // 0 = stride 1) and, with peer_h set, adds into the npeers targets
-  // peer_h[p] (every rank's combine buffer) instead of out; with peer_sig
-  // set every CTA, once its adds are fenced, increments every rank's
-  // arrival counter peer_sig[p] by one.
+  // peer_h[p] (every rank's combine buffer) instead of out.  STORE with
+  // peer_h set stores each row into every rank's buffer (the vocab-parallel
+  // LM head's all-gather; peer_h[p] already points at this rank's column
+  // offset).  With peer_sig set every CTA, once its writes are fenced,
+  // increments every rank's arrival counter peer_sig[p] by one.
   int route_gs;
   int64_t* const* peer_h;
   unsigned long long* const* peer_sig;
@@ -149,7 +151,14 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
   const int lane = threadIdx.x & 31;
   switch (E.mode) {
     case STORE:
-      if (valid) E.out[(size_t)b * E.ldo + m] = v;
+      if (valid) {
+        const size_t off = (size_t)b * E.ldo + m;
+        if (E.peer_h) {  // GEMM -> all-gather: the row lands in every rank's buffer
+          for (int p = 0; p < E.npeers; ++p) __stcg((long long*)(E.peer_h[p] + off), (long long)v);
+        } else {
+          E.out[off] = v;
+        }
+      }
       break;
     case RESID: {
       uint64_t sq = 0;

@@ -16,7 +16,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
+    ap.add_argument("--comm", default="fused", choices=["nccl", "fused", "fused-logits"])
     a = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -31,10 +31,10 @@ def main():
 
     rank, world = tp.init_distributed(timeout_s=60)
     comm = tp.NcclComm()
-    if a.comm == "fused":
+    if a.comm.startswith("fused"):
         from arc_chain_b200.parallel.fused import FusedComm
 
-        comm = FusedComm()
+        comm = FusedComm(fuse_logits=a.comm == "fused-logits")
     cfg = preset("tiny")
     if (cfg.d_ff // world) % 16:  # TP shards of the FFN must stay 16-byte rows
         cfg = dataclasses.replace(cfg, d_ff=768)
