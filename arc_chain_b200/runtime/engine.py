@@ -303,9 +303,9 @@ class Engine:
         token 0 at position 0 of the scratch page, which no request reads."""
         row = self.kv.table_row(rid)
         srow = self.kv.table_row(self.scratch_rid)
-        for s in range(0, len(tokens), chunk):
-            part = [int(t) for t in tokens[s:s + chunk]]
-            n = len(part)
+        s = 0
+        for n in self.prefill_chunks(len(tokens), chunk):
+            part = [int(t) for t in tokens[s:s + n]]
             B = self.bucket(n)
             bb = self.buffers(B)
             pad = B - n
@@ -315,6 +315,26 @@ class Engine:
             self.forward(bb, B, with_logits=logits_sink is not None)
             if logits_sink is not None:
                 logits_sink(bb.logits[:n].cpu().numpy())
+            s += n
+
+    @classmethod
+    def prefill_chunks(cls, n: int, chunk: int = 1024) -> List[int]:
+        """Chunk sizes for prefilling n tokens: full chunks, then the largest
+        power of two that fits while more than 64 tokens remain, then the
+        rest, so the power-of-two slot buckets pad little (600 tokens run as
+        512 + 64 + 24 in buckets of 512, 64 and 32 slots, not as one
+        1024-slot forward).  Any split gives the same exact KV."""
+        out = []
+        while n > 0:
+            if n >= chunk:
+                take = chunk
+            elif n > 64 and cls.bucket(n) != n:
+                take = 1 << (n.bit_length() - 1)
+            else:
+                take = n
+            out.append(take)
+            n -= take
+        return out
 
     def score(self, tokens: Sequence[int], chunk: int = 256):
         """Q16 logits [len(tokens), vocab] after each of `tokens`, fed from
