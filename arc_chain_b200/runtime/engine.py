@@ -92,6 +92,7 @@ class StepBuffers:
         # per-norm sum of squares: [2 * n_layers + 1, B] (u64 bits in int64)
         self.ss = torch.zeros(2 * c.n_layers + 1, B, dtype=I64, device=dev)
         self.err = torch.zeros(1, dtype=I32, device=dev)
+        self.nrm_cnt = torch.zeros(2, dtype=I32, device=dev)  # fused-norm tile / CTA counters
         self.logits_local = torch.zeros(B, model.vocab_local, dtype=I64, device=dev)
         self.logits = self.logits_local if model.tp_size == 1 else torch.zeros(B, c.vocab, dtype=I64, device=dev)
         # sampling state (one sampled slot per row)
@@ -129,6 +130,9 @@ class Engine:
         self.op_events = None
         # single-stream decode steps as one persistent kernel (runtime/decode_step.py)
         self.use_step_kernel = os.environ.get("ARCB_STEP_KERNEL", "0") == "1"
+        # RMSNorms fused into the preceding residual GEMM (W_o -> FFN norm,
+        # W_down -> next attention norm / final norm); set before the first forward
+        self.fuse_norm = os.environ.get("ARCB_FUSE_NORM", "0") == "1"
         self._step_progs = {}
 
     # ------------------------------------------------------------------ buffers
@@ -154,6 +158,7 @@ class Engine:
         ss = bb.ss
         E = self._epis(bb)
         reduce_in_kernel = cm.size == 1 or getattr(cm, "fused", False)
+        fused_norm = self._norm_fused()
         nv = torch.cuda.nvtx if self.nvtx else None
         ev = self.op_events
 
@@ -169,8 +174,9 @@ class Engine:
             e = E[l]
             if nv:
                 nv.range_push(f"layer {l} attention")
-            ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
-            mark("norm")
+            if l == 0 or not fused_norm:
+                ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
+                mark("norm")
             ops.linear_gemm(Ly.qkv, bb.mXd, B, c0, bb.P, bb.tiles, e["qkv"])
             mark("qkv")
             ops.attn(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo, c1,
@@ -186,8 +192,9 @@ class Engine:
             if nv:
                 nv.range_pop()
                 nv.range_push(f"layer {l} ffn")
-            ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
-            mark("norm")
+            if not fused_norm:
+                ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
+                mark("norm")
             ops.linear_gemm(Ly.gu, bb.mXd, B, c2, bb.P, bb.tiles, e["gu"])
             mark("gate_up")
             if reduce_in_kernel:
@@ -201,14 +208,15 @@ class Engine:
                 nv.range_pop()
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
-            ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
+            if not fused_norm:
+                ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
             lm_e = cm.lm_epi(E[-1]["lm"], bb, c.vocab, m.vocab_offset) if hasattr(cm, "lm_epi") else E[-1]["lm"]
             ops.linear_gemm(m.lm, bb.mXd, B, cf, bb.P, bb.tiles, lm_e)
             cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset, bb=bb)
 
     def _epis(self, bb: StepBuffers):
         """Epilogue descriptors of every fused GEMM of a forward over `bb`."""
-        if bb.epis is not None:
+        if bb.epis is not None and getattr(bb, "epis_norm", None) == self._norm_fused():
             return bb.epis
         m, c = self.m, self.m.cfg
         d, dh = c.d_model, c.d_head
@@ -226,6 +234,15 @@ class Engine:
                 "partial": ops.epi(ops.PARTIAL, Ly.wo.s, bb.err),
             })
         out.append({"lm": ops.epi(ops.STORE, m.lm.s, bb.err, out=bb.logits_local, ldo=m.lm.M)})
+        if self._norm_fused():
+            L = c.n_layers
+            for l, Ly in enumerate(m.layers):
+                nxt_gamma = m.layers[l + 1].attn_norm if l + 1 < L else m.final_norm
+                nxt_cnt = bb.cnt[4 * (l + 1):4 * (l + 1) + 1]  # = the final norm's counter after the last layer
+                for e, g, lm in ((out[l]["wo"], Ly.ffn_norm, bb.cnt[4 * l + 2:4 * l + 3]),
+                                 (out[l]["down"], nxt_gamma, nxt_cnt)):
+                    e.nrm_gamma, e.nrm_ngamma = g.data_ptr(), g.numel()
+                    e.nrm_X, e.nrm_lmax, e.nrm_cnt = bb.Xd.data_ptr(), lm.data_ptr(), bb.nrm_cnt.data_ptr()
         # each GEMM prefetches the first weight tiles of the next one in the step
         chain = []
         for l, Ly in enumerate(m.layers):
@@ -235,7 +252,13 @@ class Engine:
         for (e, _), (_, nxt) in zip(chain, chain[1:]):
             ops.set_prefetch(e, nxt, self.prefetch_tiles)
         bb.epis = out
+        bb.epis_norm = self._norm_fused()
         return out
+
+    def _norm_fused(self) -> bool:
+        """Norms run inside the residual GEMMs (needs the in-kernel reduce)."""
+        cm = self.comm
+        return bool(self.fuse_norm) and (cm.size == 1 or getattr(cm, "fused", False))
 
     def decode_step(self, bb: StepBuffers) -> None:
         """forward + sample for every slot; slots advance in place.  Single-

@@ -60,6 +60,8 @@ def main():
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
     ap.add_argument("--fuse-logits", type=int, default=0,
                     help="with --comm fused: the LM head also all-gathers its logits in-kernel")
+    ap.add_argument("--fuse-norm", type=int, default=-1,
+                    help="1: RMSNorms run inside the residual GEMMs; 0: separate kernels; -1: engine default")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", default="decode", choices=["decode", "batched", "moe", "specdec"],
                     help="decode: the headline 7B single-stream ms/token; batched: 70B-architecture continuous "
@@ -156,6 +158,8 @@ def main():
     log("weights ready")
     eng = Engine(model, max_seq=max_seq, comm=comm, n_pages=2 * ((max_seq + 15) // 16))
     eng.prefetch_tiles = args.prefetch
+    if args.fuse_norm >= 0:
+        eng.fuse_norm = bool(args.fuse_norm)
     if args.step_kernel >= 0:
         eng.use_step_kernel = bool(args.step_kernel)
     prompt = gen.seeded_prompt(args.prompt_len, cfg.vocab, 1)
@@ -245,7 +249,8 @@ def main():
                        "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
                        "l2": "weights per GPU >> 126 MB L2 (streamed from HBM every step)",
                        "prefetch_tiles": args.prefetch,
-                       "step_kernel": bool(eng.use_step_kernel),
+                       "step_kernel": bool(eng.use_step_kernel), "fuse_norm": bool(eng._norm_fused()),
+                       "fuse_logits": bool(getattr(comm, "fuse_logits", False)),
                        "tokens_per_s": round(1000.0 / ms_tok, 2)},
             "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches_per_step * K),
             "first_sequence": {"tokens": len(tokens_first),

@@ -102,6 +102,18 @@ struct Epi {
   // Work schedule of launches with several n-tiles: 0 = round-robin whole
   // tiles / n-tile groups (struct Work), 1 = plain stream-K.
   int sched;
+  // Fused RMSNorm of the updated residual (RESID mode; nrm_gamma = null:
+  // off).  Every finalised tile adds 1 to nrm_cnt[0]; once it reaches the
+  // tile count, each CTA normalises its share of out ([B, ldo], the hidden
+  // state) with the completed sums of squares ss_out, writes the next
+  // GEMM's limb planes nrm_X ([8 planes, ldo] in the limb_row layout) and
+  // raises nrm_lmax to their limb count.  nrm_cnt[1] counts CTAs done; the
+  // last resets both.  The wait is bounded (ARCB_ERR_TIMEOUT_DONE).
+  const int64_t* nrm_gamma;
+  int nrm_ngamma;
+  int8_t* nrm_X;
+  int* nrm_lmax;
+  int* nrm_cnt;
 };
 
 // Ring depth for decode-sized tiles (BN <= 32).  A 5-stage ring (two CTAs

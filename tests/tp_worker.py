@@ -16,7 +16,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--comm", default="fused", choices=["nccl", "fused", "fused-logits"])
+    ap.add_argument("--comm", default="fused", choices=["nccl", "fused", "fused-logits", "fused-norm"])
     a = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -34,13 +34,14 @@ def main():
     if a.comm.startswith("fused"):
         from arc_chain_b200.parallel.fused import FusedComm
 
-        comm = FusedComm(fuse_logits=a.comm == "fused-logits")
+        comm = FusedComm(fuse_logits=a.comm in ("fused-logits", "fused-norm"))
     cfg = preset("tiny")
     if (cfg.d_ff // world) % 16:  # TP shards of the FFN must stay 16-byte rows
         cfg = dataclasses.replace(cfg, d_ff=768)
     host = gen.random_model(cfg, 0)
     oracle = arcref.Model(host)
     eng = Engine(dense.from_host(host, "cuda", rank, world), comm=comm, n_pages=512, max_seq=256)
+    eng.fuse_norm = a.comm == "fused-norm"
     res = {"comm": a.comm, "world": world, "ok": True, "checks": 0}
     prompt = gen.seeded_prompt(32, cfg.vocab, 1)
     ref, rh = oracle.generate(prompt, 24)
