@@ -127,6 +127,10 @@ def main():
                 r = bench_fgemm(M, K, a.B, a.iters, pdl=pdl)
                 r["name"] = name
                 print(json.dumps(r), flush=True)
+    if a.only == "optimeline":
+        # per-op device time of one eager 7B decode step (CUDA events between launches)
+        print(json.dumps(op_timeline(fuse_norm=os.environ.get("ARCB_FUSE_NORM") == "1")), flush=True)
+        return
     if a.only == "large":
         # 70B-architecture shapes at prefill / batched sizes: time and int8 tensor rate
         shapes = {"70b_qkv": (10240, 8192), "70b_wo": (8192, 8192), "70b_gate_up": (57344, 8192),
@@ -242,3 +246,71 @@ def timeline_fgemm(M, K, B=1, reps=5):
 
 if __name__ == "__main__":
     main()
+
+
+def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -> dict:
+    """Mean device time of each op of one eager decode step of the 7B
+    architecture (events recorded between launches; the whole step is queued
+    behind a sleep so launch overhead is not timed), one rank per GPU when
+    launched under torch.distributed.run (fused in-kernel reduce)."""
+    import collections
+
+    import torch.distributed as dist
+
+    from arc_chain_b200.formats import gen
+    from arc_chain_b200.models import dense
+    from arc_chain_b200.models.config import preset
+    from arc_chain_b200.runtime.engine import Comm, Engine
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank, comm = 0, Comm()
+    if world > 1:
+        from arc_chain_b200.parallel import tp
+        from arc_chain_b200.parallel.fused import FusedComm
+
+        rank, world = tp.init_distributed()
+        comm = FusedComm()
+    else:
+        torch.cuda.set_device(0)
+    cfg = preset("llama7b")
+    cfg.max_seq = 400
+    m = dense.random_device(cfg, torch.device("cuda", torch.cuda.current_device()), seed=0, tp_rank=rank,
+                            tp_size=world)
+    eng = Engine(m, max_seq=400, comm=comm, n_pages=64)
+    eng.fuse_norm = fuse_norm
+    p = gen.seeded_prompt(prompt_len, cfg.vocab, 1)
+    rid = eng.new_request(prompt_len + 100)
+    eng.prefill(rid, [1] + p)
+    bb = eng.buffers(1, gen_cap=64)
+    eng._reset_sampling(bb, [rid], [p[-1]], [prompt_len + 1], ())
+    for _ in range(3):
+        eng.decode_step(bb)
+    agg, cnt = collections.defaultdict(float), collections.Counter()
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        eng.op_events = []
+        torch.cuda._sleep(80_000_000)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        eng.decode_step(bb)
+        torch.cuda.synchronize()
+        prev = e0
+        for lab, e in eng.op_events:
+            agg[lab] += prev.elapsed_time(e) * 1000 / reps
+            cnt[lab] += 1
+            prev = e
+        eng.op_events = None
+    out = {"world": world, "fuse_norm": eng._norm_fused(), "total_us": round(sum(agg.values()), 1),
+           "per_op_us": {k: {"launches": cnt[k] // reps, "total": round(v, 1), "each": round(v / max(1, cnt[k] // reps), 2)}
+                         for k, v in agg.items()}}
+    if world > 1:
+        import gc
+
+        eng._graphs.clear()
+        gc.collect()
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
