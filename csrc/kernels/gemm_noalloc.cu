@@ -3,7 +3,7 @@
 // the reference.
 #include "gemm_noalloc.h"
 
-#include "common.cuh"
+#include "fgemm_dev.cuh"
 
 #include <cuda_runtime.h>
 
@@ -48,9 +48,10 @@ int scratch_for_current_device(int** out) {
 extern "C" int arcb_fgemm_noalloc(const void* tmA, const void* tmB, int M, int K, int B, int bn, const int* lmax,
                                   const void* epi, void* stream) {
   if (!tmA || !tmB || !lmax || !epi || M <= 0 || K <= 0 || B <= 0) return ARCB_NOALLOC_ERR_ARGS;
-  // The epilogue descriptor starts with its mode; 0 is the partial-only mode.
-  const int mode = *(const int*)epi;
-  if (mode == 0) return ARCB_NOALLOC_ERR_MODE;
+  // Partial-only mode leaves its result in the scratch array; the push and
+  // peer-target modes write other GPUs' buffers that the caller allocated.
+  const fg::Epi* E = (const fg::Epi*)epi;
+  if (E->mode == fg::PARTIAL || E->rp || E->peer_h || E->peer_sig) return ARCB_NOALLOC_ERR_MODE;
   const long long tiles = (long long)((M + 127) / 128) * ((B + limb_slots(B) - 1) / limb_slots(B)) + 1;
   if (tiles > ARCB_NOALLOC_MAX_TILES + 1) return ARCB_NOALLOC_ERR_TOO_MANY_TILES;
   const long long partials = 8ll * B * (long long)M;

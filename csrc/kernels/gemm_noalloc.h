@@ -33,9 +33,10 @@
 //   * Only the finalizing epilogue modes are accepted (store, residual,
 //     RoPE/KV, SwiGLU); the partial-only mode is rejected, because it leaves
 //     its result in the scratch array where the caller cannot read it.  The
-//     descriptor must also leave the tensor-parallel push mode off: that
-//     mode works on peer-mapped buffers the caller allocates, so it is not
-//     for callers of this entry point.
+//     descriptor must also leave the tensor-parallel push mode and every
+//     peer target (peer outputs, peer arrival counters) unset: those work on
+//     peer-mapped buffers that the caller allocates, so they are not for
+//     callers of this entry point, and are rejected the same way.
 #pragma once
 #include <stdint.h>
 
@@ -46,7 +47,7 @@
 // Return codes besides 0 (success) and positive CUDA error numbers.
 #define ARCB_NOALLOC_ERR_TOO_MANY_TILES (-20)   // M needs more than MAX_TILES tiles
 #define ARCB_NOALLOC_ERR_PARTIALS (-21)         // 8 * B * M > MAX_PARTIALS
-#define ARCB_NOALLOC_ERR_MODE (-22)             // partial-only / push mode requested
+#define ARCB_NOALLOC_ERR_MODE (-22)             // partial-only, push or peer-target mode requested
 #define ARCB_NOALLOC_ERR_SYMBOL (-23)           // cudaGetSymbolAddress failed
 #define ARCB_NOALLOC_ERR_ARGS (-24)             // non-positive sizes or null descriptors
 

@@ -6,8 +6,9 @@ library instead of buffers the caller passes.  This test calls it through
 its exported C symbol, twice in a row with different inputs, and requires
 each result to equal the regular entry point's (which gets torch-allocated
 scratch) exactly, the same tolerance the other kernel tests use.  It also
-checks that an oversized problem is refused.  The file is named so pytest
-collects it last.
+checks that an oversized problem, the partial-only mode and the push /
+peer-target modes are refused.  The file is named so pytest collects it
+last.
 """
 import ctypes as C
 
@@ -94,3 +95,9 @@ def test_noalloc_rejects_oversized_and_partial_mode():
     assert f(wm.addr, xm.addr, 4094 * 128 + 1, 128, 1, 16, lmax.data_ptr(), C.addressof(e), st) == -20
     p = ops.epi(ops.PARTIAL, S, err)
     assert f(wm.addr, xm.addr, 128, 128, 1, 16, lmax.data_ptr(), C.addressof(p), st) == -22
+    # push and peer-target modes write other GPUs' caller-allocated buffers: refused
+    # on the host before any launch (the pointers below are never dereferenced)
+    for field in ("rp", "peer_h", "peer_sig"):
+        q = ops.epi(ops.STORE, S, err, out=out, ldo=128)
+        setattr(q, field, 1 if field == "rp" else out.data_ptr())
+        assert f(wm.addr, xm.addr, 128, 128, 1, 16, lmax.data_ptr(), C.addressof(q), st) == -22, field
