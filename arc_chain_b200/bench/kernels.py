@@ -244,8 +244,6 @@ def timeline_fgemm(M, K, B=1, reps=5):
     return {"kernel": "fgemm_timeline", "M": M, "K": K, "B": B, "us_min_med_max": res[-1]}
 
 
-if __name__ == "__main__":
-    main()
 
 
 def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -> dict:
@@ -314,3 +312,7 @@ def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -
         dist.barrier()
         dist.destroy_process_group()
     return out
+
+
+if __name__ == "__main__":
+    main()
