@@ -178,6 +178,12 @@ def main():
                                           "tile": tile, "stages": stages, "grid": grid, "us": round(us, 2),
                                           "GB_s": round(nbytes / us / 1e3, 1), "err": int(err.item())}), flush=True)
         return
+    if a.only == "attn_batch":
+        # both attention forms across decode / batched / prefill-like grids
+        for B, heads, T in ((1, 32, 386), (8, 32, 386), (32, 32, 386), (64, 8, 512), (256, 8, 512), (512, 8, 256)):
+            for paged in (True, False):
+                print(json.dumps(bench_attn(T, n_heads=heads, B=B, iters=a.iters, paged=paged)), flush=True)
+        return
     if a.only == "attn_cs":
         for T in (130, 386, 1024):
             for cs in (1, 2, 4, 8):

@@ -194,7 +194,7 @@ class Epi(C.Structure):
                 ("nrm_X", C.c_void_p), ("nrm_lmax", C.c_void_p), ("nrm_cnt", C.c_void_p)]
 
 
-PARTIAL, STORE, RESID, QKV, SWIGLU, MOE_COMBINE = 0, 1, 2, 3, 4, 5
+PARTIAL, STORE, RESID, QKV, SWIGLU, MOE_COMBINE, STORE_PEERS = 0, 1, 2, 3, 4, 5, 6
 
 
 def fgemm_bn(B: int) -> int:

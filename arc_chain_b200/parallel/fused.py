@@ -104,6 +104,7 @@ class FusedComm(NcclComm):
         st = self._logit_state(bb, V, lo)
         if st.epi is None:
             e = ops.Epi.from_buffer_copy(epi)
+            e.mode = ops.STORE_PEERS
             e.ldo = V
             e.npeers = self.size
             e.peer_h = st.peer.data_ptr()

@@ -22,7 +22,10 @@ constexpr int NTHREADS = 192;
 constexpr int Q4_TILE = 128 * 64 + 128 * 2;
 constexpr int PAGE = 16;
 
-enum Mode : int { PARTIAL = 0, STORE = 1, RESID = 2, QKV = 3, SWIGLU = 4, MOE_COMBINE = 5 };
+// STORE_PEERS: STORE into every rank's buffer peer_h[p] (the vocab-parallel
+// LM head's all-gather); kept apart from STORE so the plain store stays one
+// instruction in the unrolled epilogue loops.
+enum Mode : int { PARTIAL = 0, STORE = 1, RESID = 2, QKV = 3, SWIGLU = 4, MOE_COMBINE = 5, STORE_PEERS = 6 };
 
 struct Epi {
   int mode;
@@ -84,8 +87,8 @@ struct Epi {
   // Expert parallelism: MOE_COMBINE reads route column g * route_gs of
   // local group g (route points at this rank's first expert column;
   // 0 = stride 1) and, with peer_h set, adds into the npeers targets
-  // peer_h[p] (every rank's combine buffer) instead of out.  STORE with
-  // peer_h set stores each row into every rank's buffer (the vocab-parallel
+  // peer_h[p] (every rank's combine buffer) instead of out.  STORE_PEERS
+  // stores each row into every rank's buffer peer_h[p] (the vocab-parallel
   // LM head's all-gather; peer_h[p] already points at this rank's column
   // offset).  With peer_sig set every CTA, once its writes are fenced,
   // increments every rank's arrival counter peer_sig[p] by one.
@@ -163,14 +166,11 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
   const int lane = threadIdx.x & 31;
   switch (E.mode) {
     case STORE:
-      if (valid) {
-        const size_t off = (size_t)b * E.ldo + m;
-        if (E.peer_h) {  // GEMM -> all-gather: the row lands in every rank's buffer
-          for (int p = 0; p < E.npeers; ++p) __stcg((long long*)(E.peer_h[p] + off), (long long)v);
-        } else {
-          E.out[off] = v;
-        }
-      }
+      if (valid) E.out[(size_t)b * E.ldo + m] = v;
+      break;
+    case STORE_PEERS:  // GEMM -> all-gather: the row lands in every rank's buffer
+      if (valid)
+        for (int p = 0; p < E.npeers; ++p) __stcg((long long*)(E.peer_h[p] + (size_t)b * E.ldo + m), (long long)v);
       break;
     case RESID: {
       uint64_t sq = 0;
@@ -257,10 +257,13 @@ __device__ __forceinline__ void push_row(const Epi& E, int M, int B, int m, bool
   for (int p = 0; p < E.npeers; ++p) __stcg((long long*)(E.peer_R[p] + off), (long long)acc);
 }
 
-// The row's destination: every rank's receive buffer (rp) or the epilogue.
+// The row's destination: every rank's receive buffer (PUSH, the rp mode) or
+// the epilogue.  Callers branch on E.rp once per tile and run a loop
+// instantiated for one of the two, so the unrolled loops carry one path.
+template <bool PUSH>
 __device__ __forceinline__ void emit_row(const Epi& E, int M, int B, int m, bool valid, int b, uint64_t acc,
                                          int& need) {
-  if (E.rp) push_row(E, M, B, m, valid, b, acc);
+  if constexpr (PUSH) push_row(E, M, B, m, valid, b, acc);
   else apply_row(E, M, m, valid, b, acc, need);
 }
 
@@ -286,12 +289,12 @@ __device__ __forceinline__ void finalize_from_R(const Epi& E, int M, int m, bool
 // L limbs per round with every load in flight together; each load otherwise
 // waits for the previous clear, and a batch of 32 slots at 3 limbs would
 // serialise 96 L2 round trips.  Called by all lanes of a warp together.
-template <int BN>
+template <int BN, bool PUSH = false>
 __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int m, bool valid, int B, int L,
                                                 int& need, int bb0 = 0, int bb1 = -1) {
   // slots [bb0, bb1) of the partial buffer (row l * B + b); the whole batch by default
   if (bb1 < 0) bb1 = B;
-  if (BN >= 64) {
+  if (BN >= 64 && !PUSH) {
     constexpr int FS = 4;  // slots per round: 4 x L loads in flight, no spills
     for (int b0 = bb0; b0 < bb1; b0 += FS) {
       int v[8][FS];
@@ -311,7 +314,7 @@ __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int
         uint64_t acc = 0;
 #pragma unroll
         for (int l = 0; l < 8; ++l) acc += (uint64_t)(int64_t)v[l][j] << (8 * l);
-        emit_row(E, M, B, m, valid, b0 + j, acc, need);
+        apply_row(E, M, m, valid, b0 + j, acc, need);
       }
     }
     return;
@@ -324,7 +327,7 @@ __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int
         acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
         *p = 0;
       }
-    emit_row(E, M, B, m, valid, b, acc, need);
+    emit_row<PUSH>(E, M, B, m, valid, b, acc, need);
   }
 }
 

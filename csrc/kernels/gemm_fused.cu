@@ -90,24 +90,26 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
   // path and the batched TMEM reads below exist for BN >= 64 only, so the
   // small-batch kernels keep their original code.
   const int bbox = (BN >= 64 && E.b_box > 0 && E.b_box < BN) ? E.b_box : BN;
-  auto load_b = [&](int s, int it, int kx, int rows) {
+  // b_row: first operand row of the item's n-tile; tile: weight tile index
+  // (m-tile * chunks + chunk) in the tiled weight layout.
+  auto load_b = [&](int s, int b_row, int kx, int rows) {
     if constexpr (BN >= 64) {
       for (int r0 = 0; r0 < rows; r0 += bbox)
-        tma_load_2d(b_base + s * C::B_BYTES + r0 * BK, &tmB, full(s), kx, W.nt(it) * BN + r0);
+        tma_load_2d(b_base + s * C::B_BYTES + r0 * BK, &tmB, full(s), kx, b_row + r0);
     } else {
-      tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, W.nt(it) * BN);
+      tma_load_2d(b_base + s * C::B_BYTES, &tmB, full(s), kx, b_row);
     }
   };
-  auto load_a = [&](int s, int it) {
+  auto load_a = [&](int s, int tile) {
     if constexpr (Q4) {
-      const uint8_t* src = q4w + (size_t)(W.mt(it) * W.nch + W.kc(it)) * Q4_TILE;
+      const uint8_t* src = q4w + (size_t)tile * Q4_TILE;
       asm volatile(
           "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
               q_base + s * C::Q_BYTES),
           "l"(src), "r"(Q4_TILE), "r"(full(s))
           : "memory");
     } else {
-      tma_load_2d(a_base + s * C::A_BYTES, &tmA, full(s), 0, W.tile_row(it));
+      tma_load_2d(a_base + s * C::A_BYTES, &tmA, full(s), 0, tile * BM);
     }
   };
   // Weights do not depend on the previous kernel: start streaming them.
@@ -125,7 +127,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
     for (int i = 0; i < pre; ++i) {
       const int it = W.item(i);
       mbar_arrive_expect_tx(full(i), C::STAGE_BYTES);
-      load_a(i, it);
+      load_a(i, W.mt(it) * W.nch + W.kc(it));
     }
   }
   pdl_wait();
@@ -137,28 +139,42 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      const int n = W.count();
-      int issued = 0;
+      // One thread issues every stage, so its per-stage work bounds the
+      // kernel at large batch (a 256-row stage is ~0.14 us of MMA): the item
+      // -> (tile, chunk) mapping is evaluated once per segment (tile) and
+      // the chunk, stage and parity then advance by increments.
+      const int live = BN >= 64 ? min(BN, (min(BN, nrows) + bbox - 1) / bbox * bbox) : BN;
+      const uint32_t tx_bytes = (Q4 ? Q4_TILE : C::A_BYTES) + live * BK;
+      int issued = 0, i = 0, s = 0;
+      uint32_t ph = 0;
       bool ok = true;
-      for (int i = 0; i < n; ++i) {
-        const int it = W.item(i), s = i % C::STAGES;
-        const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
-        const int kx = W.kc(it) * BK + (E.grp_koff ? (W.mt(it) * BM / E.grp_rows) * E.grp_koff : 0);
-        if (i < pre) {  // its transaction count (full box) was set before the dependency wait
-          load_b(s, it, kx, BN);
+      for (int it = W.item(0); it < W.it1 && ok; it = W.next(W.seg_end(it))) {
+        const int se = W.seg_end(it), mt_ = W.mt(it), nch = W.nch;
+        const int b_row = W.nt(it) * BN;
+        const int kx_off = E.grp_koff ? (mt_ * BM / E.grp_rows) * E.grp_koff : 0;
+        const int tile0 = mt_ * nch;
+        int kc = W.kc(it);
+        for (int j = it; j < se; ++j, ++i) {
+          const int kx = kc * BK + kx_off;
+          if (i < pre) {  // its transaction count (full box) was set before the dependency wait
+            load_b(s, b_row, kx, BN);
+          } else {
+            if (i >= C::STAGES && !mbar_wait(empty(s), ph ^ 1u)) {
+              set_error(E.err, ARCB_ERR_TIMEOUT_EMPTY);
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(full(s), tx_bytes);
+            load_a(s, tile0 + kc);
+            load_b(s, b_row, kx, live);
+          }
           ++issued;
-          continue;
+          if (++kc == nch) kc = 0;
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
-        if (i >= C::STAGES && !mbar_wait(empty(s), ph ^ 1u)) {
-          set_error(E.err, ARCB_ERR_TIMEOUT_EMPTY);
-          ok = false;
-          break;
-        }
-        const int live = BN >= 64 ? min(BN, (min(BN, nrows) + bbox - 1) / bbox * bbox) : BN;
-        mbar_arrive_expect_tx(full(s), (Q4 ? Q4_TILE : C::A_BYTES) + live * BK);
-        load_a(s, it);
-        load_b(s, it, kx, live);
-        ++issued;
       }
       if (!ok)
         for (int i = max(0, issued - C::STAGES); i < issued; ++i)
@@ -277,7 +293,11 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       const bool direct = whole && E.mode != PARTIAL;
       const uint32_t taddr = tmem + (uint32_t)(tb * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
       int need = 0;
-      if (BN >= 64 && direct && (nb & 7) == 0) {
+      // A tile covered by this CTA alone is recombined from TMEM; its rows go
+      // to the epilogue or, in the rp mode, to every rank's receive buffer.
+      // Only the epilogue form has the unrolled 8-slot batches (the push is
+      // the rare multi-GPU case), so the hot loops carry a single path.
+      if (BN >= 64 && direct && !E.rp && (nb & 7) == 0) {
         // 8 slots x L limbs per TMEM read batch (tile columns l * S + s0 .. + 7)
         for (int s0 = 0; s0 < nb; s0 += 8) {
           uint32_t r[8][8];
@@ -291,7 +311,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
 #pragma unroll
             for (int l = 0; l < 8; ++l)
               if (l < L) acc += (uint64_t)(int64_t)(int)r[l][j] << (8 * l);
-            emit_row(E, M, B, m, valid, sb0 + s0 + j, acc, need);
+            apply_row(E, M, m, valid, sb0 + s0 + j, acc, need);
           }
         }
       } else if (direct) {
@@ -301,7 +321,8 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
           tmem_ld_wait();
           uint64_t acc = 0;
           for (int l = 0; l < L; ++l) acc += (uint64_t)(int64_t)(int)r[l] << (8 * l);
-          emit_row(E, M, B, m, valid, sb0 + s, acc, need);
+          if (E.rp) push_row(E, M, B, m, valid, sb0 + s, acc);
+          else apply_row(E, M, m, valid, sb0 + s, acc, need);
         }
       } else if (!MULTI || ntu == 1) {
         // one slot block: tile column c is partial row c
@@ -355,7 +376,8 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         const bool last = *flag_ptr != 0;
         if (last) {
           __threadfence();
-          finalize_from_P<BN>(E, P, M, m, valid, B, L, need, sb0, sb0 + nb);
+          if (E.rp) finalize_from_P<BN, true>(E, P, M, m, valid, B, L, need, sb0, sb0 + nb);
+          else finalize_from_P<BN, false>(E, P, M, m, valid, B, L, need, sb0, sb0 + nb);
           if (warp == 2 && lane == 0) tile_cnt[tl] = 0;
         }
         pushed = last;
