@@ -21,7 +21,10 @@ at most one row-parallel GEMM ahead of a peer.  Multicast is not used (only
 plain peer stores and atomics), and no TMA reads peer memory.
 
 Symmetric memory and peer mappings come from torch.distributed's
-symmetric-memory allocator; the logits all-gather stays on NCCL.
+symmetric-memory allocator.  The vocab-parallel logits are all-gathered
+over NCCL by default; with ``fuse_logits`` the LM head GEMM stores its slice
+into every rank's logits buffer itself (STORE_PEERS epilogue) and a bounded
+arrival wait replaces the collective (exact at TP2, not yet timed).
 """
 from __future__ import annotations
 
