@@ -26,7 +26,9 @@ CXX = os.environ.get("CXX", "g++")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
                      "-Xptxas", "-warn-spills", "-I" + CSRC]
-CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-pthread", "-I" + CSRC]
+# no floating-point contraction: the host float paths restate Rust, which rounds
+# every product and sum separately
+CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-pthread", "-ffp-contract=off", "-I" + CSRC]
 
 
 def _headers():
@@ -50,7 +52,7 @@ def _run(cmd):
 
 def build_arcref(verbose=False) -> str:
     os.makedirs(LIBDIR, exist_ok=True)
-    srcs = [os.path.join(CSRC, "ref", f) for f in ("arcref.cpp", "blake3.cpp", "toy_engine.cpp", "wgsl_forward.cpp")]
+    srcs = [os.path.join(CSRC, "ref", f) for f in ("arcref.cpp", "blake3.cpp", "toy_engine.cpp", "wgsl_forward.cpp", "neuralnet.cpp")]
     out = os.path.join(LIBDIR, "libarcref.so")
     if _stale(out, srcs + _headers()):
         _run([CXX, *CXX_FLAGS, "-shared", "-o", out + ".tmp", *srcs])

@@ -72,6 +72,22 @@ def lib():
                 "arcwg_set_layer": (C.c_int, [vp, C.c_int, C.POINTER(vp), C.POINTER(vp), vp, vp]),
                 "arcwg_set_head": (C.c_int, [vp, vp, vp, vp, vp, vp, C.c_int]),
                 "arcwg_forward": (C.c_int, [vp, vp, C.c_int, vp]),
+                "arcref_save_file": (C.c_int, [vp, C.c_char_p, C.c_char_p, i64, C.c_char_p, C.c_int]),
+                "arcnn_parse": (vp, [C.c_char_p, C.c_size_t, C.c_char_p, C.c_int]),
+                "arcnn_new": (vp, []),
+                "arcnn_add_layer": (C.c_int, [vp, C.c_int, i64, i64, vp, vp, C.c_float]),
+                "arcnn_free": (None, [vp]),
+                "arcnn_tag_base": (C.c_int, [vp]),
+                "arcnn_num_layers": (i64, [vp]),
+                "arcnn_layer": (C.c_int, [vp, i64, C.POINTER(i64), C.POINTER(i64), C.POINTER(C.c_float)]),
+                "arcnn_layer_data": (i64, [vp, i64, C.c_int, vp, i64]),
+                "arcnn_input_size": (i64, [vp]),
+                "arcnn_output_size": (i64, [vp]),
+                "arcnn_serialize": (i64, [vp, C.c_int, vp, i64]),
+                "arcnn_output_len": (i64, [vp, i64]),
+                "arcnn_forward_f32": (i64, [vp, vp, i64, vp, i64]),
+                "arcnn_forward_q16": (i64, [vp, vp, i64, vp, i64]),
+                "arcnn_softmax_f32": (None, [vp, i64, vp]),
                 "arcref_num_threads": (C.c_int, []),
                 "arcref_set_threads": (None, [C.c_int]),
             }
@@ -189,6 +205,18 @@ class Model:
 
     def enable_q4(self):
         lib().arcref_enable_q4(self.h)
+
+    def save(self, path: str, vocab: Optional[List[str]] = None) -> None:
+        """Write the model as an ARC-INT8 v2 file (the reference's
+        ``save_weights`` bytes).  ``vocab`` None keeps the vocab of the file
+        the model was loaded from (an empty list for array-built models)."""
+        import json
+
+        vj = None if vocab is None else json.dumps(vocab, ensure_ascii=False, separators=(",", ":")).encode()
+        err = C.create_string_buffer(512)
+        rc = lib().arcref_save_file(self.h, path.encode(), vj, 0 if vj is None else len(vj), err, 512)
+        if rc != 0:
+            raise OSError(err.value.decode())
 
     def generate(self, prompt: Sequence[int], max_tokens: int, eos: Sequence[int] = ()) -> Tuple[List[int], bytes]:
         p = np.asarray(list(prompt), dtype=np.uint32)

@@ -262,6 +262,9 @@ struct arcref_model {
   void* map = nullptr;
   size_t map_len = 0;
   std::vector<int64_t> owned;  // aligned copies of i64 vectors from the file
+  // vocab JSON bytes of the loaded file, written back verbatim by
+  // arcref_save_file; "[]" (an empty list) when there is none
+  std::string vocab_json = "[]";
 };
 
 struct arcref_cache {
@@ -385,6 +388,12 @@ arcref_model* arcref_load_file(const char* path, char* err, int errlen) {
     arcref_free(m);
     return fail(e);
   }
+  // u64 length + vocab JSON; a missing or short tail leaves the empty list
+  if (len - r.off >= 8) {
+    uint64_t vl;
+    memcpy(&vl, r.p + r.off, 8);
+    if (len - r.off - 8 >= vl) m->vocab_json.assign((const char*)r.p + r.off + 8, (size_t)vl);
+  }
   // Resolve spans now that `owned` has stopped growing.
   size_t si = 0;
   auto vec_at = [&](Vec64& v) {
@@ -413,6 +422,53 @@ arcref_model* arcref_load_file(const char* path, char* err, int errlen) {
     vec_at(L.ffn_norm);
   }
   return m;
+}
+
+int arcref_save_file(const arcref_model* m, const char* path, const char* vocab_json,
+                     int64_t vocab_len, char* err, int errlen) {
+  FILE* f = fopen(path, "wb");
+  if (!f) {
+    if (err && errlen > 0) snprintf(err, errlen, "open failed: %s", path);
+    return -1;
+  }
+  bool ok = true;
+  auto put = [&](const void* p, size_t n) {
+    if (ok && n) ok = fwrite(p, 1, n, f) == n;
+  };
+  auto u64 = [&](uint64_t v) { put(&v, 8); };
+  auto vec = [&](const Vec64& v) {
+    u64((uint64_t)v.n);
+    put(v.p, (size_t)v.n * 8);
+  };
+  auto i8w = [&](const I8W& w) {
+    u64((uint64_t)w.rows);
+    u64((uint64_t)w.cols);
+    put(w.scales, (size_t)w.rows * 8);
+    put(w.data, (size_t)(w.rows * w.cols));
+  };
+  const arcref_config& c = m->cfg;
+  put("ARC-INT8\x02\x00", 10);
+  for (int64_t v : {c.n_layers, c.d_model, c.n_heads, c.n_kv_heads, c.d_ff, c.d_head, c.d_kv,
+                    c.vocab, c.max_seq})
+    u64((uint64_t)v);
+  u64((uint64_t)c.attn_scale);
+  vec(m->rope_cos);
+  vec(m->rope_sin);
+  i8w(m->emb);
+  i8w(m->out);
+  vec(m->final_norm);
+  for (const Layer& L : m->layers) {
+    for (const I8W* w : {&L.wq, &L.wk, &L.wv, &L.wo, &L.gate, &L.up, &L.down}) i8w(*w);
+    vec(L.attn_norm);
+    vec(L.ffn_norm);
+  }
+  const char* vj = vocab_json ? vocab_json : m->vocab_json.data();
+  const size_t vl = vocab_json ? (size_t)vocab_len : m->vocab_json.size();
+  u64((uint64_t)vl);
+  put(vj, vl);
+  ok = (fclose(f) == 0) && ok;
+  if (!ok && err && errlen > 0) snprintf(err, errlen, "write failed: %s", path);
+  return ok ? 0 : -1;
 }
 
 arcref_model* arcref_from_arrays(const arcref_config* cfg, const void* const* ptrs,

@@ -22,6 +22,16 @@ typedef struct arcref_cache arcref_cache;
 // and writes a message into `err` on failure.
 arcref_model* arcref_load_file(const char* path, char* err, int errlen);
 
+// Write the model as an ARC-INT8 v2 file, the bytes save_weights writes
+// (cached_integer_model.rs:1560-1595): header, RoPE tables, embedding and
+// output matrices, final norm, per layer 7 matrices and 2 norms, then u64
+// length + vocab JSON.  `vocab_json` (`vocab_len` UTF-8 bytes) is stored as
+// given; NULL stores the vocab bytes of the file the model was loaded from
+// ("[]" when there were none).  Q4 mode does not change what is written (the
+// INT8 weights).  Returns 0, or -1 with a message in `err`.
+int arcref_save_file(const arcref_model* m, const char* path, const char* vocab_json,
+                     int64_t vocab_len, char* err, int errlen);
+
 // Build a model over caller-owned arrays (not copied; they must outlive the
 // model).  `ptrs` order: emb_data, emb_scales, out_data, out_scales,
 // final_norm, rope_cos, rope_sin, then per layer wq, wq_s, wk, wk_s, wv, wv_s,

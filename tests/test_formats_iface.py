@@ -34,6 +34,33 @@ def test_arc_int8_v2_layout_and_roundtrip(tmp_path):
     assert a.generate([5, 6, 7], 6) == b.generate([5, 6, 7], 6)
 
 
+def test_native_arc_int8_writer(tmp_path):
+    """arcref_save_file writes the bytes the Python writer (and the
+    reference's save_weights) writes: from a loaded file, keeping its vocab
+    verbatim, and from caller arrays with a given vocab."""
+    m = gen.random_model(preset("micro"), 4)
+    m.vocab = ["<unk>", "<s>", "\u2581h\u00e9", 'q"\\', "\t"]
+    src, again, fresh = (str(tmp_path / n) for n in ("a.arc-int8", "b.arc-int8", "c.arc-int8"))
+    arc_int8.save(m, src)
+    raw = open(src, "rb").read()
+    arcref.Model(path=src).save(again)
+    assert open(again, "rb").read() == raw
+    arcref.Model(m).save(fresh, vocab=m.vocab)
+    assert open(fresh, "rb").read() == raw
+    # array-built model without a vocab: the empty list, still loadable
+    arcref.Model(m).save(fresh)
+    m2 = arc_int8.load(fresh)
+    assert m2.vocab == [] and m2.weight_hash() == m.weight_hash()
+    assert open(fresh, "rb").read()[-10:] == struct.pack("<Q", 2) + b"[]"
+    # Q4 mode changes what runs, not what is stored
+    q = arcref.Model(path=src)
+    q.enable_q4()
+    q.save(again)
+    assert open(again, "rb").read() == raw
+    with pytest.raises(OSError):
+        arcref.Model(m).save(str(tmp_path / "missing-dir" / "x.arc-int8"))
+
+
 def test_arc_int8_minor_version_byte_ignored(tmp_path):
     m = gen.random_model(preset("micro"), 1)
     p = str(tmp_path / "m.arc-int8")
