@@ -10,6 +10,8 @@ crates/arc-bench/src/*_bench.rs):
     python -m arc_chain_b200.cli convert SRC DST          # .gguf / .arc-int8 / .arc-int8v3
     python -m arc_chain_b200.cli shard MODEL OUTDIR --tp N
     python -m arc_chain_b200.cli serve [server options]
+    python -m arc_chain_b200.cli nn-run FILE (--text T | --tokens 1,2 | --embedding 0.5,1 | --image-file F)
+                                          [--integer]   # a NeuralNet / create_model.py file
 
 MODEL is a model preset name (random-init weights, ``--seed``) or a file.
 Every command prints one JSON object on stdout.
@@ -215,6 +217,42 @@ def cmd_shard(a) -> dict:
     return {"outdir": a.outdir, "manifest": man}
 
 
+def cmd_nn_run(a) -> dict:
+    """Runs a NeuralNet file (the VM's tagged f32 MLP format, or
+    create_model.py's) on the native library, as the VM engine's real
+    compute path does (crates/arc-vm/src/inference.rs:676-723).  With
+    --integer an embedding input runs through the integer form instead
+    (Q16 in and out)."""
+    from arc_chain_b200.formats import neuralnet
+    from arc_chain_b200.utils.hashing import blake3
+
+    raw = open(a.file, "rb").read()
+    net = neuralnet.NativeNet.from_bytes(raw)
+    res = {"file": a.file, "file_hash": blake3(raw).hex(), "tag_base": net.tag_base,
+           "input_size": net.input_size, "output_size": net.output_size}
+    if a.integer:
+        if a.embedding is None:
+            raise SystemExit("--integer takes an --embedding input")
+        x = [neuralnet._q16(float(v)) for v in a.embedding.split(",")]
+        res["output_q16"] = [int(v) for v in net.forward_q16(x)]
+        return res
+    if a.text is not None:
+        r = neuralnet.run_request(net, "text", a.text)
+    elif a.tokens is not None:
+        r = neuralnet.run_request(net, "tokens", [int(t) for t in a.tokens.split(",") if t])
+    elif a.embedding is not None:
+        r = neuralnet.run_request(net, "embedding", [float(v) for v in a.embedding.split(",") if v])
+    elif a.image_file is not None:
+        r = neuralnet.run_request(net, "image", open(a.image_file, "rb").read())
+    else:
+        raise SystemExit("give one of --text, --tokens, --embedding, --image-file")
+    out = r.output
+    if hasattr(out, "tolist"):
+        out = out.tolist()
+    res.update({"output": out, "tokens_used": r.tokens_used, "compute_time_ms": r.compute_time_ms, "cost": r.cost})
+    return res
+
+
 def main(argv=None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
     if argv and argv[0] == "serve":
@@ -260,9 +298,16 @@ def main(argv=None) -> int:
     p.add_argument("outdir")
     p.add_argument("--tp", type=int, required=True)
     p.add_argument("--seed", type=int, default=0)
+    p = sub.add_parser("nn-run")
+    p.add_argument("file")
+    p.add_argument("--text", default=None)
+    p.add_argument("--tokens", default=None)
+    p.add_argument("--embedding", default=None)
+    p.add_argument("--image-file", default=None)
+    p.add_argument("--integer", action="store_true", help="run the Q16 integer form on an --embedding input")
     a = ap.parse_args(argv)
     fn = {"info": cmd_info, "bench-int8": cmd_bench_int8, "generate": cmd_generate, "perplexity": cmd_perplexity,
-          "convert": cmd_convert, "shard": cmd_shard}[a.cmd]
+          "convert": cmd_convert, "shard": cmd_shard, "nn-run": cmd_nn_run}[a.cmd]
     print(json.dumps(fn(a), default=str))
     return 0
 

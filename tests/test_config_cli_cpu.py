@@ -54,6 +54,25 @@ def test_cli_info(capsys):
     assert r["model_id"] == attest.model_id_string(host.cfg)
 
 
+def test_cli_nn_run(capsys, tmp_path):
+    from arc_chain_b200.formats import neuralnet as nn
+
+    f = np.float32
+    layers = [nn.Layer("dense", W=np.array([[0.5, -0.3, 0.1, 0.2], [-0.1, 0.4, 0.3, -0.2]], f),
+                       b=np.zeros(2, f)), nn.Layer("relu"), nn.Layer("softmax")]
+    path = tmp_path / "clf.bin"
+    path.write_bytes(nn.write(layers, tag_base=1))  # create_model.py numbering
+    r = _run(capsys, "nn-run", str(path), "--embedding", "1,0.5,-0.5,0.2")
+    assert (r["tag_base"], r["input_size"], r["output_size"], r["tokens_used"]) == (1, 4, 2, 4)
+    want = nn.NativeNet.from_layers(layers).forward_f32(np.array([1, 0.5, -0.5, 0.2], f))
+    assert r["output"] == [float(v) for v in want]
+    r = _run(capsys, "nn-run", str(path), "--embedding", "1,0.5,-0.5,0.2", "--integer")
+    assert r["output_q16"] == [int(v) for v in nn.IntegerNet(layers).forward(
+        np.array([65536, 32768, -32768, 13107], np.int64))]
+    r = _run(capsys, "nn-run", str(path), "--text", "hi")
+    assert len(r["output"]) == 2 and r["tokens_used"] == 2
+
+
 def test_cli_bench_int8_roundtrip_and_determinism(capsys, tmp_path):
     path = str(tmp_path / "tiny.arc-int8")
     r = _run(capsys, "bench-int8", "tiny", "--device", "cpu", "--runs", "3", "--tokens", "4", "--save", path)
