@@ -253,3 +253,43 @@ def test_decode_text():
     # |v| * 100 in f32, saturating cast to u32, mod 128, +32 below 32
     v = np.array([0.0, -0.33, np.nan, np.inf, 0.5, 1.0, 0.05], f32)
     assert nn.decode_text(v) == " ! \x7f2d%"
+
+
+# ----------------------------------------------------------------- the VM's model registry
+def _mid(seed):
+    return bytes([seed]) + bytes(31)
+
+
+def test_engine_registry_rules():
+    from arc_chain_b200.runtime.nn_engine import EngineConfig, ModelInfo, NNEngine
+
+    raw = nn.write([dense([[0.5, -0.3, 0.1, 0.2], [-0.1, 0.4, 0.3, -0.2]], [0, 0]), Layer("relu")], tag_base=1)
+    eng = NNEngine(EngineConfig(max_loaded_models=2))
+    eng.load_model(_mid(1), ModelInfo("a"), raw)
+    with pytest.raises(ValueError, match="already loaded"):
+        eng.load_model(_mid(1), ModelInfo("a"), raw)
+    eng.load_model(_mid(2), ModelInfo("b"))  # registered without weights
+    with pytest.raises(ValueError, match=r"Maximum loaded models \(2\) reached"):
+        eng.load_model(_mid(3), ModelInfo("c"), raw)
+    with pytest.raises(ValueError, match="without weights"):
+        eng.run(_mid(2), "tokens", [1])
+    with pytest.raises(ValueError, match="Model not loaded"):
+        eng.run(_mid(9), "tokens", [1])
+    assert eng.unload_model(_mid(2)) and not eng.unload_model(_mid(2))
+    with pytest.raises(ValueError):  # bytes that parse under neither numbering: no mock
+        eng.load_model(_mid(4), ModelInfo("bad"), bytes([0xFF, 0xFE, 0xAB]))
+    assert eng.loaded_models() == [_mid(1)] and eng.model_status(_mid(1)) == "Ready"
+
+
+def test_engine_stats_accumulate():
+    from arc_chain_b200.runtime.nn_engine import ModelInfo, NNEngine
+
+    eng = NNEngine()
+    eng.load_model(_mid(8), ModelInfo("s"), nn.write([dense(np.eye(3), [0, 0, 0])]))
+    assert (eng.stats().total_inferences, eng.stats().total_tokens) == (0, 0)
+    r = eng.run(_mid(8), "tokens", [1, 2, 3])
+    assert r.output == [1, 2, 3] and (r.tokens_used, r.compute_time_ms, r.cost) == (3, 16, 15)
+    eng.run(_mid(8), "text", "hello")
+    s = eng.stats()
+    assert (s.total_inferences, s.total_tokens, s.avg_latency_ms) == (2, 8, (16 + 20) // 2)
+    assert eng.model_status(_mid(8)) == "Ready" and eng.models[_mid(8)].last_used == 2
