@@ -6,7 +6,6 @@ device work (max over ranks when distributed)."""
 from __future__ import annotations
 
 import time
-from typing import List
 
 import torch
 

@@ -23,10 +23,9 @@ block types are dequantised by the ``gguf`` package when it is installed.
 """
 from __future__ import annotations
 
-import math
 import struct
 from dataclasses import dataclass
-from typing import Dict, List, Optional, Tuple
+from typing import Dict, Tuple
 
 import numpy as np
 

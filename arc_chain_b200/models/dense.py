@@ -13,7 +13,7 @@ down by input columns, the LM head by vocab rows.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import List, Optional
 
 import numpy as np

@@ -7,7 +7,6 @@ library's kernels ran in a timed region.
 from __future__ import annotations
 
 import ctypes as C
-import math
 from typing import Optional
 
 import torch

@@ -8,7 +8,6 @@ use when the shared object is missing or stale.
 from __future__ import annotations
 
 import ctypes as C
-import os
 import threading
 from typing import List, Optional, Sequence, Tuple
 

@@ -20,8 +20,7 @@ from __future__ import annotations
 
 import json
 import time
-from dataclasses import dataclass
-from typing import Dict, List, Optional, Sequence
+from typing import List, Optional, Sequence
 
 
 class RankFailure(RuntimeError):

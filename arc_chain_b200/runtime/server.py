@@ -18,7 +18,7 @@ from __future__ import annotations
 import argparse
 import threading
 import time
-from typing import Dict, List, Optional
+from typing import List, Optional
 
 from arc_chain_b200.formats.tokenizer import Tokenizer
 from arc_chain_b200.runtime import attest

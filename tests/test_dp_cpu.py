@@ -7,7 +7,6 @@ import os
 import socket
 import time
 
-import pytest
 import torch.multiprocessing as mp
 
 from arc_chain_b200.parallel.dp import shard

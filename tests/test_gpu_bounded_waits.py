@@ -5,7 +5,6 @@ ARCB_ERR_COMM_TIMEOUT and returns; the context stays usable.  Out-of-range
 positions are reported (ARCB_ERR_SEQ_OVERFLOW) and skipped, never accessed."""
 import time
 
-import numpy as np
 import pytest
 
 torch = pytest.importorskip("torch")
