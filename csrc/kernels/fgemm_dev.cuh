@@ -294,7 +294,7 @@ __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int
                                                 int& need, int bb0 = 0, int bb1 = -1) {
   // slots [bb0, bb1) of the partial buffer (row l * B + b); the whole batch by default
   if (bb1 < 0) bb1 = B;
-  if (BN >= 64 && !PUSH) {
+  if constexpr (BN >= 64 && !PUSH) {
     constexpr int FS = 4;  // slots per round: 4 x L loads in flight, no spills
     for (int b0 = bb0; b0 < bb1; b0 += FS) {
       int v[8][FS];
@@ -317,17 +317,17 @@ __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int
         apply_row(E, M, m, valid, b0 + j, acc, need);
       }
     }
-    return;
-  }
-  for (int b = bb0; b < bb1; ++b) {
-    uint64_t acc = 0;
-    if (valid)
-      for (int l = 0; l < L; ++l) {
-        int* p = P + (size_t)(l * B + b) * M + m;
-        acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
-        *p = 0;
-      }
-    emit_row<PUSH>(E, M, B, m, valid, b, acc, need);
+  } else {
+    for (int b = bb0; b < bb1; ++b) {
+      uint64_t acc = 0;
+      if (valid)
+        for (int l = 0; l < L; ++l) {
+          int* p = P + (size_t)(l * B + b) * M + m;
+          acc += (uint64_t)(int64_t)__ldcg(p) << (8 * l);
+          *p = 0;
+        }
+      emit_row<PUSH>(E, M, B, m, valid, b, acc, need);
+    }
   }
 }
 
