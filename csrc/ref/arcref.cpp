@@ -34,12 +34,17 @@ class Pool {
  public:
   explicit Pool(int n) { resize(n); }
   ~Pool() { stop(); }
-  int size() const { return (int)workers_.size() + 1; }
+  int size() const { return threads_; }
+  // Not concurrent with parallel_for.  New workers start at the current job
+  // generation, so they wait for the next job instead of taking a finished
+  // one.
   void resize(int n) {
     stop();
     if (n < 1) n = 1;
     quit_ = false;
-    for (int i = 0; i < n - 1; ++i) workers_.emplace_back([this, i] { loop(i + 1); });
+    threads_ = n;
+    const uint64_t g = gen_;
+    for (int i = 0; i < n - 1; ++i) workers_.emplace_back([this, i, g] { loop(i + 1, g); });
   }
   // Runs f(lo, hi) over [0, n) split into size() contiguous ranges.
   void parallel_for(int64_t n, const std::function<void(int64_t, int64_t)>& f) {
@@ -68,8 +73,7 @@ class Pool {
     int64_t lo = idx * per, hi = std::min<int64_t>(n, lo + per);
     if (lo < hi) f(lo, hi);
   }
-  void loop(int idx) {
-    uint64_t seen = 0;
+  void loop(int idx, uint64_t seen) {
     for (;;) {
       const std::function<void(int64_t, int64_t)>* job;
       int64_t n;
@@ -100,6 +104,7 @@ class Pool {
   std::condition_variable cv_, done_cv_;
   const std::function<void(int64_t, int64_t)>* job_ = nullptr;
   int64_t n_ = 0;
+  int threads_ = 1;
   int pending_ = 0;
   uint64_t gen_ = 0;
   bool quit_ = false;
