@@ -44,18 +44,34 @@ def _stale(target: str, deps) -> bool:
 
 
 def _run(cmd):
-    r = subprocess.run(cmd, capture_output=True, text=True)
+    # a sanitizer runtime preloaded into the Python process is not the
+    # compiler's business
+    env = {k: v for k, v in os.environ.items() if k != "LD_PRELOAD"}
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     if r.returncode != 0:
         raise RuntimeError(f"build failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
     return r.stdout + r.stderr
 
 
+# ARCB_HOST_SANITIZE=1 builds and loads ``libarcref_san.so`` instead: the host
+# library under AddressSanitizer and UndefinedBehaviorSanitizer.  Python itself
+# is not instrumented, so the runtimes must be preloaded:
+#   ARCB_HOST_SANITIZE=1 ASAN_OPTIONS=detect_leaks=0 \
+#   LD_PRELOAD="$(gcc -print-file-name=libasan.so) $(gcc -print-file-name=libubsan.so)" \
+#   python -m pytest tests -m "not gpu"
+SANITIZE_FLAGS = ["-O1", "-g", "-fno-omit-frame-pointer", "-fsanitize=address,undefined"]
+
+
 def build_arcref(verbose=False) -> str:
     os.makedirs(LIBDIR, exist_ok=True)
     srcs = [os.path.join(CSRC, "ref", f) for f in ("arcref.cpp", "blake3.cpp", "toy_engine.cpp", "wgsl_forward.cpp", "neuralnet.cpp")]
-    out = os.path.join(LIBDIR, "libarcref.so")
+    san = os.environ.get("ARCB_HOST_SANITIZE", "0") not in ("", "0")
+    out = os.path.join(LIBDIR, "libarcref_san.so" if san else "libarcref.so")
     if _stale(out, srcs + _headers()):
-        _run([CXX, *CXX_FLAGS, "-shared", "-o", out + ".tmp", *srcs])
+        flags = CXX_FLAGS + (SANITIZE_FLAGS if san else [])
+        # the sanitized build uses the g++ on PATH: the one whose runtimes
+        # `gcc -print-file-name` names for the preload
+        _run(["g++" if san else CXX, *flags, "-shared", "-o", out + ".tmp", *srcs])
         os.replace(out + ".tmp", out)
         if verbose:
             print("built", out)
