@@ -30,6 +30,12 @@ using namespace q16;
 // ---------------------------------------------------------------------------
 namespace {
 
+// Set on the pool's worker threads: a parallel_for issued from inside a job
+// runs inline instead of waiting for the pool that is running it.
+thread_local bool t_pool_worker = false;
+
+// One job at a time: callers on other host threads (ctypes releases the GIL)
+// queue on call_mu_ rather than sharing the job slot.
 class Pool {
  public:
   explicit Pool(int n) { resize(n); }
@@ -39,6 +45,7 @@ class Pool {
   // generation, so they wait for the next job instead of taking a finished
   // one.
   void resize(int n) {
+    std::lock_guard<std::mutex> call(call_mu_);
     stop();
     if (n < 1) n = 1;
     quit_ = false;
@@ -48,8 +55,13 @@ class Pool {
   }
   // Runs f(lo, hi) over [0, n) split into size() contiguous ranges.
   void parallel_for(int64_t n, const std::function<void(int64_t, int64_t)>& f) {
-    int t = size();
-    if (t == 1 || n < 2) {
+    if (n < 2 || t_pool_worker) {
+      f(0, n);
+      return;
+    }
+    std::lock_guard<std::mutex> call(call_mu_);
+    const int t = size();
+    if (t == 1) {
       f(0, n);
       return;
     }
@@ -74,6 +86,7 @@ class Pool {
     if (lo < hi) f(lo, hi);
   }
   void loop(int idx, uint64_t seen) {
+    t_pool_worker = true;
     for (;;) {
       const std::function<void(int64_t, int64_t)>* job;
       int64_t n;
@@ -100,7 +113,7 @@ class Pool {
     workers_.clear();
   }
   std::vector<std::thread> workers_;
-  std::mutex mu_;
+  std::mutex call_mu_, mu_;
   std::condition_variable cv_, done_cv_;
   const std::function<void(int64_t, int64_t)>* job_ = nullptr;
   int64_t n_ = 0;

@@ -69,3 +69,36 @@ def test_toy_engine_golden():
     toks, h = ToyIntegerModel(100, 64, 2, 128, 2).generate_with_hash([1, 5, 10, 15], 8, 99)
     assert toks == [29, 18, 72, 47, 18, 72, 47, 47]
     assert h.hex() == "eb554f4f8afa13876ac66968b71c0d139eae83d5899a09931d5e65c47172eb1d"
+
+
+def test_oracle_concurrent_callers():
+    """Several host threads (an HTTP server's workers, say) call the oracle
+    at once; ctypes releases the GIL, so the native worker pool is shared
+    between them.  Every result must still equal the pinned hash."""
+    import threading
+
+    name, seed, plen, pseed, n, _, h8, _, _ = DENSE[0]
+    host = gen.random_model(preset(name), seed)
+    prompt = gen.seeded_prompt(plen, host.cfg.vocab, pseed)
+    models = [arcref.Model(host) for _ in range(4)]
+    got, errs = [], []
+
+    def work(m):
+        try:
+            for _ in range(2):
+                got.append(m.generate(prompt, n)[1].hex())
+        except Exception as e:  # pragma: no cover - reported below
+            errs.append(e)
+
+    L = arcref.lib()
+    old = L.arcref_num_threads()
+    L.arcref_set_threads(max(4, old))
+    try:
+        ts = [threading.Thread(target=work, args=(m,)) for m in models]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+    finally:
+        L.arcref_set_threads(old)
+    assert not errs and got == [h8] * 8
