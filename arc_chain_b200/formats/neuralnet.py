@@ -11,7 +11,8 @@ Embedding; crates/arc-vm/src/inference.rs:51-55, 132-211) while
 create_model.py writes 1..5 (scripts/create_model.py:30-61), and the VM
 silently falls back to a mock when parsing fails (inference.rs:566-573).
 :func:`parse` accepts both: it parses the file under each numbering and keeps
-the one that consumes the bytes exactly; failing both, it applies the VM's
+the one that consumes the bytes exactly (the VM's when both do, as for a file
+of only ReLU / Softmax layers); failing both, it applies the VM's
 own rule (numbering 0..4, bytes after the last layer ignored).  It never
 falls back to a mock.
 

@@ -25,7 +25,8 @@ def round_half_away_f32(v: np.ndarray) -> np.ndarray:
 def quantize_f32(values: np.ndarray, n_rows: int, n_cols: int):
     """Returns (int8 [n_rows, n_cols], int64 scales [n_rows])."""
     w = np.asarray(values, dtype=np.float32).reshape(n_rows, n_cols)
-    abs_max = np.maximum(np.abs(w).max(axis=1), np.float32(1e-10)).astype(np.float32)
+    # fold from 0.0 as the reference does, so an empty row has abs_max 0 (then 1e-10)
+    abs_max = np.maximum(np.abs(w).max(axis=1, initial=np.float32(0)), np.float32(1e-10)).astype(np.float32)
     inv = (np.float32(127.0) / abs_max).astype(np.float32)
     data = np.clip(round_half_away_f32(w * inv[:, None]), -127, 127).astype(np.int8)
     am_i = np.trunc(abs_max).astype(np.int64)

@@ -10,8 +10,9 @@
 //   Embedding  u32 vocab, u32 dim, f32 table[vocab*dim]
 // The VM numbers the tags 0..4 (Dense, ReLU, Softmax, LayerNorm, Embedding)
 // and create_model.py 1..5.  arcnn_parse takes the numbering under which the
-// whole image parses exactly; failing both, the VM's own rule (0..4, bytes
-// after the last layer ignored, inference.rs:132-211).
+// whole image parses exactly (the VM's when both do, as for a file of only
+// ReLU / Softmax layers); failing both, the VM's own rule (0..4, bytes after
+// the last layer ignored, inference.rs:132-211).
 //
 // Two executions:
 //   arcnn_forward_f32  the VM's f32 forward (inference.rs:282-381) with the
