@@ -2,7 +2,10 @@
 restated in Python: over every CTA the items cover each (tile, chunk) of
 the GEMM exactly once, the round-robin part hands out whole tiles, each
 CTA's item sequence is what its loops walk (item / next / seg_end), and the
-stream-K tail keeps the per-CTA load within one tile of even."""
+stream-K tail keeps the per-CTA load within one tile of even.  The TMA
+producer's segment walk (csrc/kernels/gemm_fused.cu: chunk index stepped
+with wrap inside a segment) gives the same chunks as kc(it).  Fixed shapes
+plus a random-shape sweep."""
 import itertools
 
 import pytest
@@ -63,6 +66,23 @@ class Work:
                                              (5, 7, 3, 8), (2, 4, 8, 3)])
 @pytest.mark.parametrize("multi", [False, True])
 def test_items_cover_each_tile_chunk_once(Mt, nch, ntu, grid, multi):
+    check_cover(Mt, nch, ntu, grid, multi)
+
+
+def test_cover_property_random_shapes():
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+
+    @hyp.settings(max_examples=400, deadline=None)
+    @hyp.given(st.integers(1, 200), st.integers(1, 64), st.integers(1, 40), st.integers(1, 300), st.booleans())
+    def prop(Mt, nch, ntu, grid, multi):
+        hyp.assume(Mt * ntu * nch <= 40000)
+        check_cover(Mt, nch, ntu, grid, multi)
+
+    prop()
+
+
+def check_cover(Mt, nch, ntu, grid, multi):
     seen = {}
     loads = []
     for c in range(grid):
@@ -76,6 +96,11 @@ def test_items_cover_each_tile_chunk_once(Mt, nch, ntu, grid, multi):
             assert all(W.tile(j) == t for j in range(it, se))
             if it < W.dp_end:
                 assert it % nch == 0 and se - it == nch  # round-robin tiles are whole
+            # the producer steps the chunk index inside a segment (kc + 1, wrapping)
+            kc = W.kc(it)
+            for j in range(it, se):
+                assert kc == W.kc(j)
+                kc = 0 if kc + 1 == nch else kc + 1
             walk.extend(range(it, se))
             it = W.next(se)
         assert walk == items
