@@ -1,0 +1,44 @@
+"""The paged KV cache's host bookkeeping under random reserve / release
+sequences: page tables stay disjoint, tables plus the free list are exactly
+the pool, a request's table only grows while it lives, and a reservation
+that does not fit raises without taking any page."""
+import pytest
+
+from arc_chain_b200.runtime.kv_paged import PAGE, PagedKV
+
+hyp = pytest.importorskip("hypothesis")
+st = hyp.strategies
+
+OPS = st.lists(st.tuples(st.sampled_from(["reserve", "release"]), st.integers(0, 5), st.integers(0, 6 * PAGE)),
+               max_size=60)
+
+
+@hyp.settings(max_examples=300, deadline=None)
+@hyp.given(st.integers(1, 24), st.integers(1, 8), OPS)
+def test_page_tables_partition_the_pool(n_pages, max_per_seq, ops):
+    kv = PagedKV(1, n_pages, 1, 1, "cpu", max_per_seq)
+    for op, rid, n_tok in ops:
+        before = {r: list(t) for r, t in kv.tables.items()}
+        free_before = list(kv.pool.free)
+        if op == "reserve":
+            need = (n_tok + PAGE - 1) // PAGE
+            try:
+                t = kv.reserve(rid, n_tok)
+            except ValueError:
+                assert need > max_per_seq
+            except MemoryError:
+                assert need - len(before.get(rid, [])) > len(free_before)
+                assert kv.pool.free == free_before
+                assert all(kv.tables.get(r, []) == p for r, p in before.items())
+            else:
+                assert len(t) >= need and t[:len(before.get(rid, []))] == before.get(rid, [])
+        else:
+            kv.release(rid)
+            assert rid not in kv.tables
+        owned = [p for t in kv.tables.values() for p in t]
+        assert len(owned) == len(set(owned))
+        assert sorted(owned + kv.pool.free) == list(range(n_pages))
+        assert kv.pool.used == len(owned)
+        for r in kv.tables:
+            row = kv.table_row(r)
+            assert len(row) == max_per_seq and row[:len(kv.tables[r])] == kv.tables[r]
