@@ -38,6 +38,7 @@ import numpy as np
 import torch
 
 from arc_chain_b200.runtime.engine import Engine, I32
+from arc_chain_b200.runtime.kv_paged import PAGE, PagedKV
 from arc_chain_b200.utils.hashing import blake3
 
 
@@ -57,6 +58,21 @@ class Request:
     @property
     def done(self) -> bool:
         return self.output_hash is not None
+
+
+def check_fits(kv: PagedKV, held: int, n_prompt: int, max_tokens: int) -> None:
+    """Raises ValueError for a request that no amount of waiting would admit:
+    its 1 + prompt + max_tokens positions need more pages than one sequence
+    may hold (the engine's max_seq), or more than the pool has besides the
+    `held` pages that stay reserved (the idle lanes' scratch page).  Such a
+    request would otherwise wait at the head of the queue for good."""
+    need = (1 + n_prompt + max_tokens + PAGE - 1) // PAGE
+    if need > kv.max_pages_per_seq:
+        raise ValueError(f"request of {n_prompt} prompt + {max_tokens} new tokens needs {need} KV pages; "
+                         f"a sequence holds at most {kv.max_pages_per_seq}")
+    if need > kv.n_pages - held:
+        raise ValueError(f"request needs {need} KV pages; the cache has {kv.n_pages - held} besides "
+                         f"the {held} it keeps reserved")
 
 
 class Scheduler:
@@ -131,12 +147,16 @@ class Scheduler:
         self.lanes[lane] = None
 
     # ------------------------------------------------------------ API
+    def _check_fits(self, n_prompt: int, max_tokens: int) -> None:
+        if max_tokens > self.gen_cap:
+            raise ValueError(f"max_tokens {max_tokens} > gen_cap {self.gen_cap}")
+        check_fits(self.e.kv, len(self.e.kv.tables.get(self._scratch_rid, [])), n_prompt, max_tokens)
+
     def submit(self, prompt: Sequence[int], max_tokens: int) -> int:
+        self._check_fits(len(prompt), int(max_tokens))
         rid = self.e._rid
         self.e._rid += 1
         r = Request(rid, [int(t) for t in prompt], int(max_tokens), t_submit=time.perf_counter())
-        if max_tokens > self.gen_cap:
-            raise ValueError(f"max_tokens {max_tokens} > gen_cap {self.gen_cap}")
         self.requests[rid] = r
         self.waiting.append(r)
         return rid
@@ -277,6 +297,7 @@ class Scheduler:
                 r.tokens = list(q["tokens"])
                 r.output_hash = bytes.fromhex(q["output_hash"])
             else:
+                sch._check_fits(len(r.prompt), r.max_tokens)
                 r.resume = list(q["tokens"])
                 sch.waiting.append(r)
             sch.requests[rid] = r

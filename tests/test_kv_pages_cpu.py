@@ -42,3 +42,16 @@ def test_page_tables_partition_the_pool(n_pages, max_per_seq, ops):
         for r in kv.tables:
             row = kv.table_row(r)
             assert len(row) == max_per_seq and row[:len(kv.tables[r])] == kv.tables[r]
+
+
+def test_requests_that_can_never_fit_are_refused():
+    from arc_chain_b200.runtime.scheduler import check_fits
+
+    kv = PagedKV(1, 8, 1, 1, "cpu", 8)  # 8 pages, a sequence may hold all 8
+    check_fits(kv, 1, 100, 11)  # 112 positions = 7 pages: fits beside the scratch page
+    with pytest.raises(ValueError, match="besides"):
+        check_fits(kv, 1, 100, 12)  # 113 positions = 8 pages, only 7 outside the scratch page
+    kv = PagedKV(1, 64, 1, 1, "cpu", 4)
+    check_fits(kv, 1, 30, 33)  # 64 positions = 4 pages
+    with pytest.raises(ValueError, match="at most 4"):
+        check_fits(kv, 1, 30, 34)
