@@ -41,6 +41,7 @@ def lib():
                 "arcref_cache_new": (vp, [vp]),
                 "arcref_cache_free": (None, [vp]),
                 "arcref_cache_len": (i64, [vp]),
+                "arcref_cache_overflow": (C.c_int, [vp]),
                 "arcref_cache_truncate": (None, [vp, i64]),
                 "arcref_forward": (None, [vp, vp, C.c_uint32, vp]),
                 "arcref_last_hidden": (None, [vp, vp]),
@@ -224,6 +225,8 @@ class Model:
         h = np.zeros(32, dtype=np.uint8)
         n = lib().arcref_generate(self.h, _p(p) if p.size else None, p.size, max_tokens,
                                   _p(e) if e.size else None, e.size, _p(out), _p(h))
+        if n < 0:
+            raise ValueError(f"{1 + len(p)} + {max_tokens} positions run past the model's RoPE tables (max_seq)")
         return [int(t) for t in out[:n]], h.tobytes()
 
     def weight_hash(self) -> bytes:
@@ -254,6 +257,8 @@ class Cache:
     def forward(self, token: int) -> np.ndarray:
         out = np.empty(self.model.cfg.vocab, dtype=np.int64)
         lib().arcref_forward(self.model.h, self.h, int(token), _p(out))
+        if lib().arcref_cache_overflow(self.h):
+            raise ValueError("position past the model's RoPE tables (max_seq)")
         return out
 
     def last_hidden(self) -> np.ndarray:

@@ -288,6 +288,9 @@ struct arcref_model {
 struct arcref_cache {
   std::vector<std::vector<int64_t>> k, v;
   int64_t seq_len = 0;
+  // set when a forward was asked for a position past the RoPE tables (the
+  // reference indexes them unchecked and panics there)
+  bool overflow = false;
   std::vector<int64_t> last_hidden;
 };
 
@@ -298,11 +301,23 @@ struct Reader {
   size_t n, off = 0;
   bool ok = true;
   std::string err;
+  // Compares against the bytes left (no off + k, which a corrupted size
+  // field could wrap).
   bool need(size_t k, const char* what) {
     if (!ok) return false;
-    if (off + k > n) {
+    if (k > n - off) {
       ok = false;
       err = std::string("truncated file reading ") + what;
+      return false;
+    }
+    return true;
+  }
+  // `count` items of `size` bytes, checked before anything is allocated.
+  bool need_items(uint64_t count, uint64_t size, const char* what) {
+    if (!ok) return false;
+    if (size && count > (n - off) / size) {
+      ok = false;
+      err = std::string("size field exceeds the file reading ") + what;
       return false;
     }
     return true;
@@ -320,7 +335,7 @@ struct Reader {
 bool read_vec(Reader& r, std::vector<std::pair<size_t, size_t>>& spans, std::vector<int64_t>& owned,
               const char* what) {
   uint64_t len = r.u64(what);
-  if (!r.need(len * 8, what)) return false;
+  if (!r.need_items(len, 8, what)) return false;
   size_t at = owned.size();
   owned.resize(at + len);
   memcpy(owned.data() + at, r.p + r.off, len * 8);
@@ -331,9 +346,16 @@ bool read_vec(Reader& r, std::vector<std::pair<size_t, size_t>>& spans, std::vec
 
 bool read_i8w(Reader& r, I8W& w, std::vector<std::pair<size_t, size_t>>& spans,
               std::vector<int64_t>& owned, const char* what) {
-  w.rows = (int64_t)r.u64(what);
-  w.cols = (int64_t)r.u64(what);
-  if (!r.need((size_t)w.rows * 8, what)) return false;
+  const uint64_t rows = r.u64(what), cols = r.u64(what);
+  uint64_t bytes = 0;
+  if (!r.need_items(rows, 8, what)) return false;
+  if (__builtin_mul_overflow(rows, cols, &bytes) || bytes > r.n - r.off - rows * 8) {
+    r.ok = false;
+    r.err = std::string("size field exceeds the file reading ") + what;
+    return false;
+  }
+  w.rows = (int64_t)rows;
+  w.cols = (int64_t)cols;
   size_t at = owned.size();
   owned.resize(at + w.rows);
   memcpy(owned.data() + at, r.p + r.off, w.rows * 8);
@@ -349,7 +371,7 @@ bool read_i8w(Reader& r, I8W& w, std::vector<std::pair<size_t, size_t>>& spans,
 
 extern "C" {
 
-arcref_model* arcref_load_file(const char* path, char* err, int errlen) {
+static arcref_model* load_file(const char* path, char* err, int errlen) {
   auto fail = [&](const std::string& m) -> arcref_model* {
     if (err && errlen > 0) snprintf(err, errlen, "%s", m.c_str());
     return nullptr;
@@ -388,6 +410,13 @@ arcref_model* arcref_load_file(const char* path, char* err, int errlen) {
   read_i8w(r, m->emb, spans, m->owned, "embedding");
   read_i8w(r, m->out, spans, m->owned, "output");
   read_vec(r, spans, m->owned, "final_norm");
+  // every layer holds 7 matrices (16-byte headers) and 2 vectors (8-byte
+  // lengths) at least: a larger count is a corrupted header, refused before
+  // anything is allocated for it
+  if (r.ok && c.n_layers > 0 && (uint64_t)c.n_layers > (r.n - r.off) / (7 * 16 + 2 * 8)) {
+    arcref_free(m);
+    return fail("layer count exceeds the file");
+  }
   m->layers.resize(c.n_layers);
   for (int64_t l = 0; l < c.n_layers && r.ok; ++l) {
     Layer& L = m->layers[l];
@@ -439,7 +468,41 @@ arcref_model* arcref_load_file(const char* path, char* err, int errlen) {
     vec_at(L.attn_norm);
     vec_at(L.ffn_norm);
   }
+  // the forward pass indexes every matrix with the config's dimensions
+  std::string bad;
+  auto want = [&](const I8W& w, int64_t rows, int64_t cols, const char* name) {
+    if (bad.empty() && (w.rows != rows || w.cols != cols))
+      bad = std::string(name) + " is " + std::to_string(w.rows) + " x " + std::to_string(w.cols) +
+            ", the config needs " + std::to_string(rows) + " x " + std::to_string(cols);
+  };
+  if (c.n_heads < 1 || c.n_kv_heads < 1 || c.d_head < 2 || c.n_heads * c.d_head != c.d_model ||
+      c.n_kv_heads * c.d_head != c.d_kv || c.vocab < 1)
+    bad = "inconsistent config (heads x d_head must equal d_model and d_kv)";
+  want(m->emb, c.vocab, c.d_model, "embedding");
+  want(m->out, c.vocab, c.d_model, "output");
+  for (const Layer& L : m->layers) {
+    want(L.wq, c.d_model, c.d_model, "wq");
+    want(L.wk, c.d_kv, c.d_model, "wk");
+    want(L.wv, c.d_kv, c.d_model, "wv");
+    want(L.wo, c.d_model, c.d_model, "wo");
+    want(L.gate, c.d_ff, c.d_model, "gate");
+    want(L.up, c.d_ff, c.d_model, "up");
+    want(L.down, c.d_model, c.d_ff, "down");
+  }
+  if (!bad.empty()) {
+    arcref_free(m);
+    return fail(bad);
+  }
   return m;
+}
+
+arcref_model* arcref_load_file(const char* path, char* err, int errlen) {
+  try {
+    return load_file(path, err, errlen);
+  } catch (const std::exception& e) {  // no C++ exception crosses the C ABI
+    if (err && errlen > 0) snprintf(err, errlen, "load failed: %s", e.what());
+    return nullptr;
+  }
 }
 
 int arcref_save_file(const arcref_model* m, const char* path, const char* vocab_json,
@@ -546,6 +609,7 @@ arcref_cache* arcref_cache_new(const arcref_model* m) {
   return c;
 }
 void arcref_cache_free(arcref_cache* c) { delete c; }
+int arcref_cache_overflow(const arcref_cache* c) { return c->overflow ? 1 : 0; }
 int64_t arcref_cache_len(const arcref_cache* c) { return c->seq_len; }
 void arcref_cache_truncate(arcref_cache* c, int64_t len) {
   if (len >= c->seq_len) return;
@@ -565,6 +629,11 @@ void arcref_forward(arcref_model* m, arcref_cache* cache, uint32_t token, int64_
   const arcref_config& c = m->cfg;
   const int64_t d = c.d_model, dh = c.d_head, half = dh / 2;
   const int64_t pos = cache->seq_len;
+  if ((pos + 1) * half > m->rope_cos.n || (pos + 1) * half > m->rope_sin.n) {
+    cache->overflow = true;
+    std::fill(logits, logits + c.vocab, 0);
+    return;
+  }
   const int64_t* lut = exp_lut();
   int64_t idx = std::min<int64_t>((int64_t)token, c.vocab - 1);
   std::vector<int64_t> h(d), n(d), q(d), kb(c.d_kv), vb(c.d_kv), ao(d), pr(d), g(c.d_ff),
@@ -643,9 +712,10 @@ int64_t arcref_generate(arcref_model* m, const uint32_t* prompt, int64_t n_promp
   arcref_forward(m, cache, 1, logits.data());  // BOS
   for (int64_t i = 0; i < n_prompt; ++i) arcref_forward(m, cache, prompt[i], logits.data());
   int64_t ng = 0;
-  for (int64_t t = 0; t < max_tokens; ++t) {
+  for (int64_t t = 0; t < max_tokens && !cache->overflow; ++t) {
     uint32_t last = ng > 0 ? out_tokens[ng - 1] : (n_prompt > 0 ? prompt[n_prompt - 1] : 0);
     arcref_forward(m, cache, last, logits.data());
+    if (cache->overflow) break;
     for (int64_t k = ng - 1, cnt = 0; k >= 0 && cnt < 64; --k, ++cnt) {
       uint32_t ti = out_tokens[k];
       if ((int64_t)ti < m->cfg.vocab) logits[ti] = penalize(logits[ti]);
@@ -661,7 +731,9 @@ int64_t arcref_generate(arcref_model* m, const uint32_t* prompt, int64_t n_promp
     for (int64_t e = 0; e < n_eos; ++e) stop |= (eos[e] == (uint32_t)best);
     if (stop) break;
   }
+  const bool overflow = cache->overflow;
   arcref_cache_free(cache);
+  if (overflow) return -1;
   std::vector<uint8_t> bytes(ng * 4);
   for (int64_t i = 0; i < ng; ++i) {
     uint32_t t = out_tokens[i];

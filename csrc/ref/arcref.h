@@ -49,6 +49,8 @@ void arcref_enable_q4(arcref_model* m);
 
 // Greedy generate with the reference's quirks (1518-1557).  Returns the number
 // of generated tokens (<= max_tokens); writes BLAKE3(LE u32 tokens) to hash32.
+// Returns -1 when the sequence runs past the RoPE tables (the reference's
+// max_seq), where the reference's unchecked indexing panics.
 int64_t arcref_generate(arcref_model* m, const uint32_t* prompt, int64_t n_prompt,
                         int64_t max_tokens, const uint32_t* eos, int64_t n_eos,
                         uint32_t* out_tokens, uint8_t* hash32);
@@ -58,7 +60,10 @@ arcref_cache* arcref_cache_new(const arcref_model* m);
 void arcref_cache_free(arcref_cache* c);
 int64_t arcref_cache_len(const arcref_cache* c);
 void arcref_cache_truncate(arcref_cache* c, int64_t len);
+// A position past the RoPE tables writes zero logits and sets the cache's
+// overflow flag (arcref_cache_overflow) instead of reading past them.
 void arcref_forward(arcref_model* m, arcref_cache* c, uint32_t token, int64_t* logits);
+int arcref_cache_overflow(const arcref_cache* c);
 // Hidden state after the last layer (before the final norm) of the last
 // forward call, d_model values.
 void arcref_last_hidden(const arcref_cache* c, int64_t* out);

@@ -135,3 +135,59 @@ def test_native_net_equals_python_restatement(case, base):
     xq = np.array([nn._q16(v) for v in x], np.int64)
     with np.errstate(over="ignore"):
         np.testing.assert_array_equal(net.forward_q16(xq), nn.IntegerNet(layers).forward(xq))
+
+
+_FILE = {}
+
+
+def _model_file(tmp_dir):
+    if "raw" not in _FILE:
+        import os
+        from arc_chain_b200.formats import arc_int8, gen
+        from arc_chain_b200.models.config import preset
+
+        p = os.path.join(tmp_dir, "m.arc-int8")
+        arc_int8.save(gen.random_model(preset("micro"), 1), p)
+        _FILE["raw"] = open(p, "rb").read()
+    return _FILE["raw"]
+
+
+@settings(max_examples=150, deadline=None)
+@given(st.data())
+def test_corrupted_files_load_or_raise(tmp_path_factory, data):
+    """Truncations and overwritten 8-byte words anywhere in an ARC-INT8 file:
+    the native and Python readers either load a model or raise ValueError;
+    a size field that points past the end never reaches an allocation."""
+    from arc_chain_b200.formats import arc_int8
+
+    d = tmp_path_factory.mktemp("corrupt")
+    raw = bytearray(_model_file(str(d)))
+    if data.draw(st.booleans()):
+        raw = raw[:data.draw(st.integers(0, len(raw) - 1))]
+    else:
+        off = data.draw(st.integers(0, len(raw) // 8 - 1)) * 8
+        raw[off:off + 8] = data.draw(st.sampled_from([1 << 61, (1 << 64) - 1, 1 << 40, 0, 3])).to_bytes(8, "little")
+    p = str(d / "c.arc-int8")
+    open(p, "wb").write(bytes(raw))
+    for load in (lambda: arcref.Model(path=p), lambda: arc_int8.load(p)):
+        try:
+            load()
+        except (ValueError, MemoryError, OverflowError, struct_error()):
+            pass
+
+
+def struct_error():
+    import struct
+
+    return struct.error
+
+
+def test_oracle_refuses_positions_past_the_rope_tables():
+    from arc_chain_b200.formats import gen
+    from arc_chain_b200.models.config import preset
+
+    host = gen.random_model(preset("micro"), 2)  # max_seq 256
+    m = arcref.Model(host)
+    assert len(m.generate(list(range(3, 203)), 55)[0]) == 55  # positions 0..255
+    with pytest.raises(ValueError, match="RoPE"):
+        m.generate(list(range(3, 203)), 56)
