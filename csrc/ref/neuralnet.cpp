@@ -208,7 +208,7 @@ struct arcnn_net {
 
 extern "C" {
 
-arcnn_net* arcnn_parse(const uint8_t* data, size_t len, char* err, int errlen) {
+static arcnn_net* parse(const uint8_t* data, size_t len, char* err, int errlen) {
   std::vector<NNLayer> layers;
   std::string e, first_err;
   size_t used = 0;
@@ -233,10 +233,21 @@ arcnn_net* arcnn_parse(const uint8_t* data, size_t len, char* err, int errlen) {
   return net;
 }
 
+// No C++ exception (an allocation failure on a huge but well-formed file)
+// crosses the C ABI.
+arcnn_net* arcnn_parse(const uint8_t* data, size_t len, char* err, int errlen) {
+  try {
+    return parse(data, len, err, errlen);
+  } catch (const std::exception& e) {
+    if (err && errlen > 0) snprintf(err, (size_t)errlen, "parse failed: %s", e.what());
+    return nullptr;
+  }
+}
+
 arcnn_net* arcnn_new(void) { return new arcnn_net(); }
 
-int arcnn_add_layer(arcnn_net* net, int kind, int64_t rows, int64_t cols, const float* a,
-                    const float* b, float eps) {
+static int add_layer(arcnn_net* net, int kind, int64_t rows, int64_t cols, const float* a,
+                     const float* b, float eps) {
   NNLayer L;
   L.kind = kind;
   switch (kind) {
@@ -266,6 +277,15 @@ int arcnn_add_layer(arcnn_net* net, int kind, int64_t rows, int64_t cols, const 
   build_int(L);
   net->layers.push_back(std::move(L));
   return 0;
+}
+
+int arcnn_add_layer(arcnn_net* net, int kind, int64_t rows, int64_t cols, const float* a,
+                    const float* b, float eps) {
+  try {
+    return add_layer(net, kind, rows, cols, a, b, eps);
+  } catch (const std::exception&) {
+    return -2;
+  }
 }
 
 void arcnn_free(arcnn_net* net) { delete net; }

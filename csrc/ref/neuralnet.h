@@ -43,7 +43,8 @@ arcnn_net* arcnn_parse(const uint8_t* data, size_t len, char* err, int errlen);
 arcnn_net* arcnn_new(void);
 // Append a layer.  Dense: a = W [rows*cols], b = bias [rows].  LayerNorm:
 // a = gamma [rows], b = beta [rows], eps.  Embedding: a = table [rows*cols].
-// ReLU / Softmax take no arrays.  Returns 0, or -1 for an unknown kind.
+// ReLU / Softmax take no arrays.  Returns 0, -1 for an unknown kind, or -2
+// when the layer could not be allocated.
 int arcnn_add_layer(arcnn_net* net, int kind, int64_t rows, int64_t cols, const float* a,
                     const float* b, float eps);
 void arcnn_free(arcnn_net* net);

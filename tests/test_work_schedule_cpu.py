@@ -73,7 +73,7 @@ def test_cover_property_random_shapes():
     hyp = pytest.importorskip("hypothesis")
     st = hyp.strategies
 
-    @hyp.settings(max_examples=400, deadline=None)
+    @hyp.settings(max_examples=400, deadline=None, derandomize=True)
     @hyp.given(st.integers(1, 200), st.integers(1, 64), st.integers(1, 40), st.integers(1, 300), st.booleans())
     def prop(Mt, nch, ntu, grid, multi):
         hyp.assume(Mt * ntu * nch <= 40000)
