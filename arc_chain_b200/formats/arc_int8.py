@@ -175,6 +175,10 @@ def load(path: str) -> Int8Model:
                       d_ff=d_ff, d_head=d_head, vocab=vocab, max_seq=max_seq, attn_scale=attn_scale)
     if cfg.d_kv != d_kv:
         raise ValueError(f"d_kv {d_kv} != n_kv_heads*d_head {cfg.d_kv}")
+    if n_heads < 1 or n_kv_heads < 1 or d_head < 2 or n_heads * d_head != d_model or vocab < 1:
+        raise ValueError("inconsistent config (heads x d_head must equal d_model)")
+    if n_layers > (len(mm) - b.off) // (7 * 16 + 2 * 8):  # each layer's headers alone
+        raise ValueError("layer count exceeds the file")
     rope_cos, rope_sin = b.vec(), b.vec()
     emb, emb_s = b.i8w()
     out, out_s = b.i8w()
@@ -186,6 +190,16 @@ def load(path: str) -> Int8Model:
             L[n], L[n + "_s"] = b.i8w()
         L["attn_norm"], L["ffn_norm"] = b.vec(), b.vec()
         layers.append(L)
+    # the forward indexes every matrix with the config's dimensions
+    want = {"embedding": (emb, (vocab, d_model)), "output": (out, (vocab, d_model))}
+    shapes = {"wq": (d_model, d_model), "wk": (d_kv, d_model), "wv": (d_kv, d_model), "wo": (d_model, d_model),
+              "gate": (d_ff, d_model), "up": (d_ff, d_model), "down": (d_model, d_ff)}
+    for li, L in enumerate(layers):
+        for n, shp in shapes.items():
+            want[f"layers.{li}.{n}"] = (L[n], shp)
+    for name, (a, shp) in want.items():
+        if tuple(a.shape) != shp:
+            raise ValueError(f"{name} is {a.shape[0]} x {a.shape[1]}, the config needs {shp[0]} x {shp[1]}")
     vlen = b.u64()
     try:
         vocab_list = json.loads(bytes(b.arr(np.uint8, vlen)).decode())

@@ -169,11 +169,14 @@ def test_corrupted_files_load_or_raise(tmp_path_factory, data):
         raw[off:off + 8] = data.draw(st.sampled_from([1 << 61, (1 << 64) - 1, 1 << 40, 0, 3])).to_bytes(8, "little")
     p = str(d / "c.arc-int8")
     open(p, "wb").write(bytes(raw))
+    ok = []
     for load in (lambda: arcref.Model(path=p), lambda: arc_int8.load(p)):
         try:
             load()
+            ok.append(True)
         except (ValueError, MemoryError, OverflowError, struct_error()):
-            pass
+            ok.append(False)
+    assert ok[0] == ok[1]  # the two readers accept the same files
 
 
 def struct_error():
