@@ -81,6 +81,9 @@ class Service:
         self.tok = Tokenizer(vocab)
         self.weight_hash = weight_hash
         self.attestations: List[dict] = []
+        # the HTTP layer runs requests on a thread pool: the counters and the
+        # attestation list are updated under this lock
+        self._mu = threading.Lock()
         self.n_requests = 0
         self.total_tokens = 0
         self.total_ms = 0.0
@@ -95,16 +98,18 @@ class Service:
                                       (t1 - t0) * 1000, self.b.name)
         a = attest.attest(self.b.cfg, text, toks, self.weight_hash).body()
         out["attestation"] = a
-        self.attestations.append(a)
-        self.n_requests += 1
-        self.total_tokens += len(toks)
-        self.total_ms += (t2 - t1) * 1000
+        with self._mu:
+            self.attestations.append(a)
+            self.n_requests += 1
+            self.total_tokens += len(toks)
+            self.total_ms += (t2 - t1) * 1000
         return out
 
     def stats(self) -> dict:
-        return {"requests": self.n_requests, "tokens": self.total_tokens,
-                "avg_ms_per_token": self.total_ms / self.total_tokens if self.total_tokens else 0.0,
-                "model": attest.model_id_string(self.b.cfg)}
+        with self._mu:
+            return {"requests": self.n_requests, "tokens": self.total_tokens,
+                    "avg_ms_per_token": self.total_ms / self.total_tokens if self.total_tokens else 0.0,
+                    "model": attest.model_id_string(self.b.cfg)}
 
 
 def make_app(svc: Service):

@@ -20,3 +20,31 @@ def test_service_run_and_attestation():
     assert svc.run("w5 w7 w9", 6)["attestation"] == r["attestation"]
     app = server.make_app(svc)
     assert {"/inference/run", "/health", "/stats", "/inference/attestations"} <= {x.path for x in app.routes}
+
+
+def test_concurrent_requests_match_sequential():
+    """Requests served at once from several threads (as the HTTP layer's
+    worker pool does) give the same attestations as one at a time, and every
+    request is counted."""
+    import threading
+
+    host = gen.random_model(preset("tiny"), 0)  # large enough for the oracle's worker pool
+    host.vocab = ["<unk>", "<s>", "</s>", "▁"] + [f"▁w{i}" for i in range(host.cfg.vocab - 4)]
+    svc = server.Service(server.OracleBackend(host), host.vocab, host.weight_hash())
+    texts = [f"w{i} w{i + 3} w{2 * i}" for i in range(6)]
+    want = {t: svc.run(t, 4)["attestation"] for t in texts}
+    got, errs = {}, []
+
+    def work(t):
+        try:
+            got[t] = svc.run(t, 4)["attestation"]
+        except Exception as e:  # pragma: no cover - reported below
+            errs.append(e)
+
+    ts = [threading.Thread(target=work, args=(t,)) for t in texts]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not errs and got == want
+    assert svc.stats()["requests"] == 2 * len(texts) and len(svc.attestations) == 2 * len(texts)
