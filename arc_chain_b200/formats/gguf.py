@@ -245,8 +245,18 @@ def dequantize(raw: np.ndarray, t: int, n: int) -> np.ndarray:
 
 # ---------------------------------------------------------------- import
 def _round_half_away(v: np.ndarray) -> np.ndarray:
+    """Rust's ``x.round() as i64``: half away from zero, then a saturating
+    cast (NaN -> 0, out of range -> i64::MIN / i64::MAX).  Inputs come from
+    f32 values, so ``|v| + 0.5`` is exact in f64."""
     v = np.asarray(v, dtype=np.float64)
-    return (np.sign(v) * np.floor(np.abs(v) + 0.5)).astype(np.int64)
+    with np.errstate(invalid="ignore"):
+        r = np.sign(v) * np.floor(np.abs(v) + 0.5)
+    out = np.zeros(r.shape, dtype=np.int64)
+    hi, lo = r >= 2.0 ** 63, r <= -(2.0 ** 63)
+    mid = ~(hi | lo | np.isnan(r))
+    out[mid] = r[mid].astype(np.int64)
+    out[hi], out[lo] = np.iinfo(np.int64).max, np.iinfo(np.int64).min
+    return out
 
 
 def norm_q16(x: np.ndarray) -> np.ndarray:

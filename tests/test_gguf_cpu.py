@@ -118,3 +118,46 @@ def test_imported_model_runs_on_oracle(tmp_path):
 def _i8_only(m):
     m.emb_q16 = None
     return m
+
+
+def test_q16_rounding_saturates_like_rust():
+    v = np.array([np.nan, np.inf, -np.inf, 1e30, -1e30, 2.5, -2.5, 0.49999997, -0.5], np.float32)
+    got = G._round_half_away(v)
+    i64 = np.iinfo(np.int64)
+    assert list(got) == [0, i64.max, i64.min, i64.max, i64.min, 3, -3, 0, -1]
+
+
+def test_corrupted_gguf_loads_or_raises(tmp_path):
+    """Truncations and overwritten 8-byte words of a GGUF file: the importer
+    loads a model or raises an ordinary error; it never hangs on a corrupted
+    count or length field."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+    src = tmp_path / "m.gguf"
+    _write_llama(src, QT.Q8_0)
+    base = src.read_bytes()
+
+    @hyp.settings(max_examples=60, deadline=None, derandomize=True)
+    @hyp.given(st.data())
+    def prop(data):
+        raw = bytearray(base)
+        if data.draw(st.booleans()):
+            raw = raw[:data.draw(st.integers(0, len(raw) - 1))]
+        else:
+            off = data.draw(st.integers(0, len(raw) // 8 - 1)) * 8
+            raw[off:off + 8] = data.draw(st.sampled_from([1 << 61, (1 << 64) - 1, 1 << 33, 0, 7])).to_bytes(8, "little")
+        p = tmp_path / "c.gguf"
+        p.write_bytes(bytes(raw))
+        try:
+            G.load_gguf(str(p))
+        except (ValueError, KeyError, IndexError, TypeError, OverflowError, MemoryError, UnicodeDecodeError,
+                AssertionError, ZeroDivisionError, struct_error()):
+            pass
+
+    prop()
+
+
+def struct_error():
+    import struct
+
+    return struct.error
