@@ -23,14 +23,26 @@ def round_half_away_f32(v: np.ndarray) -> np.ndarray:
 
 
 def quantize_f32(values: np.ndarray, n_rows: int, n_cols: int):
-    """Returns (int8 [n_rows, n_cols], int64 scales [n_rows])."""
+    """Returns (int8 [n_rows, n_cols], int64 scales [n_rows]).  NaN entries
+    are skipped by the row maximum (f32::max) and quantise to 0; an infinite
+    maximum saturates ``abs_max as i64``; the scale division truncates."""
     w = np.asarray(values, dtype=np.float32).reshape(n_rows, n_cols)
-    # fold from 0.0 as the reference does, so an empty row has abs_max 0 (then 1e-10)
-    abs_max = np.maximum(np.abs(w).max(axis=1, initial=np.float32(0)), np.float32(1e-10)).astype(np.float32)
+    # fold from 0.0 with a NaN-ignoring max, as the reference does; an empty
+    # row has abs_max 0 (then 1e-10)
+    abs_max = np.fmax.reduce(np.abs(w), axis=1, initial=np.float32(0)).astype(np.float32)
+    abs_max = np.maximum(abs_max, np.float32(1e-10)).astype(np.float32)
     inv = (np.float32(127.0) / abs_max).astype(np.float32)
-    data = np.clip(round_half_away_f32(w * inv[:, None]), -127, 127).astype(np.int8)
-    am_i = np.trunc(abs_max).astype(np.int64)
-    scales = np.maximum((am_i * ONE + 126) // 127, 1).astype(np.int64)
+    with np.errstate(invalid="ignore"):
+        r = np.clip(round_half_away_f32(w * inv[:, None]), -127, 127)
+    data = np.where(np.isnan(r), 0, r).astype(np.int8)
+    am = np.trunc(abs_max.astype(np.float64))
+    hi = am >= 2.0 ** 63
+    am_i = np.where(hi, 0.0, am).astype(np.int64)  # every value kept here is below 2^63
+    am_i[hi] = np.iinfo(np.int64).max
+    with np.errstate(over="ignore"):
+        num = am_i * ONE + 126  # wrapping, as the reference's release build
+    q = np.abs(num) // 127
+    scales = np.maximum(np.where(num >= 0, q, -q), 1).astype(np.int64)
     return data, scales
 
 

@@ -293,3 +293,27 @@ def test_engine_stats_accumulate():
     s = eng.stats()
     assert (s.total_inferences, s.total_tokens, s.avg_latency_ms) == (2, 8, (16 + 20) // 2)
     assert eng.model_status(_mid(8)) == "Ready" and eng.models[_mid(8)].last_used == 2
+
+
+def test_quantiser_nan_and_infinite_rows_match_native():
+    """NaN entries are skipped by the row maximum and quantise to 0; an
+    infinite maximum saturates the scale's integer cast (both restatements)."""
+    W = np.array([[np.nan, 0.5, -2.0], [np.inf, 1.0, 0.0], [-np.inf, np.nan, 3.0], [0.25, -0.75, 0.0]], f32)
+    layer = dense(W, [0.0, 0.0, 0.0, 0.0])
+    for x in ([spec.ONE, 2 * spec.ONE, -spec.ONE], [0, 0, 0], [7, -3, 65536 * 100]):
+        x = np.array(x, np.int64)
+        with np.errstate(over="ignore"):
+            np.testing.assert_array_equal(NativeNet.from_layers([layer]).forward_q16(x), nn.IntegerNet([layer]).forward(x))
+    from arc_chain_b200.formats.quantize import quantize_f32
+
+    q, s = quantize_f32(W.reshape(-1), 4, 3)
+    assert list(q[0]) == [0, 32, -127] and s[0] == (2 * spec.ONE + 126) // 127
+    # inv = 127 / inf = 0 and inf * 0 is NaN, which quantises to 0; i64::MAX * ONE
+    # wraps to -ONE, and (-ONE + 126) / 127 < 1 gives scale 1
+    assert list(q[1]) == [0, 0, 0] and s[1] == 1
+    # a finite maximum in [2^62, 2^63) keeps its own value: (am * ONE) wraps
+    big = np.array([[2.0 ** 62 * 1.5, 1.0]], f32)
+    am = int(np.float32(2.0 ** 62 * 1.5))
+    num = ((am * spec.ONE + 126 + (1 << 63)) % (1 << 64)) - (1 << 63)
+    want = max(1, -(abs(num) // 127) if num < 0 else num // 127)
+    assert quantize_f32(big.reshape(-1), 1, 2)[1][0] == want
