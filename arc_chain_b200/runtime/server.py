@@ -41,18 +41,31 @@ class OracleBackend:
         return self.m.generate(prompt, max_tokens, eos)[0]
 
 
+class BackendError(RuntimeError):
+    """The serving backend failed; the request was not completed."""
+
+
 class SchedulerBackend:
-    """Serves from the GPU engine through the continuous-batching scheduler."""
+    """Serves from the GPU engine through the continuous-batching scheduler.
+
+    One daemon thread steps the scheduler while requests are queued or
+    running; callers wait on a condition variable.  If a step raises (a
+    CUDA error, a failure while admitting or decoding), the loop records the
+    exception, stops, and wakes every caller: requests in flight and any
+    later request raise :class:`BackendError` instead of waiting forever."""
 
     name = "INT8 integer, B200 (sm_100a), continuous batching"
 
-    def __init__(self, engine, max_batch: int = 16, gen_cap: int = 512):
-        from arc_chain_b200.runtime.scheduler import Scheduler
+    def __init__(self, engine=None, max_batch: int = 16, gen_cap: int = 512, sched=None):
+        if sched is None:
+            from arc_chain_b200.runtime.scheduler import Scheduler
 
-        self.cfg = engine.m.cfg
-        self.sched = Scheduler(engine, max_batch=max_batch, eos=RPC_EOS, gen_cap=gen_cap)
+            sched = Scheduler(engine, max_batch=max_batch, eos=RPC_EOS, gen_cap=gen_cap)
+        self.cfg = engine.m.cfg if engine is not None else getattr(sched, "cfg", None)
+        self.sched = sched
         self.cv = threading.Condition()
         self.stop = False
+        self.error: Optional[BaseException] = None
         self.t = threading.Thread(target=self._loop, daemon=True)
         self.t.start()
 
@@ -63,16 +76,36 @@ class SchedulerBackend:
                 if not busy:
                     self.cv.wait(timeout=0.05)
                     continue
-                self.sched.step()
+                try:
+                    self.sched.step()
+                except BaseException as e:  # the thread must not die silently
+                    self.error = e
+                    self.stop = True
+                    self.cv.notify_all()
+                    return
                 self.cv.notify_all()
+
+    def _raise(self):
+        raise BackendError(f"serving backend failed: {self.error!r}") from self.error
 
     def generate(self, prompt, max_tokens, eos=RPC_EOS):
         with self.cv:
+            if self.error is not None:
+                self._raise()
             rid = self.sched.submit(prompt, max_tokens)
             self.cv.notify_all()
             while not self.sched.requests[rid].done:
+                if self.error is not None:
+                    self.sched.requests.pop(rid, None)
+                    self._raise()
                 self.cv.wait(timeout=0.1)
             return self.sched.requests.pop(rid).tokens
+
+    def close(self):
+        with self.cv:
+            self.stop = True
+            self.cv.notify_all()
+        self.t.join(timeout=5)
 
 
 class Service:

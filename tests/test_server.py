@@ -48,3 +48,69 @@ def test_concurrent_requests_match_sequential():
         t.join()
     assert not errs and got == want
     assert svc.stats()["requests"] == 2 * len(texts) and len(svc.attestations) == 2 * len(texts)
+
+
+class _StubRequest:
+    def __init__(self):
+        self.done = False
+        self.tokens = []
+
+
+class _FailingScheduler:
+    """Scheduler stand-in: accepts requests, then its step raises."""
+
+    cfg = None
+
+    def __init__(self, fail_after: int = 0):
+        self.waiting = []
+        self.lanes = [None]
+        self.requests = {}
+        self.steps = 0
+        self.fail_after = fail_after
+
+    def submit(self, prompt, max_tokens):
+        rid = len(self.requests)
+        self.requests[rid] = _StubRequest()
+        self.waiting.append(rid)
+        return rid
+
+    def step(self):
+        self.steps += 1
+        if self.steps > self.fail_after:
+            raise RuntimeError("CUDA error: an illegal memory access was encountered (injected on the host)")
+        rid = self.waiting.pop(0)
+        self.requests[rid].done = True
+        self.requests[rid].tokens = [7]
+
+
+def test_scheduler_failure_raises_in_callers():
+    """A step that raises ends the loop, wakes the waiting caller with an
+    error, and every later request fails at once instead of hanging."""
+    import threading
+
+    import pytest
+
+    be = server.SchedulerBackend(sched=_FailingScheduler(fail_after=1))
+    try:
+        assert be.generate([1, 2], 4) == [7]  # the first step succeeds
+        res = {}
+
+        def call(i):
+            try:
+                res[i] = be.generate([3], 4)
+            except server.BackendError as e:
+                res[i] = e
+
+        ts = [threading.Thread(target=call, args=(i,)) for i in range(3)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join(timeout=10)
+        assert not any(t.is_alive() for t in ts), "a caller is still waiting"
+        assert all(isinstance(res[i], server.BackendError) for i in range(3))
+        assert isinstance(be.error, RuntimeError)
+        with pytest.raises(server.BackendError):
+            be.generate([4], 1)
+        assert not be.t.is_alive()
+    finally:
+        be.close()
