@@ -117,11 +117,10 @@ def main():
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--only", default="")
-    ap.add_argument("--shape", default="", help="one of " + ",".join(SHAPES_7B) +
-                    "; with --only stream: comma-separated buffer sizes in MB")
+    ap.add_argument("--shape", default="", help="one of " + ",".join(SHAPES_7B))
     a = ap.parse_args()
     torch.cuda.set_device(0)
-    if a.shape and a.only != "stream":
+    if a.shape:
         M, K = SHAPES_7B[a.shape]
         r = bench_fgemm(M, K, a.B, a.iters)
         r["name"] = a.shape
@@ -148,41 +147,6 @@ def main():
                     r["name"] = name
                     r["int8_TOPS"] = round(2 * M * K * 4 * B / (r["us"] * 1e-6) / 1e12, 1)
                     print(json.dumps(r), flush=True)
-        return
-    if a.only == "stream":
-        # bulk-copy streaming probe: achievable weight-load bandwidth without MMA
-        sizes = [int(x) << 20 for x in a.shape.split(",")] if a.shape else [2048]
-        cap = max(sizes) << 20 if not a.shape else max(sizes)
-        cap = max(cap, 2 << 30)
-        buf = torch.randint(-127, 128, (cap // 128, 128), dtype=torch.int8, device="cuda")
-        tm = ops.TensorMap(buf, 128)
-        err = torch.zeros(1, dtype=torch.int32, device="cuda")
-        flush = torch.empty(256 << 20, dtype=torch.int8, device="cuda")
-        for nbytes in ([2 << 30] if not a.shape else sizes):
-          for mode in (0, 1):
-            for tile in (16384, 32768):
-                for stages in (4, 6, 8, 11):
-                    if stages * tile > 216 * 1024:
-                        continue
-                    for grid in (ops.num_sms(),):
-                        def run():
-                            ops.check(ops.lib().arcb_stream_probe(tm.addr, buf.data_ptr(), nbytes, tile, stages, mode,
-                                                                  grid, err.data_ptr(), ops._s()), "stream_probe")
-                        run()
-                        torch.cuda.synchronize()
-                        tot = 0.0
-                        for _ in range(5):
-                            flush.zero_()  # cold L2 for every timed launch
-                            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                            t0.record()
-                            run()
-                            t1.record()
-                            torch.cuda.synchronize()
-                            tot += t0.elapsed_time(t1) * 1000
-                        us = tot / 5
-                        print(json.dumps({"probe": "stream", "MB": nbytes >> 20, "mode": ["tma2d", "bulk1d"][mode],
-                                          "tile": tile, "stages": stages, "grid": grid, "us": round(us, 2),
-                                          "GB_s": round(nbytes / us / 1e3, 1), "err": int(err.item())}), flush=True)
         return
     if a.only == "attn_batch":
         # attention forms across decode / batched / prefill-like grids

@@ -40,7 +40,6 @@ _SIGS = {
     "arcb_blake3_batch_commit": (i32, [vp, i64, vp, i64, vp, vp, i64, vp, vp]),
     "arcb_merkle_root": (i32, [vp, i64, vp, vp, vp, vp]),
     "arcb_ep_wait_apply": (i32, [vp, vp, C.c_uint64, vp, vp, i64, vp, vp, vp]),
-    "arcb_stream_probe": (i32, [vp, vp, i64, i32, i32, i32, i32, vp, vp]),
     "arcb_ds_sizes": (i32, [vp]),
     "arcb_ds_gemm": (i32, [vp, vp, vp, i32, i32, i32, i32, vp, vp, vp]),
     "arcb_decode_step": (i32, [vp, vp]),
