@@ -132,6 +132,9 @@ def main():
                 r = bench_fgemm(M, K, a.B, a.iters, pdl=pdl)
                 r["name"] = name
                 print(json.dumps(r), flush=True)
+    if a.only == "flowprof":
+        print(json.dumps(flow_profile()), flush=True)
+        return
     if a.only == "optimeline":
         # per-op device time of one eager 7B decode step (CUDA events between launches)
         print(json.dumps(op_timeline(fuse_norm=os.environ.get("ARCB_FUSE_NORM") == "1")), flush=True)
@@ -259,6 +262,7 @@ def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -
                             tp_size=world)
     eng = Engine(m, max_seq=400, comm=comm, n_pages=64)
     eng.fuse_norm = fuse_norm
+    eng.use_step_kernel = False  # the per-kernel path, one event per op
     p = gen.seeded_prompt(prompt_len, cfg.vocab, 1)
     rid = eng.new_request(prompt_len + 100)
     eng.prefill(rid, [1] + p)
@@ -286,6 +290,107 @@ def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -
     out = {"world": world, "fuse_norm": eng._norm_fused(), "total_us": round(sum(agg.values()), 1),
            "per_op_us": {k: {"launches": cnt[k] // reps, "total": round(v, 1), "each": round(v / max(1, cnt[k] // reps), 2)}
                          for k, v in agg.items()}}
+    if world > 1:
+        import gc
+
+        eng._graphs.clear()
+        gc.collect()
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def flow_profile(model: str = "llama7b", prompt_len: int = 128, steps: int = 6) -> dict:
+    """The persistent dataflow decode step (runtime/step_flow.py) of one GPU
+    or of this rank: CUDA-event time per step, per-role wait totals over the
+    CTAs (mean and max, us) and CTA 0's phase timeline summed by kind."""
+    import collections
+    import os
+
+    import torch.distributed as dist
+
+    from arc_chain_b200.formats import gen
+    from arc_chain_b200.models import dense
+    from arc_chain_b200.models.config import preset
+    from arc_chain_b200.runtime.engine import Engine
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank, comm = 0, None
+    if world > 1:
+        from arc_chain_b200.parallel import tp
+        from arc_chain_b200.parallel.fused import FusedComm
+
+        rank, world = tp.init_distributed()
+        comm = FusedComm()
+    else:
+        torch.cuda.set_device(0)
+    cfg = preset(model)
+    cfg.max_seq = 400
+    m = dense.random_device(cfg, torch.device("cuda", torch.cuda.current_device()), seed=0, tp_rank=rank,
+                            tp_size=world)
+    eng = Engine(m, max_seq=400, comm=comm, n_pages=64)
+    p = gen.seeded_prompt(prompt_len, cfg.vocab, 1)
+    rid = eng.new_request(prompt_len + 100)
+    eng.prefill(rid, [1] + p)
+    bb = eng.buffers(1, gen_cap=64)
+    eng._reset_sampling(bb, [rid], [p[-1]], [prompt_len + 1], ())
+    flow = eng.flow_step(bb)
+    for _ in range(3):
+        eng.decode_step(bb)
+    sweep = {}
+    default_pf = flow.prog.pf_tiles
+    for pf in sorted({0, 8, 16, 24, 32, 48, default_pf}):
+        flow.set_prefetch(pf)
+        ts = []
+        for _ in range(steps):
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            flow.launch()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1000)
+        sweep[pf] = round(sorted(ts)[len(ts) // 2], 1)
+    flow.set_prefetch(default_pf)
+    flow.enable_stats(True)
+    flow.enable_profile(True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    flow.launch()
+    torch.cuda.synchronize()
+    st = flow.stats()
+    ph, gm = flow.profile()
+    if os.environ.get("ARCB_FLOW_TIMELINE"):
+        torch.save({"phases": ph, "gemms": gm, "kinds": flow.kinds}, os.environ["ARCB_FLOW_TIMELINE"])
+    names = {0: "norm", 1: "gemm", 2: "attn"}
+    L = cfg.n_layers
+    lo = 1 + 7 * (L // 2)
+
+    def q3(x):
+        x = x[x > 0]
+        if x.numel() == 0:
+            return None
+        v = x.sort().values
+        return [round(float(v[0]), 1), round(float(v[len(v) // 2]), 1), round(float(v[-1]), 1)]
+
+    mid = []
+    gi = sum(1 for k in flow.kinds[:lo] if k == 1)
+    for p in range(lo, lo + 7):
+        row = {"kind": names[flow.kinds[p]], "start": q3(ph[:, p, 0]), "end": q3(ph[:, p, 1])}
+        if flow.kinds[p] == 1:
+            row.update({"w_first": q3(gm[:, gi, 0]), "b_first": q3(gm[:, gi, 1]), "mma_first": q3(gm[:, gi, 2]),
+                        "mma_last": q3(gm[:, gi, 3])})
+            gi += 1
+        mid.append(row)
+    out = {"model": model, "world": world, "rank": rank, "step_us_by_l2_prefetch_tiles": sweep,
+           "stats_us": st, "mid_layer_min_med_max_us": mid, "step_end_us": q3(ph[:, -1, 1]),
+           "kernel_errors": eng.check_errors()}
+    flow.enable_stats(False)
+    flow.enable_profile(False)
     if world > 1:
         import gc
 

@@ -40,7 +40,7 @@ class RunConfig:
     pdl: bool = True             # programmatic dependent launch between kernels
     attn_paged: bool = True      # TMA-fed page-ring attention
     attn_gqa: bool = False       # grouped-query attention form (one cluster per KV head) for decode
-    step_kernel: bool = False    # persistent decode-step kernel (single stream, one GPU)
+    step_kernel: bool = False    # 1-2 slot decode steps as one persistent dataflow kernel
     device: str = "cuda"
 
     def __post_init__(self):

@@ -127,8 +127,10 @@ class Engine:
         self.nvtx = bool(os.environ.get("ARCB_NVTX"))
         # optional op timeline of eager forwards: list of (label, CUDA event) appended after each op
         self.op_events = None
-        # single-stream decode steps as one persistent kernel (runtime/decode_step.py)
-        self.use_step_kernel = os.environ.get("ARCB_STEP_KERNEL", "0") == "1"
+        # decode steps of 1-2 slots as one persistent dataflow kernel
+        # (runtime/step_flow.py) where it applies (ARCB_FLOW=1); otherwise one
+        # kernel per op.  Same tokens either way.
+        self.use_step_kernel = os.environ.get("ARCB_FLOW", "0") == "1"
         # RMSNorms fused into the preceding residual GEMM (W_o -> FFN norm,
         # W_down -> next attention norm / final norm); set before the first
         # forward.  Exact, but measured slower on the 7B decode (3.01 vs 2.85
@@ -264,25 +266,28 @@ class Engine:
         return bool(self.fuse_norm) and (cm.size == 1 or getattr(cm, "fused", False))
 
     def decode_step(self, bb: StepBuffers) -> None:
-        """forward + sample for every slot; slots advance in place.  Single-
-        stream steps (B <= 2, one GPU, int8 weights) run as one persistent
-        kernel when ``use_step_kernel`` is set."""
-        prog = self._step_program(bb) if getattr(self, "use_step_kernel", False) else None
-        if prog is not None:
-            m, c = self.m, self.m.cfg
-            ops.embed(bb.tokens, m.emb, m.emb_s, c.vocab, c.d_model, bb.B, bb.h, prog.cnt, bb.ss)
-            prog.launch()
+        """forward + sample for every slot; slots advance in place.  Steps of
+        1-2 slots run as one persistent dataflow kernel (embedding, every
+        layer, LM head) when ``use_step_kernel`` is set and the model fits it
+        (runtime/step_flow.py); otherwise one kernel per op."""
+        flow = self.flow_step(bb) if getattr(self, "use_step_kernel", False) else None
+        if flow is not None:
+            flow.launch()
+            logits = flow.logits
         else:
             self.forward(bb, bb.B, True)
-        ops.sample(bb.logits, self.m.cfg.vocab, bb.B, bb.hist, bb.count, bb.gen, bb.tokens, pos_inc=bb.pos,
+            logits = bb.logits
+        ops.sample(logits, self.m.cfg.vocab, bb.B, bb.hist, bb.count, bb.gen, bb.tokens, pos_inc=bb.pos,
                    done=bb.done, eos=bb.eos[:max(1, bb.n_eos)] if bb.n_eos else None)
 
-    def _step_program(self, bb: StepBuffers):
-        from arc_chain_b200.runtime import decode_step as dstep
+    def flow_step(self, bb: StepBuffers):
+        """The dataflow step program of `bb`, or None where it does not apply."""
+        from arc_chain_b200.runtime import step_flow
 
         key = id(bb)
         if key not in self._step_progs:
-            self._step_progs[key] = dstep.StepProgram(self, bb) if dstep.eligible(self, bb) else None
+            why = step_flow.eligible(self, bb.B)
+            self._step_progs[key] = step_flow.FlowStep(self, bb) if why is None else None
         return self._step_progs[key]
 
     def capture(self, bb: StepBuffers) -> torch.cuda.CUDAGraph:
