@@ -238,6 +238,10 @@ def main():
                "steps": steps, "matches_graph_tokens": got == tokens_first[:len(got)]}
 
     err = eng.check_errors()
+    from arc_chain_b200.bench import golden
+
+    golden_cfg = (args.model == golden.MODEL and args.prompt_len == golden.PROMPT_LEN)
+    golden_ok = bool(golden_cfg and golden.prefix_ok(tokens_first))
     if rank == 0:
         out = {
             "metric": METRIC, "value": round(ms_tok, 4), "unit": "ms/token", "n_gpus": world, "steps": K,
@@ -255,6 +259,9 @@ def main():
             "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches_per_step * K),
             "first_sequence": {"tokens": len(tokens_first),
                                "blake3": blake3(np.asarray(tokens_first, dtype="<u4").tobytes()).hex()},
+            # the generated tokens equal the CPU oracle's pinned 256-token output (prefix)
+            "hash_ok": golden_ok,
+            "oracle_output_hash_256": golden.OUTPUT_HASH_256 if golden_cfg else None,
             "kernel_errors": err, "impl": "b200",
         }
         print(json.dumps(out))

@@ -102,3 +102,29 @@ def test_oracle_concurrent_callers():
     finally:
         L.arcref_set_threads(old)
     assert not errs and got == [h8] * 8
+
+
+def test_pinned_7b_output_is_consistent():
+    """The pinned 7B tokens hash to the pinned output hash (cheap check of
+    the golden table itself)."""
+    import numpy as np
+
+    from arc_chain_b200.bench import golden
+    from arc_chain_b200.utils.hashing import blake3
+
+    assert len(golden.TOKENS_256) == 256
+    assert blake3(np.asarray(golden.TOKENS_256, dtype="<u4").tobytes()).hex() == golden.OUTPUT_HASH_256
+    assert golden.prefix_ok(golden.TOKENS_256[:25]) and not golden.prefix_ok(golden.TOKENS_256[1:26])
+
+
+@pytest.mark.skipif(not __import__("os").environ.get("ARCB_SLOW"), reason="7B on the CPU oracle: ~5 min (ARCB_SLOW=1)")
+def test_oracle_reproduces_pinned_7b_output():
+    from arc_chain_b200.bench import golden
+
+    cfg = preset(golden.MODEL)
+    cfg.max_seq = 400
+    host = gen.random_model(cfg, golden.WEIGHT_SEED)
+    assert host.weight_hash().hex() == golden.WEIGHT_HASH
+    prompt = gen.seeded_prompt(golden.PROMPT_LEN, cfg.vocab, golden.PROMPT_SEED)
+    toks, h = arcref.Model(host).generate(prompt, 256)
+    assert toks == golden.TOKENS_256 and h.hex() == golden.OUTPUT_HASH_256
