@@ -107,9 +107,26 @@ def bench_attn(T, n_heads=32, dh=128, B=1, iters=50, cluster=None, paged=True, n
     ops.set_attn_paged(True)
     ops.set_attn_gqa(False)
     kind = "attn_gqa" if (paged and gqa and n_kv < n_heads) else ("attn_paged" if paged else "attn_cluster")
-    return {"kernel": kind, "T": T, "heads": n_heads, "kv_heads": n_kv, "B": B, "us": round(us, 2),
-            "frac_of_measured_hbm": round(nbytes / us / 1e3 / hbm_peak_gbs(), 3),
-            "GB_s": round(nbytes / us / 1e3, 1), "cluster": cluster or ops.attn_cluster_size(B, n_heads)}
+    res = {"kernel": kind, "T": T, "heads": n_heads, "kv_heads": n_kv, "B": B, "us": round(us, 2),
+           "frac_of_measured_hbm": round(nbytes / us / 1e3 / hbm_peak_gbs(), 3),
+           "GB_s": round(nbytes / us / 1e3, 1), "cluster": cluster or ops.attn_cluster_size(B, n_heads)}
+    if n_kv < n_heads and n_heads // n_kv <= 8:
+        # the block form: one CTA per (slot, KV head) for its query heads
+        X2 = torch.zeros_like(X)
+        run = lambda: ops.attn_gqa_block(q, K, V, pt, pos, n_heads, n_kv, dh, 5793, B, X2, lm, pages * 16,
+                                         pages * 16, err)
+        if run():
+            torch.cuda.synchronize()
+            t0.record()
+            for _ in range(iters):
+                run()
+            t1.record()
+            torch.cuda.synchronize()
+            ub = t0.elapsed_time(t1) * 1000 / iters
+            res["gqa_block_us"] = round(ub, 2)
+            res["gqa_block_frac_of_measured_hbm"] = round(nbytes / ub / 1e3 / hbm_peak_gbs(), 3)
+    return res
+
 
 
 def main():
@@ -117,6 +134,8 @@ def main():
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--only", default="")
+    ap.add_argument("--model", default="")
+    ap.add_argument("--T", type=int, default=800)
     ap.add_argument("--shape", default="", help="one of " + ",".join(SHAPES_7B))
     a = ap.parse_args()
     torch.cuda.set_device(0)
@@ -132,8 +151,8 @@ def main():
                 r = bench_fgemm(M, K, a.B, a.iters, pdl=pdl)
                 r["name"] = name
                 print(json.dumps(r), flush=True)
-    if a.only == "flowprof":
-        print(json.dumps(flow_profile()), flush=True)
+    if a.only == "optimeline_batched":
+        print(json.dumps(op_timeline_batched(a.model or "llama70b", a.B if a.B > 1 else 64, a.T)), flush=True)
         return
     if a.only == "optimeline":
         # per-op device time of one eager 7B decode step (CUDA events between launches)
@@ -262,7 +281,6 @@ def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -
                             tp_size=world)
     eng = Engine(m, max_seq=400, comm=comm, n_pages=64)
     eng.fuse_norm = fuse_norm
-    eng.use_step_kernel = False  # the per-kernel path, one event per op
     p = gen.seeded_prompt(prompt_len, cfg.vocab, 1)
     rid = eng.new_request(prompt_len + 100)
     eng.prefill(rid, [1] + p)
@@ -301,105 +319,46 @@ def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -
     return out
 
 
-def flow_profile(model: str = "llama7b", prompt_len: int = 128, steps: int = 6) -> dict:
-    """The persistent dataflow decode step (runtime/step_flow.py) of one GPU
-    or of this rank: CUDA-event time per step, per-role wait totals over the
-    CTAs (mean and max, us) and CTA 0's phase timeline summed by kind."""
+
+def op_timeline_batched(model: str = "llama70b", B: int = 64, T: int = 800, reps: int = 3) -> dict:
+    """Per-op device time of one eager decode step over B slots, every slot at
+    position T - 1 (distinct pages), on one GPU: where a batched step's time goes."""
     import collections
-    import os
 
-    import torch.distributed as dist
-
-    from arc_chain_b200.formats import gen
     from arc_chain_b200.models import dense
     from arc_chain_b200.models.config import preset
     from arc_chain_b200.runtime.engine import Engine
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank, comm = 0, None
-    if world > 1:
-        from arc_chain_b200.parallel import tp
-        from arc_chain_b200.parallel.fused import FusedComm
-
-        rank, world = tp.init_distributed()
-        comm = FusedComm()
-    else:
-        torch.cuda.set_device(0)
+    torch.cuda.set_device(0)
     cfg = preset(model)
-    cfg.max_seq = 400
-    m = dense.random_device(cfg, torch.device("cuda", torch.cuda.current_device()), seed=0, tp_rank=rank,
-                            tp_size=world)
-    eng = Engine(m, max_seq=400, comm=comm, n_pages=64)
-    p = gen.seeded_prompt(prompt_len, cfg.vocab, 1)
-    rid = eng.new_request(prompt_len + 100)
-    eng.prefill(rid, [1] + p)
-    bb = eng.buffers(1, gen_cap=64)
-    eng._reset_sampling(bb, [rid], [p[-1]], [prompt_len + 1], ())
-    flow = eng.flow_step(bb)
-    for _ in range(3):
-        eng.decode_step(bb)
-    sweep = {}
-    default_pf = flow.prog.pf_tiles
-    for pf in sorted({0, 8, 16, 24, 32, 48, default_pf}):
-        flow.set_prefetch(pf)
-        ts = []
-        for _ in range(steps):
-            torch.cuda.synchronize()
-            if world > 1:
-                dist.barrier()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            flow.launch()
-            e1.record()
-            torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1) * 1000)
-        sweep[pf] = round(sorted(ts)[len(ts) // 2], 1)
-    flow.set_prefetch(default_pf)
-    flow.enable_stats(True)
-    flow.enable_profile(True)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    flow.launch()
-    torch.cuda.synchronize()
-    st = flow.stats()
-    ph, gm = flow.profile()
-    if os.environ.get("ARCB_FLOW_TIMELINE"):
-        torch.save({"phases": ph, "gemms": gm, "kinds": flow.kinds}, os.environ["ARCB_FLOW_TIMELINE"])
-    names = {0: "norm", 1: "gemm", 2: "attn"}
-    L = cfg.n_layers
-    lo = 1 + 7 * (L // 2)
-
-    def q3(x):
-        x = x[x > 0]
-        if x.numel() == 0:
-            return None
-        v = x.sort().values
-        return [round(float(v[0]), 1), round(float(v[len(v) // 2]), 1), round(float(v[-1]), 1)]
-
-    mid = []
-    gi = sum(1 for k in flow.kinds[:lo] if k == 1)
-    for p in range(lo, lo + 7):
-        row = {"kind": names[flow.kinds[p]], "start": q3(ph[:, p, 0]), "end": q3(ph[:, p, 1])}
-        if flow.kinds[p] == 1:
-            row.update({"w_first": q3(gm[:, gi, 0]), "b_first": q3(gm[:, gi, 1]), "mma_first": q3(gm[:, gi, 2]),
-                        "mma_last": q3(gm[:, gi, 3])})
-            gi += 1
-        mid.append(row)
-    out = {"model": model, "world": world, "rank": rank, "step_us_by_l2_prefetch_tiles": sweep,
-           "stats_us": st, "mid_layer_min_med_max_us": mid, "step_end_us": q3(ph[:, -1, 1]),
-           "kernel_errors": eng.check_errors()}
-    flow.enable_stats(False)
-    flow.enable_profile(False)
-    if world > 1:
-        import gc
-
-        eng._graphs.clear()
-        gc.collect()
+    cfg.max_seq = (T + 16 + 15) // 16 * 16
+    m = dense.random_device(cfg, torch.device("cuda", 0), seed=0)
+    pps = cfg.max_seq // 16
+    eng = Engine(m, max_seq=cfg.max_seq, n_pages=B * pps + 4)
+    bb = eng.buffers(B, gen_cap=8)
+    bb.tokens.copy_(torch.arange(B, dtype=torch.int32) * 7 + 3)
+    bb.pos.fill_(T - 1)
+    bb.pt.copy_(torch.arange(B * pps, dtype=torch.int32).view(B, pps)[:, :bb.pt.shape[1]])
+    for _ in range(2):
+        eng.forward(bb, B, True)
+    agg, cnt = collections.defaultdict(float), collections.Counter()
+    for _ in range(reps):
         torch.cuda.synchronize()
-        dist.barrier()
-        dist.destroy_process_group()
-    return out
+        eng.op_events = []
+        torch.cuda._sleep(80_000_000)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        eng.forward(bb, B, True)
+        torch.cuda.synchronize()
+        prev = e0
+        for lab, e in eng.op_events:
+            agg[lab] += prev.elapsed_time(e) * 1000 / reps
+            cnt[lab] += 1
+            prev = e
+        eng.op_events = None
+    return {"model": model, "B": B, "T": T, "total_us": round(sum(agg.values()), 1), "kernel_errors": eng.check_errors(),
+            "per_op_us": {k: {"launches": cnt[k] // reps, "total": round(v, 1), "each": round(v / max(1, cnt[k] // reps), 2)}
+                          for k, v in agg.items()}}
 
 
 if __name__ == "__main__":

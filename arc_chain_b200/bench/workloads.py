@@ -5,6 +5,7 @@ random-init weights and seeded prompts; timing is CUDA events around the
 device work (max over ranks when distributed)."""
 from __future__ import annotations
 
+import os
 import time
 
 import torch
@@ -55,6 +56,7 @@ def batched(model: str, n_requests: int, rank: int, world: int, comm, max_batch:
     sch = Scheduler(eng, max_batch=lanes, prefill_chunk=1024, gen_cap=max(olens))
     for i in range(n_requests):
         sch.submit(gen.seeded_prompt(plens[i], cfg.vocab, 1000 + i), olens[i])
+    sch.phase_events = []  # device time of prefill and decode, separately
     # warm-up: one step builds the decode graph
     _sync_barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -71,6 +73,7 @@ def batched(model: str, n_requests: int, rank: int, world: int, comm, max_batch:
             "unit": "generated tokens/s", "higher_is_better": True, "n_requests": n_requests, "lanes": lanes,
             "generated_tokens": gen_tokens, "prompt_tokens": prompt_tokens, "device_ms": round(dev_ms, 2),
             "wall_s": round(wall, 3), "decode_steps": sch.steps, "kv_pages": n_pages,
+            "device_ms_by_phase": sch.phase_times_ms(),
             "config": {"model": model, "parallelism": f"tp{world}", "prompt_len": list(prompt_range),
                        "out_len": list(out_range)}}
 
@@ -129,10 +132,17 @@ def spec_decode(target: str, draft: str, batch: int, prompt_len: int, gen_len: i
     teng = Engine(tm, max_seq=tc.max_seq, comm=comm, n_pages=batch * ((tc.max_seq + 15) // 16) + 4)
     deng = None
     if rank == 0:
-        dc = preset(draft)
-        dc.max_seq = tc.max_seq
-        deng = Engine(dense.random_device(dc, dev, seed=1), max_seq=dc.max_seq,
-                      n_pages=batch * ((dc.max_seq + 15) // 16) + 4)
+        if draft == "self":
+            # the target's own weights (unsharded, Q4 group-32) as the draft:
+            # every proposal is accepted, so the run shows the speculative
+            # path's best case and its verify cost
+            dm = dense.to_q4(dense.random_device(tc, dev, seed=0), "group")
+            deng = Engine(dm, max_seq=tc.max_seq, n_pages=batch * ((tc.max_seq + 15) // 16) + 4)
+        else:
+            dc = preset(draft)
+            dc.max_seq = tc.max_seq
+            deng = Engine(dense.random_device(dc, dev, seed=1), max_seq=dc.max_seq,
+                          n_pages=batch * ((dc.max_seq + 15) // 16) + 4)
     sd = SpecDecoder(teng, deng, k=k, lanes=batch, gen_cap=gen_len)
     prompts = [gen.seeded_prompt(prompt_len, tc.vocab, 1 + i) for i in range(batch)]
     _sync_barrier(world)
@@ -143,9 +153,16 @@ def spec_decode(target: str, draft: str, batch: int, prompt_len: int, gen_len: i
     _sync_barrier(world)
     ms = _max_over_ranks(e0.elapsed_time(e1), world)
     toks = sum(len(t) for t, _ in out)
+    exact = None
+    if os.environ.get("ARCB_SPEC_CHECK", "1") != "0":
+        # every sequence equals plain greedy decoding of the target
+        plain = [teng.generate(p, gen_len)[0] for p in prompts]
+        exact = all(list(t) == pl for (t, _), pl in zip(out, plain))
+    note = ("the draft is the target itself: every proposal is accepted" if draft == "self" else
+            "random-init target and draft are unrelated models, so almost no draft token is accepted")
     return {"metric": f"speculative decoding ({target} Q4 g32 + {draft} draft) tok/s",
             "value": round(toks / (ms / 1000), 2), "unit": "tokens/s", "higher_is_better": True,
             "acceptance": round(sd.acceptance, 4), "rounds": sd.rounds, "tokens": toks, "device_ms": round(ms, 2),
             "config": {"target": target, "draft": draft, "k": k, "batch": batch, "prompt_len": prompt_len,
                        "gen_len": gen_len, "parallelism": f"tp{world}"},
-            "note": "random-init target and draft are unrelated models, so almost no draft token is accepted"}
+            "equals_plain_greedy": exact, "note": note}

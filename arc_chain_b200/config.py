@@ -40,7 +40,6 @@ class RunConfig:
     pdl: bool = True             # programmatic dependent launch between kernels
     attn_paged: bool = True      # TMA-fed page-ring attention
     attn_gqa: bool = False       # grouped-query attention form (one cluster per KV head) for decode
-    step_kernel: bool = False    # 1-2 slot decode steps as one persistent dataflow kernel
     device: str = "cuda"
 
     def __post_init__(self):
@@ -195,5 +194,4 @@ def build_engine(cfg: RunConfig, rank: int = 0, world: int = 1, comm=None):
     if cfg.quant == "q4-group":
         m = dense.to_q4(m, "group")
     eng = Engine(m, max_seq=cfg.max_seq or None, comm=comm, n_pages=cfg.kv_pages or None)
-    eng.use_step_kernel = bool(cfg.step_kernel)
     return eng

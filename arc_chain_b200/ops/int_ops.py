@@ -279,6 +279,34 @@ def attn(q, Kc, Vc, pt, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax, max_T, e
           "attn_cluster")
 
 
+def attn_prefill(q, Kc, Vc, pt_row, nq, p0, n_heads, n_kv, dh, attn_scale, B, X, lmax, max_T, err) -> bool:
+    """Causal attention of a prefill chunk (slots [0, nq) = positions p0 ..
+    p0 + nq - 1 of one sequence, page-table row `pt_row`; slots [nq, B)
+    padding): every K/V page is read once per 16 positions.  False when the
+    chunk's scores do not fit in shared memory (nothing was launched)."""
+    rc = lib().arcb_attn_prefill(_p(q), _p(Kc), _p(Vc), _p(pt_row), nq, p0, n_heads, n_kv, dh, int(attn_scale), max_T,
+                                 B, _p(X), _p(lmax), _p(err), _s())
+    if rc == -3:
+        return False
+    _count()
+    check(rc, "attn_prefill")
+    return True
+
+
+def attn_gqa_block(q, Kc, Vc, pt, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax, max_T, t_lim, err) -> bool:
+    """Grouped-query decode attention, one CTA per (slot, KV head) serving
+    that KV head's query heads (each page read once for all of them).
+    t_lim bounds every slot's position + 1.  False when the scores do not
+    fit in shared memory (nothing was launched)."""
+    rc = lib().arcb_attn_gqa_block(_p(q), _p(Kc), _p(Vc), _p(pt), pt.shape[1], _p(pos), n_heads, n_kv, dh,
+                                   int(attn_scale), max_T, t_lim, B, _p(X), _p(lmax), _p(err), _s())
+    if rc == -3:
+        return False
+    _count()
+    check(rc, "attn_gqa_block")
+    return True
+
+
 # --------------------------------------------------------------- Q4 weights
 Q4_TILE = 128 * 64 + 128 * 2
 

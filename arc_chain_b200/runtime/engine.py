@@ -127,10 +127,6 @@ class Engine:
         self.nvtx = bool(os.environ.get("ARCB_NVTX"))
         # optional op timeline of eager forwards: list of (label, CUDA event) appended after each op
         self.op_events = None
-        # decode steps of 1-2 slots as one persistent dataflow kernel
-        # (runtime/step_flow.py) where it applies (ARCB_FLOW=1); otherwise one
-        # kernel per op.  Same tokens either way.
-        self.use_step_kernel = os.environ.get("ARCB_FLOW", "0") == "1"
         # RMSNorms fused into the preceding residual GEMM (W_o -> FFN norm,
         # W_down -> next attention norm / final norm); set before the first
         # forward.  Exact, but measured slower on the 7B decode (3.01 vs 2.85
@@ -138,7 +134,12 @@ class Engine:
         # resident and prefetch weights while it runs, which the fused form,
         # holding every SM until its norm phase ends, gives up.
         self.fuse_norm = os.environ.get("ARCB_FUSE_NORM", "0") == "1"
-        self._step_progs = {}
+        # prefill chunks: one chunk-attention launch per layer (each K/V page
+        # read once per 16 positions) instead of the per-position decode kernel
+        self.prefill_attn = os.environ.get("ARCB_PREFILL_ATTN", "1") != "0"
+        # decode steps of 8+ slots with grouped-query heads: one CTA per (slot,
+        # KV head) serving its query heads
+        self.gqa_block = os.environ.get("ARCB_GQA_BLOCK", "1") != "0"
 
     # ------------------------------------------------------------------ buffers
     def buffers(self, B: int, gen_cap: int = 0) -> StepBuffers:
@@ -148,8 +149,12 @@ class Engine:
         return self._bufs[key]
 
     # ------------------------------------------------------------------ forward
-    def forward(self, bb: StepBuffers, B: int, with_logits: bool = True) -> None:
-        """One forward over slots 0..B-1 of `bb` (tokens/pos/pt already set)."""
+    def forward(self, bb: StepBuffers, B: int, with_logits: bool = True, span=None) -> None:
+        """One forward over slots 0..B-1 of `bb` (tokens/pos/pt already set).
+        span = (n, p0): slots [0, n) are positions p0.. of one sequence (page
+        table row 0) and the rest padding; attention then runs as one
+        chunk-attention launch that reads every K/V page once per 16
+        positions (the same exact values as the per-position kernel)."""
         m, c, cm = self.m, self.m.cfg, self.comm
         d, dh = c.d_model, c.d_head
         nh, nkv = m.n_heads_local, m.n_kv_local
@@ -184,8 +189,20 @@ class Engine:
                 mark("norm")
             ops.linear_gemm(Ly.qkv, bb.mXd, B, c0, bb.P, bb.tiles, e["qkv"])
             mark("qkv")
-            ops.attn(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo, c1,
-                     self.max_pages * PAGE, bb.err)
+            T_all = self.max_pages * PAGE
+            if span is not None:
+                done = self.prefill_attn and ops.attn_prefill(bb.q, self.kv.K[l], self.kv.V[l], bb.pt[0], span[0],
+                                                              span[1], nh, nkv, dh, m.attn_scale, B, bb.Xo, c1, T_all,
+                                                              bb.err)
+            else:
+                # many decode slots with grouped-query heads: one CTA per (slot,
+                # KV head) reads each page once for its query heads
+                done = (self.gqa_block and nh // nkv >= 2 and nh // nkv <= 8 and B * nkv >= 64 and
+                        ops.attn_gqa_block(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale,
+                                           B, bb.Xo, c1, T_all, min(T_all, self.max_seq), bb.err))
+            if not done:
+                ops.attn(bb.q, self.kv.K[l], self.kv.V[l], bb.pt, bb.pos, nh, nkv, dh, m.attn_scale, B, bb.Xo, c1,
+                         self.max_pages * PAGE, bb.err)
             mark("attn")
             if reduce_in_kernel:
                 cm.fgemm_reduce(Ly.wo, bb.mXo, B, c1, bb, e["wo"], site=0)
@@ -218,6 +235,7 @@ class Engine:
             lm_e = cm.lm_epi(E[-1]["lm"], bb, c.vocab, m.vocab_offset) if hasattr(cm, "lm_epi") else E[-1]["lm"]
             ops.linear_gemm(m.lm, bb.mXd, B, cf, bb.P, bb.tiles, lm_e)
             cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset, bb=bb)
+            mark("lm_head")
 
     def _epis(self, bb: StepBuffers):
         """Epilogue descriptors of every fused GEMM of a forward over `bb`."""
@@ -266,29 +284,10 @@ class Engine:
         return bool(self.fuse_norm) and (cm.size == 1 or getattr(cm, "fused", False))
 
     def decode_step(self, bb: StepBuffers) -> None:
-        """forward + sample for every slot; slots advance in place.  Steps of
-        1-2 slots run as one persistent dataflow kernel (embedding, every
-        layer, LM head) when ``use_step_kernel`` is set and the model fits it
-        (runtime/step_flow.py); otherwise one kernel per op."""
-        flow = self.flow_step(bb) if getattr(self, "use_step_kernel", False) else None
-        if flow is not None:
-            flow.launch()
-            logits = flow.logits
-        else:
-            self.forward(bb, bb.B, True)
-            logits = bb.logits
-        ops.sample(logits, self.m.cfg.vocab, bb.B, bb.hist, bb.count, bb.gen, bb.tokens, pos_inc=bb.pos,
+        """forward + sample for every slot; slots advance in place."""
+        self.forward(bb, bb.B, True)
+        ops.sample(bb.logits, self.m.cfg.vocab, bb.B, bb.hist, bb.count, bb.gen, bb.tokens, pos_inc=bb.pos,
                    done=bb.done, eos=bb.eos[:max(1, bb.n_eos)] if bb.n_eos else None)
-
-    def flow_step(self, bb: StepBuffers):
-        """The dataflow step program of `bb`, or None where it does not apply."""
-        from arc_chain_b200.runtime import step_flow
-
-        key = id(bb)
-        if key not in self._step_progs:
-            why = step_flow.eligible(self, bb.B)
-            self._step_progs[key] = step_flow.FlowStep(self, bb) if why is None else None
-        return self._step_progs[key]
 
     def capture(self, bb: StepBuffers) -> torch.cuda.CUDAGraph:
         """Capture one decode step of `bb` into a CUDA graph (after a warm-up
@@ -354,7 +353,7 @@ class Engine:
             bb.tokens.copy_(torch.tensor(part + [0] * pad, dtype=I32))
             bb.pos.copy_(torch.tensor(list(range(start_pos + s, start_pos + s + n)) + [0] * pad, dtype=I32))
             bb.pt.copy_(torch.tensor([row] * n + [srow] * pad, dtype=I32))
-            self.forward(bb, B, with_logits=logits_sink is not None)
+            self.forward(bb, B, with_logits=logits_sink is not None, span=(n, start_pos + s))
             if logits_sink is not None:
                 logits_sink(bb.logits[:n].cpu().numpy())
             s += n

@@ -185,15 +185,39 @@ class Scheduler:
         t0 = time.perf_counter()
         if self._t0 is None:
             self._t0 = t0
+        ev = getattr(self, "phase_events", None)
+        if ev is not None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
         admitted = self._admit()
+        if ev is not None and admitted:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            ev.append(("prefill", e0, e1))
         active = sum(1 for x in self.lanes if x is not None)
         if active == 0:
             return 0
         fin0 = self.finished
+        if ev is not None:
+            d0 = torch.cuda.Event(enable_timing=True)
+            d0.record()
         try:
             return self._decode(active)
         finally:
+            if ev is not None:
+                d1 = torch.cuda.Event(enable_timing=True)
+                d1.record()
+                ev.append(("decode", d0, d1))
             self._record(t0, admitted, active, self.finished - fin0)
+
+    def phase_times_ms(self) -> dict:
+        """Device time (CUDA events) spent in prefill (admission) and in decode
+        steps, when ``phase_events`` was set to a list before running."""
+        out = {"prefill": 0.0, "decode": 0.0}
+        torch.cuda.synchronize()
+        for kind, a, b in getattr(self, "phase_events", None) or []:
+            out[kind] += a.elapsed_time(b)
+        return {k: round(v, 2) for k, v in out.items()}
 
     def _record(self, t0: float, admitted: int, active: int, finished: int) -> None:
         pool = self.e.kv.pool

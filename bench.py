@@ -67,10 +67,9 @@ def main():
                     help="decode: the headline 7B single-stream ms/token; batched: 70B-architecture continuous "
                          "batching tok/s; moe: MLA+MoE batch-32 decode; specdec: Q4 target + INT8 draft")
     ap.add_argument("--requests", type=int, default=128)
+    ap.add_argument("--draft", default="draft1b", help="specdec draft: a preset name, or 'self' (the target's weights)")
     ap.add_argument("--batch", type=int, default=0)
     ap.add_argument("--prefetch", type=int, default=0, help="weight tiles per CTA each GEMM prefetches for the next")
-    ap.add_argument("--step-kernel", type=int, default=-1,
-                    help="1: each decode step as one persistent kernel, 0: one kernel per op, -1: engine default")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -132,7 +131,7 @@ def main():
                 out = wl.moe_decode("dsv2lite", args.batch or 32, args.prompt_len if args.prompt_len != 128 else 512,
                                     256, args.steps, args.warmup, rank, world, ep_comm)
             else:
-                out = wl.spec_decode("llama7b", "draft1b", args.batch or 8, 256, 256, 4, rank, world,
+                out = wl.spec_decode("llama7b", args.draft, args.batch or 8, 256, 256, 4, rank, world,
                                      comm or tp_comm_none())
         out.update({"n_gpus": world, "warmup": args.warmup, "steps": args.steps, "scaling": "weak",
                     "dtype": "int8 weights x int64 Q16 activations (exact)", "impl": "b200",
@@ -160,8 +159,6 @@ def main():
     eng.prefetch_tiles = args.prefetch
     if args.fuse_norm >= 0:
         eng.fuse_norm = bool(args.fuse_norm)
-    if args.step_kernel >= 0:
-        eng.use_step_kernel = bool(args.step_kernel)
     prompt = gen.seeded_prompt(args.prompt_len, cfg.vocab, 1)
 
     W, K, G = args.warmup, args.steps, args.gen_len
@@ -253,7 +250,7 @@ def main():
                        "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
                        "l2": "weights per GPU >> 126 MB L2 (streamed from HBM every step)",
                        "prefetch_tiles": args.prefetch,
-                       "step_kernel": bool(eng.use_step_kernel), "fuse_norm": bool(eng._norm_fused()),
+                       "fuse_norm": bool(eng._norm_fused()),
                        "fuse_logits": bool(getattr(comm, "fuse_logits", False)),
                        "tokens_per_s": round(1000.0 / ms_tok, 2)},
             "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches_per_step * K),

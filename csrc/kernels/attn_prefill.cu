@@ -1,0 +1,313 @@
+// Exact causal attention for a prefill chunk: QB consecutive positions of one
+// sequence per CTA, every K and V page streamed once for all of them.
+//
+// Integer semantics per (position, head), as the reference CPU engine
+// (crates/arc-inference/src/cached_integer_model.rs:1448-1476,
+// softmax_i64 integer_lut.rs:78-100) and the decode kernels: score_j =
+// ((q.k_j >> 16) * attn_scale) >> 16 with wrapping i64 dots over keys j <= p;
+// w = softmax_i64(scores) (exact max, exact sum of LUT exps, per-term
+// (e_j * ONE) / sum); o = sum_j (w_j * v_j) >> 16 rounded per term.  No
+// online softmax: all scores of the block stay in shared memory.
+//
+// Why: the decode kernel run once per position re-reads the whole prefix for
+// every position of the chunk (a 1024-position chunk reads each K/V page up
+// to 1024 times, times the query heads of a KV head).  Here a page is read
+// once per QB positions.
+//
+// Two modes share the kernel (the block's "queries" read the same pages):
+//  * MODE 0, prefill: grid (ceil(B / QB), n_heads).  Slots [0, nq) are the
+//    chunk's positions p0, p0 + 1, ... of the sequence whose page-table row
+//    is pt[0]; query i of block x is slot x * QB + i of head blockIdx.y;
+//    slots [nq, B) (padding) get zero outputs.
+//  * MODE 1, grouped-query decode: grid (B, n_kv).  Query i is query head
+//    kvh * G + i (G = n_heads / n_kv <= QB) of slot blockIdx.x at position
+//    pos[slot], pages pt[slot]: the G heads that share a KV head read each of
+//    its pages once, instead of once per head.
+// QB * 16 threads.  Output: limb planes of the W_o operand (limb_row layout
+// of B slots) and the limb count (atomicMax).  The page ring holds `ring`
+// pages (set per launch from the shared memory the scores leave).
+#include "common.cuh"
+#include "lut.cuh"
+
+using namespace q16;
+
+namespace ap {
+
+constexpr int PAGE = 16;
+constexpr int MAX_RING = 8;
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ uint64_t hsum16(uint64_t v) {  // over the 16 lanes of a half-warp
+#pragma unroll
+  for (int m = 8; m >= 1; m >>= 1) v += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
+  return v;
+}
+__device__ __forceinline__ int64_t hmax16(int64_t v) {
+#pragma unroll
+  for (int m = 8; m >= 1; m >>= 1) {
+    const int64_t o = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, m);
+    v = o > v ? o : v;
+  }
+  return v;
+}
+
+template <int QB, int DH, int MODE>
+__global__ void __launch_bounds__(QB * 16) k_attn_block(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
+                                                        const int64_t* __restrict__ Vc, const int* __restrict__ pt,
+                                                        int pt_stride, const int* __restrict__ pos, int nq, int p0,
+                                                        int n_heads, int n_kv, int64_t attn_scale, int max_T, int B,
+                                                        int RING, int8_t* __restrict__ X, int* __restrict__ lmax,
+                                                        int* __restrict__ err) {
+  constexpr int NT = QB * 16;
+  constexpr int PB = PAGE * DH * 8;  // one page of one KV head
+  constexpr int EPT = DH / 16;       // output elements per thread in the value pass
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ int64_t lut[EXP_LUT_N];
+  __shared__ __align__(8) uint64_t full[MAX_RING];
+  __shared__ int s_need, s_abort;
+  const int tid = threadIdx.x, qi = tid >> 4, kk = tid & 15;
+  const int G = n_heads / n_kv;
+  const int d = n_heads * DH;
+  const uint32_t ring = (smem_u32(dsm) + 127u) & ~127u;
+  uint8_t* ringp = dsm + (ring - smem_u32(dsm));
+  int64_t* qs = (int64_t*)(ringp + RING * PB);  // [QB][DH]
+  int64_t* sc = qs + QB * DH;                   // [QB][Tp] scores -> exps -> weights
+  if (tid == 0) {
+    for (int s = 0; s < RING; ++s) mbar_init(smem_u32(&full[s]), 1);
+    fence_barrier_init();
+    s_need = 0;
+    s_abort = 0;
+  }
+  pdl_wait_dep();
+  pdl_allow_next();
+  // block geometry: live queries, their slot / head / position, the pages
+  int nreal, slot, hq, kvh, pq, Tmax;
+  const int* ptb;
+  if (MODE == 0) {
+    const int s0 = blockIdx.x * QB;
+    hq = blockIdx.y;
+    kvh = hq / G;
+    nreal = max(0, min(QB, nq - s0));
+    slot = s0 + qi;
+    pq = p0 + s0 + qi;
+    Tmax = nreal > 0 ? p0 + s0 + nreal : 0;  // keys of the block's last position
+    ptb = pt;
+  } else {
+    slot = blockIdx.x;
+    kvh = blockIdx.y;
+    hq = kvh * G + qi;
+    nreal = G;
+    pq = pos[slot];
+    Tmax = pq + 1;
+    ptb = pt + (size_t)slot * pt_stride;
+  }
+  const bool bad = nreal > 0 && (Tmax > max_T || Tmax < 1 || (MODE == 0 && p0 < 0));
+  if (bad && tid == 0) set_error(err, ARCB_ERR_SEQ_OVERFLOW);
+  const int npg = (nreal > 0 && !bad) ? (Tmax + PAGE - 1) / PAGE : 0;
+  const int Tp = npg * PAGE;
+  const int uses = 2 * npg;
+  int issued = 0;
+  auto issue = [&](int u) {  // thread 0
+    const bool isv = u >= npg;
+    const int page = ptb[isv ? u - npg : u];
+    const int64_t* src = (isv ? Vc : Kc) + ((size_t)page * n_kv + kvh) * PAGE * DH;
+    const uint32_t bar = smem_u32(&full[u % RING]);
+    mbar_arrive_expect_tx(bar, PB);
+    bulk_g2s(ring + (u % RING) * PB, src, PB, bar);
+  };
+  __syncthreads();
+  if (tid == 0)
+    for (; issued < min(RING, uses); ++issued) issue(issued);
+  for (int i = tid; i < EXP_LUT_N; i += NT) lut[i] = g_exp_lut.v[i];
+  for (int i = tid; i < QB * DH; i += NT) {
+    const int qq = i / DH, e = i - qq * DH;
+    const size_t src = MODE == 0 ? (size_t)(blockIdx.x * QB + qq) * d + blockIdx.y * DH + e
+                                 : (size_t)blockIdx.x * d + (kvh * G + qq) * DH + e;
+    qs[i] = qq < nreal && !bad ? q[src] : 0;
+  }
+  auto wait_use = [&](int u) -> bool {
+    if (tid == 0 && !mbar_wait(smem_u32(&full[u % RING]), (uint32_t)(u / RING) & 1u)) {
+      s_abort = 1;
+      set_error(err, ARCB_ERR_TIMEOUT_FULL);
+    }
+    __syncthreads();
+    return s_abort == 0;
+  };
+  auto release = [&]() {
+    __syncthreads();
+    if (tid == 0 && issued < uses) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(issued++);
+    }
+  };
+  const bool live = qi < nreal && !bad;
+  // ---- pass 1: scores of keys j <= pq (thread: position qi, key kk of each page)
+  int64_t mx = INT64_MIN;
+  bool ok = true;
+  for (int pi = 0; pi < npg && ok; ++pi) {
+    if (!(ok = wait_use(pi))) break;
+    const int64_t* kp = (const int64_t*)(ringp + (pi % RING) * PB);
+    const int j = pi * PAGE + kk;
+    if (live && j <= pq) {
+      const int64_t* kr = kp + kk * DH;
+      const int64_t* qr = qs + qi * DH;
+      uint64_t acc = 0;
+#pragma unroll 8
+      for (int e0 = 0; e0 < DH; ++e0) {
+        const int e = (e0 + kk) & (DH - 1);  // rotated so the 16 key rows hit different banks
+        acc += (uint64_t)qr[e] * (uint64_t)kr[e];
+      }
+      const int64_t s = attn_score((int64_t)acc, attn_scale);
+      sc[qi * Tp + j] = s;
+      mx = s > mx ? s : mx;
+    }
+    release();
+  }
+  // ---- pass 2: exact max and sum of exps per position; pass 3: weights
+  mx = hmax16(mx);
+  const int Tq = pq + 1;
+  uint64_t su = 0;
+  if (ok && live)
+    for (int j = kk; j < Tq; j += 16) {
+      const int64_t ex = integer_exp(wsub(sc[qi * Tp + j], mx), lut);
+      sc[qi * Tp + j] = ex;
+      su += (uint64_t)ex;
+    }
+  const int64_t gsum = (int64_t)hsum16(su);
+  if (ok && live)
+    for (int j = kk; j < Tq; j += 16) {
+      int64_t w;
+      if (Tq == 1) w = ONE;
+      else if (gsum == 0) w = ONE / Tq;
+      else w = wmul(sc[qi * Tp + j], ONE) / gsum;
+      sc[qi * Tp + j] = w;
+    }
+  __syncthreads();
+  // ---- value pass: thread = position qi, elements kk + 16 m
+  uint64_t o[EPT];
+#pragma unroll
+  for (int m = 0; m < EPT; ++m) o[m] = 0;
+  for (int pi = 0; pi < npg && ok; ++pi) {
+    const int u = npg + pi;
+    if (!(ok = wait_use(u))) break;
+    const int64_t* vp = (const int64_t*)(ringp + (u % RING) * PB);
+    if (live) {
+      const int kmax = min(PAGE, Tq - pi * PAGE);
+      for (int k = 0; k < kmax; ++k) {
+        const int64_t w = sc[qi * Tp + pi * PAGE + k];
+#pragma unroll
+        for (int m = 0; m < EPT; ++m) o[m] += (uint64_t)mulshr(w, vp[k * DH + kk + 16 * m]);
+      }
+    }
+    release();
+  }
+  // copies in flight (only after an abort) must land before the CTA exits
+  if (tid == 0)
+    for (int u = max(0, issued - RING); u < issued; ++u) mbar_wait(smem_u32(&full[u % RING]), (uint32_t)(u / RING) & 1u);
+  // ---- limb planes of the W_o operand (zeros for padding slots)
+  int need = 0;
+  if (slot < B && (MODE == 0 || qi < G)) {
+#pragma unroll
+    for (int m = 0; m < EPT; ++m) {
+      int8_t dg[8];
+      const int nl = (live && ok) ? limb_split8((int64_t)o[m], dg) : 0;
+      if (!(live && ok))
+#pragma unroll
+        for (int l = 0; l < 8; ++l) dg[l] = 0;
+      need = nl > need ? nl : need;
+#pragma unroll
+      for (int l = 0; l < 8; ++l) X[limb_row(l, slot, B) * d + hq * DH + kk + 16 * m] = dg[l];
+    }
+  }
+  need = __reduce_max_sync(0xffffffffu, need);
+  if ((tid & 31) == 0 && need) atomicMax(&s_need, need);
+  __syncthreads();
+  if (tid == 0 && s_need && lmax) atomicMax(lmax, s_need);
+}
+
+static size_t smem_bytes(int QB, int DH, int Tp, int ring) {
+  return 128 + (size_t)ring * PAGE * DH * 8 + (size_t)QB * DH * 8 + (size_t)QB * Tp * 8;
+}
+
+template <int QB, int DH, int MODE>
+int launch(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride, const int* pos, int nq,
+           int p0, int n_heads, int n_kv, int64_t attn_scale, int max_T, int B, int Tlim, int8_t* X, int* lmax,
+           int* err, cudaStream_t st) {
+  const int Tp = (Tlim + PAGE - 1) / PAGE * PAGE;
+  int ring = MAX_RING;
+  while (ring > 2 && smem_bytes(QB, DH, Tp, ring) > 220 * 1024) --ring;
+  const size_t smem = smem_bytes(QB, DH, Tp, ring);
+  if (smem > 220 * 1024) return -3;
+  static size_t attr = 0;
+  if (smem > attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_attn_block<QB, DH, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    attr = smem;
+  }
+  const dim3 grid = MODE == 0 ? dim3((B + QB - 1) / QB, n_heads) : dim3(B, n_kv);
+  // a position beyond the score buffer is reported (ARCB_ERR_SEQ_OVERFLOW), never written past it
+  const int cap = max_T < Tp ? max_T : Tp;
+  return launch_k(k_attn_block<QB, DH, MODE>, grid, dim3(QB * 16), smem, st, q, Kc, Vc, pt, pt_stride, pos, nq, p0,
+                  n_heads, n_kv, attn_scale, cap, B, ring, X, lmax, err);
+}
+
+}  // namespace ap
+
+extern "C" {
+
+// Largest key count the block kernel serves with QB queries per CTA.
+int arcb_attn_prefill_max_T(int dh, int qb) {
+  const int fixed = 128 + 2 * ap::PAGE * dh * 8 + qb * dh * 8;
+  return ((220 * 1024 - fixed) / (qb * 8)) / ap::PAGE * ap::PAGE;
+}
+
+// Causal attention of a prefill chunk: slots [0, nq) hold positions p0 ..
+// p0 + nq - 1 of the sequence whose page table is pt (one row), slots
+// [nq, B) are padding (zero outputs).  q: [B, n_heads * dh]; X: W_o limb
+// planes of B slots (limb_row layout).  Returns -3 when the chunk's scores
+// do not fit in shared memory (the caller then uses the decode kernel).
+int arcb_attn_prefill(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int nq, int p0,
+                      int n_heads, int n_kv, int dh, int64_t attn_scale, int max_T, int B, int8_t* X, int* lmax,
+                      int* err, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (n_kv <= 0 || n_heads % n_kv) return -2;
+  const int T = p0 + nq;
+  const bool wide = T <= arcb_attn_prefill_max_T(dh, 16);
+  if (dh == 128)
+    return wide ? ap::launch<16, 128, 0>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
+                                         lmax, err, st)
+                : ap::launch<8, 128, 0>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
+                                        lmax, err, st);
+  if (dh == 64)
+    return wide ? ap::launch<16, 64, 0>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
+                                        lmax, err, st)
+                : ap::launch<8, 64, 0>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
+                                       lmax, err, st);
+  return -2;
+}
+
+// Grouped-query decode attention: one CTA per (slot, KV head) serves the
+// G = n_heads / n_kv query heads of that KV head (G <= 8), reading each page
+// of the slot once.  Scores for up to t_lim keys (the largest position + 1
+// of any slot) stay in shared memory; returns -3 when they do not fit.
+int arcb_attn_gqa_block(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride,
+                        const int* pos, int n_heads, int n_kv, int dh, int64_t attn_scale, int max_T, int t_lim, int B,
+                        int8_t* X, int* lmax, int* err, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > 8) return -2;
+  if (dh == 128)
+    return ap::launch<8, 128, 1>(q, Kc, Vc, pt, pt_stride, pos, 0, 0, n_heads, n_kv, attn_scale, max_T, B, t_lim, X,
+                                 lmax, err, st);
+  if (dh == 64)
+    return ap::launch<8, 64, 1>(q, Kc, Vc, pt, pt_stride, pos, 0, 0, n_heads, n_kv, attn_scale, max_T, B, t_lim, X,
+                                lmax, err, st);
+  return -2;
+}
+
+}  // extern "C"

@@ -452,11 +452,27 @@ __global__ void k_sample(int64_t* __restrict__ logits, int ldl, int V, const int
   if (done && done[s]) return;
   int64_t* lg = logits + (size_t)(lrow ? lrow[s] : s) * ldl;
   const int cnt = count[s];
-  if (threadIdx.x == 0) {
-    const int n = cnt < 64 ? cnt : 64;
-    for (int k = 0; k < n; ++k) {
-      const int t = hist[s * 64 + ((cnt - 1 - k) & 63)];
-      if (t >= 0 && t < V) lg[t] = penalize(lg[t]);
+  // The penalty compounds per occurrence, and occurrences of different ids
+  // touch different logits, so the result depends only on each id's count
+  // among the newest min(cnt, 64): thread k takes history entry k, and the
+  // first entry of each id applies the penalty count times (one round trip
+  // instead of 64 dependent ones).
+  __shared__ int ht[64];
+  const int n = cnt < 64 ? cnt : 64;
+  if (threadIdx.x < n) ht[threadIdx.x] = hist[s * 64 + ((cnt - 1 - threadIdx.x) & 63)];
+  __syncthreads();
+  if (threadIdx.x < n) {
+    const int k = threadIdx.x, t = ht[k];
+    bool first = t >= 0 && t < V;
+    int c = 0;
+    for (int j = 0; j < n; ++j) {
+      c += ht[j] == t;
+      first &= !(j < k && ht[j] == t);
+    }
+    if (first) {
+      int64_t v = lg[t];
+      for (int r = 0; r < c; ++r) v = penalize(v);
+      lg[t] = v;
     }
   }
   __syncthreads();

@@ -1,7 +1,7 @@
 """Full-size end-to-end check: the 7B-architecture decoder (seeded random
 INT8 weights generated on the device) generates the CPU oracle's pinned
-256-token output, bit for bit, through the per-kernel path and through the
-persistent dataflow decode step."""
+256-token output, bit for bit (CUDA-graph decode steps, chunked prefill
+with the chunk attention kernel)."""
 import pytest
 
 torch = pytest.importorskip("torch")
@@ -27,12 +27,10 @@ def engine():
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("flow", [False, True], ids=["per_kernel", "dataflow"])
-def test_7b_generates_pinned_oracle_tokens(engine, flow):
+def test_7b_generates_pinned_oracle_tokens(engine):
     from arc_chain_b200.utils.hashing import blake3
     import numpy as np
 
-    engine.use_step_kernel = flow
     prompt = gen.seeded_prompt(golden.PROMPT_LEN, engine.m.cfg.vocab, golden.PROMPT_SEED)
     toks, h = engine.generate(prompt, 256)
     assert toks == golden.TOKENS_256

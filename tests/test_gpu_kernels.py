@@ -287,3 +287,34 @@ def test_speculative_decoding_equals_plain_greedy(same_draft):
     if same_draft:
         assert sd.acceptance == 1.0
     assert target.check_errors() == 0 and draft.check_errors() == 0
+
+
+def test_sample_penalty_and_argmax_match_reference():
+    """k_sample: compounding repetition penalty over the newest 64 ids (with
+    repeated ids) then argmax with lowest-index ties, against a direct
+    restatement of the reference loop (cached_integer_model.rs:1537-1548)."""
+    from arc_chain_b200 import spec
+    from arc_chain_b200.ops import int_ops as ops
+
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(3)
+    V, S = 5000, 6
+    for cnt in (0, 1, 7, 64, 100):
+        logits = rng.integers(-(1 << 40), 1 << 40, size=(S, V), dtype=np.int64)
+        logits[:, 17] = logits[:, 4000] = logits.max() + 5  # a tie: the lower index wins
+        hist = rng.integers(0, 40, size=(S, 64)).astype(np.int32)  # many repeats
+        hist[:, ::5] = 17
+        want = []
+        for s_ in range(S):
+            lg = logits[s_].copy()
+            for k in range(min(cnt, 64)):
+                t = int(hist[s_, (cnt - 1 - k) & 63])
+                lg[t] = spec.penalize(int(lg[t]))
+            want.append(int(np.argmax(lg)))
+        L = torch.from_numpy(logits).to(dev)
+        gen_ = torch.zeros(S, 200, dtype=torch.int32, device=dev)
+        tok = torch.zeros(S, dtype=torch.int32, device=dev)
+        ops.sample(L, V, S, torch.from_numpy(hist).to(dev), torch.full((S,), cnt, dtype=torch.int32, device=dev),
+                   gen_, tok)
+        torch.cuda.synchronize()
+        assert tok.cpu().tolist() == want, cnt

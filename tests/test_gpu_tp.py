@@ -1,5 +1,5 @@
 """Tensor parallelism for the dense decoder: 2-rank (and, where the box has
-them, 4-rank) runs with the NCCL all-reduce, with the fused in-GEMM reduce
+them, 4- and 8-rank) runs with the NCCL all-reduce, with the fused in-GEMM reduce
 over NVLink peer memory, and with the LM head's fused all-gather as well,
 every token checked against the oracle."""
 import json
@@ -19,7 +19,7 @@ def _ngpu():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("comm", ["nccl", "fused", "fused-logits", "fused-norm"])
 def test_tp_matches_oracle(comm, world):
     if _ngpu() < world:

@@ -42,7 +42,6 @@ def main():
     oracle = arcref.Model(host)
     eng = Engine(dense.from_host(host, "cuda", rank, world), comm=comm, n_pages=512, max_seq=256)
     eng.fuse_norm = a.comm == "fused-norm"
-    eng.use_step_kernel = a.comm.startswith("fused")  # single-stream steps as the dataflow kernel
     res = {"comm": a.comm, "world": world, "ok": True, "checks": 0}
     prompt = gen.seeded_prompt(32, cfg.vocab, 1)
     ref, rh = oracle.generate(prompt, 24)
@@ -58,12 +57,6 @@ def main():
         for rid, (p, n) in zip(rids, specs):
             res["ok"] &= sch.requests[rid].tokens == oracle.generate(p, n)[0]
             res["checks"] += 1
-    from arc_chain_b200.runtime.step_flow import FlowStep
-
-    # single-stream steps ran as the persistent dataflow kernel (fused comm only)
-    res["flow"] = any(isinstance(v, FlowStep) for v in eng._step_progs.values())
-    if a.comm.startswith("fused"):
-        res["ok"] &= res["flow"]
     res["kernel_errors"] = eng.check_errors()
     res["ok"] &= res["kernel_errors"] == 0
     flag = torch.tensor([0 if res["ok"] else 1], device="cuda")
