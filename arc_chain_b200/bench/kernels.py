@@ -74,14 +74,13 @@ def bench_fgemm(M, K, B, iters=50, mode="store", pdl=True, sub_box=None, ctas=No
             "GB_s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak_gbs(), 3)}
 
 
-def bench_attn(T, n_heads=32, dh=128, B=1, iters=50, cluster=None, paged=True, n_kv=None, gqa=True):
+def bench_attn(T, n_heads=32, dh=128, B=1, iters=50, cluster=None, paged=True, n_kv=None):
     """Decode attention over T cached tokens; paged selects the TMA-fed
     page-ring form (else per-thread loads); n_kv < n_heads is grouped-query
-    attention, run by the one-cluster-per-KV-head form when gqa is set."""
+    attention, also timed in the block form (one CTA per slot and KV head)."""
     dev = torch.device("cuda")
     n_kv = n_kv or n_heads
     ops.set_attn_paged(paged)
-    ops.set_attn_gqa(gqa)
     pages = (T + 15) // 16
     npg = pages * B
     K = torch.randint(-(1 << 18), 1 << 18, (npg, n_kv, 16, dh), dtype=torch.int64, device=dev)
@@ -105,8 +104,7 @@ def bench_attn(T, n_heads=32, dh=128, B=1, iters=50, cluster=None, paged=True, n
     assert int(err.item()) == 0
     nbytes = 2 * B * T * n_kv * dh * 8  # the K and V bytes, each read once
     ops.set_attn_paged(True)
-    ops.set_attn_gqa(False)
-    kind = "attn_gqa" if (paged and gqa and n_kv < n_heads) else ("attn_paged" if paged else "attn_cluster")
+    kind = "attn_paged" if paged else "attn_cluster"
     res = {"kernel": kind, "T": T, "heads": n_heads, "kv_heads": n_kv, "B": B, "us": round(us, 2),
            "frac_of_measured_hbm": round(nbytes / us / 1e3 / hbm_peak_gbs(), 3),
            "GB_s": round(nbytes / us / 1e3, 1), "cluster": cluster or ops.attn_cluster_size(B, n_heads)}
@@ -179,9 +177,8 @@ def main():
     if a.only == "attn_gqa":
         # 70B-style grouped-query decode (64 query / 8 KV heads; TP8 shard 8 / 1)
         for B, heads, kv, T in ((1, 64, 8, 1024), (16, 64, 8, 800), (64, 64, 8, 800), (64, 8, 1, 800), (128, 8, 1, 800)):
-            for paged, gqa in ((True, True), (True, False), (False, False)):
-                print(json.dumps(bench_attn(T, n_heads=heads, B=B, iters=a.iters, paged=paged, n_kv=kv, gqa=gqa)),
-                      flush=True)
+            for paged in (True, False):
+                print(json.dumps(bench_attn(T, n_heads=heads, B=B, iters=a.iters, paged=paged, n_kv=kv)), flush=True)
         return
     if a.only == "attn_cs":
         for T in (130, 386, 1024):

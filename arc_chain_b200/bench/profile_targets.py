@@ -184,7 +184,29 @@ def norm_limbs():
 
 
 
-TARGETS = {"attn": attn, "gemm_b1": gemm_b1, "gemm_b256": gemm_b256, "commit": commit, "ed25519": ed25519,
+def attn_block():
+    """Grouped-query block decode attention: 128 slots x 1 KV head (8 query
+    heads), T = 800 (the 70B TP8 shape): one wave of 128 CTAs."""
+    from arc_chain_b200.ops import int_ops as ops
+
+    dev = torch.device("cuda")
+    B, H, KV, DH, T = 128, 8, 1, 128, 800
+    pages = (T + 15) // 16
+    K = torch.randint(-(1 << 18), 1 << 18, (B * pages, KV, 16, DH), dtype=torch.int64, device=dev)
+    V = torch.randint(-(1 << 18), 1 << 18, (B * pages, KV, 16, DH), dtype=torch.int64, device=dev)
+    q = torch.randint(-(1 << 18), 1 << 18, (B, H * DH), dtype=torch.int64, device=dev)
+    pt = torch.arange(B * pages, dtype=torch.int32, device=dev).view(B, pages)
+    pos = torch.full((B,), T - 1, dtype=torch.int32, device=dev)
+    X = torch.zeros(ops.limb_rows(B), H * DH, dtype=torch.int8, device=dev)
+    lm = torch.zeros(1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    _timed(lambda: ops.attn_gqa_block(q, K, V, pt, pos, H, KV, DH, 5793, B, X, lm, T, T, err), 3, 10,
+           {"kernel": "k_attn_block<8,128,1>", "B": B, "heads": H, "kv_heads": KV, "T": T,
+            "bytes": 2 * B * T * KV * DH * 8})
+    assert int(err.item()) == 0
+
+
+TARGETS = {"attn_block": attn_block, "attn": attn, "gemm_b1": gemm_b1, "gemm_b256": gemm_b256, "commit": commit, "ed25519": ed25519,
            "mla_attn": mla_attn, "moe_route": moe_route, "q4_gemm": q4_gemm, "sample": sample,
            "norm_limbs": norm_limbs}
 

@@ -39,7 +39,7 @@ class RunConfig:
     use_graph: bool = True       # CUDA-graph the decode step
     pdl: bool = True             # programmatic dependent launch between kernels
     attn_paged: bool = True      # TMA-fed page-ring attention
-    attn_gqa: bool = False       # grouped-query attention form (one cluster per KV head) for decode
+    gqa_block: bool = True       # grouped-query decode over 8+ slots: one CTA per (slot, KV head)
     device: str = "cuda"
 
     def __post_init__(self):
@@ -170,7 +170,6 @@ def build_engine(cfg: RunConfig, rank: int = 0, world: int = 1, comm=None):
 
     ops.set_pdl(cfg.pdl)
     ops.set_attn_paged(cfg.attn_paged)
-    ops.set_attn_gqa(cfg.attn_gqa)
     dev = torch.device(cfg.device, torch.cuda.current_device()) if cfg.device == "cuda" else torch.device(cfg.device)
     if not is_file(cfg.model) and preset(cfg.model).n_experts:
         from arc_chain_b200.models import mla_moe_engine as me
@@ -194,4 +193,5 @@ def build_engine(cfg: RunConfig, rank: int = 0, world: int = 1, comm=None):
     if cfg.quant == "q4-group":
         m = dense.to_q4(m, "group")
     eng = Engine(m, max_seq=cfg.max_seq or None, comm=comm, n_pages=cfg.kv_pages or None)
+    eng.gqa_block = bool(cfg.gqa_block)
     return eng

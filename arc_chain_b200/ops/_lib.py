@@ -54,7 +54,6 @@ _SIGS = {
     "arcb_moe_route": (i32, [vp, i32, i32, i32, i32, i32, vp, vp]),
     "arcb_set_pdl": (None, [i32]),
     "arcb_set_attn_paged": (None, [i32]),
-    "arcb_set_attn_gqa": (None, [i32]),
     "arcb_wg_layernorm": (i32, [vp, i64, vp, i64, vp, i64, i32, vp]),
     "arcb_wg_quantize": (i32, [vp, i64, vp, i64, vp, vp]),
     "arcb_wg_matmul": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, vp, i64, vp]),

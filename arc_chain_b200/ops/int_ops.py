@@ -223,21 +223,6 @@ def set_pdl(on: bool) -> None:
     lib().arcb_set_pdl(int(on))
 
 
-_ATTN_GQA = [False]
-
-
-def set_attn_gqa(on: bool) -> None:
-    """Decode attention for grouped-query heads with 8 or more slots: one
-    cluster per KV head serving its query heads (True) or one per query head
-    (False, the default); identical results."""
-    _ATTN_GQA[0] = bool(on)
-    lib().arcb_set_attn_gqa(int(on))
-
-
-def attn_gqa_enabled() -> bool:
-    return _ATTN_GQA[0]
-
-
 def set_attn_paged(on: bool) -> None:
     """Decode attention for standard heads: TMA-fed page ring (True, the
     default) or per-thread loads (False); identical results."""

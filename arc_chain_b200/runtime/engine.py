@@ -333,15 +333,7 @@ class Engine:
         token 0 at position 0 of the scratch page, which no request reads."""
         row = self.kv.table_row(rid)
         srow = self.kv.table_row(self.scratch_rid)
-        # every slot of a prefill chunk is a position of the same sequence:
-        # the per-query-head attention form does better there than the
-        # grouped-query form, which serves decode steps over many sequences
-        prev = ops.attn_gqa_enabled()
-        ops.set_attn_gqa(False)
-        try:
-            self._prefill_chunks(row, srow, tokens, start_pos, chunk, logits_sink)
-        finally:
-            ops.set_attn_gqa(prev)
+        self._prefill_chunks(row, srow, tokens, start_pos, chunk, logits_sink)
 
     def _prefill_chunks(self, row, srow, tokens, start_pos, chunk, logits_sink) -> None:
         s = 0

@@ -22,7 +22,6 @@
 using namespace q16;
 
 int arcb_attn_paged_enabled();
-int arcb_attn_gqa_enabled();
 
 namespace {
 
@@ -462,296 +461,6 @@ int launch_paged(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const i
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
-// ---------------------------------------------------------------- grouped-query form
-// For GQA (G = n_heads / n_kv query heads per KV head) one cluster serves all
-// G query heads of a (slot, KV head): grid (CS, n_kv, B).  Each K and V page
-// is then streamed once instead of once per query head (8 times for the
-// 64/8-head 70B architecture), for the same arithmetic per head: scores,
-// exps, weights and per-term products are computed per query head exactly as
-// in k_attn_paged, and the three exact cluster exchanges carry G values each.
-template <int CS, int G>
-__global__ void __launch_bounds__(NT) k_attn_paged_gqa(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
-                                                       const int64_t* __restrict__ Vc, const int* __restrict__ pt,
-                                                       int pt_stride, const int* __restrict__ pos, int n_kv,
-                                                       int64_t attn_scale, int max_T, int B, int8_t* __restrict__ X,
-                                                       int* __restrict__ lmax, int64_t* __restrict__ o_out,
-                                                       int* __restrict__ err) {
-  constexpr int DH = 128;                // one output element per thread in the value pass
-  constexpr int PB = PAGE * DH * 8;      // bytes of one page of one KV head
-  constexpr int EPL = DH / 32;           // elements per lane in a dot
-  static_assert(NT == DH && NT == 128 && PAGE == 16, "4 warps x 4 keys per page; one element per thread");
-  extern __shared__ __align__(128) uint8_t dsm[];
-  __shared__ int64_t lut[EXP_LUT_N];
-  __shared__ __align__(8) uint64_t full[RING];
-  __shared__ unsigned long long xo[G][DH];
-  __shared__ int64_t red[NT / 32][G];
-  __shared__ long long xmax[G];
-  __shared__ unsigned long long xsum[G];
-  __shared__ int xneed, abort_;
-  const uint32_t ring = (smem_u32(dsm) + 127u) & ~127u;
-  volatile int* abort_p = &abort_;
-  const uint32_t rank = cluster_rank();
-  const int kvh = blockIdx.y, b = blockIdx.z;
-  const int n_heads = n_kv * G;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) {
-    for (int s = 0; s < RING; ++s) mbar_init(smem_u32(&full[s]), 1);
-    fence_barrier_init();
-    xneed = 0;
-    *abort_p = 0;
-  }
-  pdl_wait_dep();
-  pdl_allow_next();
-  const int T = pos[b] + 1;
-  const bool bad = T > max_T || T < 1;
-  if (bad && rank == 0 && tid == 0) set_error(err, ARCB_ERR_SEQ_OVERFLOW);
-  const int npT = bad ? 0 : (T + PAGE - 1) / PAGE;
-  const int p0 = npT * (int)rank / CS, p1 = npT * ((int)rank + 1) / CS;
-  const int np = p1 - p0;
-  const int n = bad ? 0 : max(0, min(T, p1 * PAGE) - min(T, p0 * PAGE));  // local keys
-  const int nkmax = ((max_T + PAGE - 1) / PAGE + CS - 1) / CS * PAGE;      // score row stride
-  int64_t* sc = (int64_t*)(dsm + (ring - smem_u32(dsm)) + RING * PB);      // [G][nkmax]
-  const int d = n_heads * DH;
-  const int* ptb = pt + (size_t)b * pt_stride;
-  const int uses = 2 * np;
-  int issued = 0;
-  auto issue = [&](int u) {
-    const bool isv = u >= np;
-    const int page = ptb[p0 + (isv ? u - np : u)];
-    const int64_t* src = (isv ? Vc : Kc) + ((size_t)page * n_kv + kvh) * PAGE * DH;
-    const uint32_t bar = smem_u32(&full[u % RING]);
-    mbar_arrive_expect_tx(bar, PB);
-    bulk_g2s(ring + (u % RING) * PB, src, PB, bar);
-  };
-  __syncthreads();
-  if (tid == 0)
-    for (; issued < min(RING, uses); ++issued) issue(issued);
-  for (int i = tid; i < EXP_LUT_N; i += NT) lut[i] = g_exp_lut.v[i];
-  uint64_t qv[G][EPL];
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int i = 0; i < EPL; ++i)
-      qv[g][i] = bad ? 0 : (uint64_t)q[(size_t)b * d + (kvh * G + g) * DH + lane + 32 * i];
-
-  auto wait_use = [&](int u) -> bool {
-    if (*abort_p) return false;
-    if (!mbar_wait(smem_u32(&full[u % RING]), (uint32_t)(u / RING) & 1u)) {
-      *abort_p = 1;
-      set_error(err, ARCB_ERR_TIMEOUT_FULL);
-      return false;
-    }
-    return true;
-  };
-  auto release = [&](int u) {
-    __syncthreads();
-    if (tid == 0 && issued < uses && !*abort_p) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(issued++);
-    }
-  };
-
-  // ---- pass 1: scores of the local keys for every query head, local maxima
-  int64_t mx[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) mx[g] = INT64_MIN;
-  for (int pi = 0; pi < np; ++pi) {
-    const bool ok = wait_use(pi);
-    __syncthreads();
-    if (!ok || *abort_p) break;
-    const int64_t* kp = (const int64_t*)(dsm + (ring - smem_u32(dsm)) + (pi % RING) * PB);
-#pragma unroll 1
-    for (int kk = 0; kk < 4; ++kk) {
-      const int64_t* row = kp + (warp * 4 + kk) * DH;
-      uint64_t kr[EPL];
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) kr[i] = (uint64_t)row[lane + 32 * i];
-      const int jj = pi * PAGE + warp * 4 + kk;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        uint64_t a = 0;
-#pragma unroll
-        for (int i = 0; i < EPL; ++i) a += qv[g][i] * kr[i];
-        a = warp_sum_u64(a);
-        if (jj < n) {
-          const int64_t sv = attn_score((int64_t)a, attn_scale);
-          if (lane == 0) sc[g * nkmax + jj] = sv;
-          mx[g] = sv > mx[g] ? sv : mx[g];
-        }
-      }
-    }
-    release(pi);
-  }
-  if (lane == 0)
-#pragma unroll
-    for (int g = 0; g < G; ++g) red[warp][g] = mx[g];
-  __syncthreads();
-  if (tid < G) {
-    int64_t m = red[0][tid];
-    for (int w = 1; w < NT / 32; ++w) m = red[w][tid] > m ? red[w][tid] : m;
-    xmax[tid] = m;
-  }
-  cluster_sync();
-  int64_t gmax[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    gmax[g] = INT64_MIN;
-#pragma unroll
-    for (int r = 0; r < CS; ++r) {
-      const int64_t v = (int64_t)ld_cluster_u64(&xmax[g], r);
-      gmax[g] = v > gmax[g] ? v : gmax[g];
-    }
-  }
-
-  // ---- pass 2: exps of the local keys, local sums per head
-  uint64_t sacc[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) sacc[g] = 0;
-  for (int jj = tid; jj < n; jj += NT) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const int64_t e = integer_exp(wsub(sc[g * nkmax + jj], gmax[g]), lut);
-      sc[g * nkmax + jj] = e;
-      sacc[g] += (uint64_t)e;
-    }
-  }
-#pragma unroll
-  for (int g = 0; g < G; ++g) sacc[g] = warp_sum_u64(sacc[g]);
-  __syncthreads();
-  if (lane == 0)
-#pragma unroll
-    for (int g = 0; g < G; ++g) red[warp][g] = (int64_t)sacc[g];
-  __syncthreads();
-  if (tid < G) {
-    uint64_t t = 0;
-    for (int w = 0; w < NT / 32; ++w) t += (uint64_t)red[w][tid];
-    xsum[tid] = t;
-  }
-  cluster_sync();
-  int64_t gsum[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    uint64_t gs = 0;
-#pragma unroll
-    for (int r = 0; r < CS; ++r) gs += ld_cluster_u64(&xsum[g], r);
-    gsum[g] = (int64_t)gs;
-  }
-
-  // ---- pass 3: weights, partial outputs (thread: element tid of every head)
-  for (int jj = tid; jj < n; jj += NT) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      int64_t w;
-      if (T == 1) w = ONE;
-      else if (gsum[g] == 0) w = ONE / T;
-      else w = wmul(sc[g * nkmax + jj], ONE) / gsum[g];
-      sc[g * nkmax + jj] = w;
-    }
-  }
-  __syncthreads();
-  const int e = tid;
-  uint64_t o[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) o[g] = 0;
-  for (int pi = 0; pi < np; ++pi) {
-    const int u = np + pi;
-    const bool ok = wait_use(u);
-    __syncthreads();
-    if (!ok || *abort_p) break;
-    const int64_t* vp = (const int64_t*)(dsm + (ring - smem_u32(dsm)) + (u % RING) * PB);
-    const int kmax = min(PAGE, n - pi * PAGE);
-    for (int k = 0; k < kmax; ++k) {
-      const int64_t v = vp[k * DH + e];
-#pragma unroll
-      for (int g = 0; g < G; ++g) o[g] += (uint64_t)mulshr(sc[g * nkmax + pi * PAGE + k], v);
-    }
-    release(u);
-  }
-#pragma unroll
-  for (int g = 0; g < G; ++g) xo[g][e] = o[g];
-  if (tid == 0)
-    for (int u = max(0, issued - RING); u < issued; ++u) mbar_wait(smem_u32(&full[u % RING]), (uint32_t)(u / RING) & 1u);
-  cluster_sync();
-
-  // ---- cross-CTA sum of partial outputs; rank r finalises a slice of the G x DH outputs
-  constexpr int TOT = G * DH, per = (TOT + CS - 1) / CS;
-  int need = 0;
-  for (int idx = (int)rank * per + tid; idx < min(TOT, ((int)rank + 1) * per); idx += NT) {
-    const int g = idx / DH, ee = idx - g * DH;
-    uint64_t acc = 0;
-#pragma unroll
-    for (int r = 0; r < CS; ++r) acc += ld_cluster_u64(&xo[g][ee], r);
-    if (bad) continue;
-    const int col = (kvh * G + g) * DH + ee;
-    const size_t off = (size_t)b * d + col;
-    if (o_out) o_out[off] = (int64_t)acc;
-    if (X) {
-      int8_t dg[8];
-      const int nl = limb_split8((int64_t)acc, dg);
-      need = nl > need ? nl : need;
-#pragma unroll
-      for (int l = 0; l < 8; ++l) X[limb_row(l, b, B) * d + col] = dg[l];
-    }
-  }
-  need = __reduce_max_sync(0xffffffffu, need);
-  if (lane == 0 && need) atomicMax(&xneed, need);
-  __syncthreads();
-  if (tid == 0 && lmax && xneed) atomicMax(lmax, xneed);
-  cluster_sync();  // no CTA may exit while a peer still reads its shared memory
-}
-
-inline size_t gqa_smem(int G, int cs, int max_T) {
-  const int nkmax = ((max_T + PAGE - 1) / PAGE + cs - 1) / cs * PAGE;
-  return 128 + (size_t)RING * PAGE * 128 * 8 + (size_t)G * nkmax * 8;
-}
-
-template <int CS, int G>
-int launch_gqa(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride, const int* pos,
-               int n_kv, int64_t attn_scale, int max_T, int B, int8_t* X, int* lmax, int64_t* o_out, int* err,
-               cudaStream_t st) {
-  const size_t smem = gqa_smem(G, CS, max_T);
-  static size_t attr = 0;
-  if (smem > attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_attn_paged_gqa<CS, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return (int)e;
-    attr = smem;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(CS, n_kv, B);
-  cfg.blockDim = dim3(NT);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute at[2];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = CS;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
-  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[1].val.programmaticStreamSerializationAllowed = arcb_pdl_enabled();
-  cfg.attrs = at;
-  cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_attn_paged_gqa<CS, G>, q, Kc, Vc, pt, pt_stride, pos, n_kv, attn_scale,
-                                     max_T, B, X, lmax, o_out, err);
-  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
-}
-
-// Cluster size for the grouped form: the smallest that keeps a CTA within
-// ~110 KB of shared memory (two per SM) and gives at least one wave of CTAs.
-template <int G>
-int gqa_any(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride, const int* pos,
-            int n_kv, int64_t attn_scale, int max_T, int B, int8_t* X, int* lmax, int64_t* o_out, int* err,
-            cudaStream_t st) {
-  int cs = 1;
-  while (cs < 8 && (gqa_smem(G, cs, max_T) > 110 * 1024 || (long long)cs * n_kv * B < 148)) cs *= 2;
-  if (gqa_smem(G, cs, max_T) > 200 * 1024) return -3;
-  switch (cs) {
-    case 1: return launch_gqa<1, G>(q, Kc, Vc, pt, pt_stride, pos, n_kv, attn_scale, max_T, B, X, lmax, o_out, err, st);
-    case 2: return launch_gqa<2, G>(q, Kc, Vc, pt, pt_stride, pos, n_kv, attn_scale, max_T, B, X, lmax, o_out, err, st);
-    case 4: return launch_gqa<4, G>(q, Kc, Vc, pt, pt_stride, pos, n_kv, attn_scale, max_T, B, X, lmax, o_out, err, st);
-    default: return launch_gqa<8, G>(q, Kc, Vc, pt, pt_stride, pos, n_kv, attn_scale, max_T, B, X, lmax, o_out, err, st);
-  }
-}
-
 template <int DH>
 int paged_any(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride, const int* pos,
               int n_heads, int n_kv, int64_t attn_scale, int max_T, int B, int cluster, int8_t* X, int* lmax,
@@ -821,17 +530,6 @@ extern "C" int arcb_attn_cluster(const int64_t* q, const int64_t* Kc, const int6
   const int max_pages = (max_T + PAGE - 1) / PAGE;
   const bool fits = cluster >= 1 && 128 + (size_t)RING * PAGE * dh * 8 +
                                         (size_t)((max_pages + cluster - 1) / cluster) * PAGE * 8 <= 200 * 1024;
-  const int G = n_kv > 0 && n_heads % n_kv == 0 ? n_heads / n_kv : 0;
-  // The grouped form pays off once a step has several sequences (one KV
-  // stream serves G query heads); a single stream has too few clusters.
-  if (arcb_attn_paged_enabled() && arcb_attn_gqa_enabled() && dh == 128 && (G == 2 || G == 4 || G == 8) &&
-      B >= 8) {
-    int rc = -3;
-    if (G == 2) rc = gqa_any<2>(q, Kc, Vc, pt, pt_stride, pos, n_kv, attn_scale, max_T, B, X, lmax, o_out, err, st);
-    if (G == 4) rc = gqa_any<4>(q, Kc, Vc, pt, pt_stride, pos, n_kv, attn_scale, max_T, B, X, lmax, o_out, err, st);
-    if (G == 8) rc = gqa_any<8>(q, Kc, Vc, pt, pt_stride, pos, n_kv, attn_scale, max_T, B, X, lmax, o_out, err, st);
-    if (rc != -3) return rc;  // -3: too long for the grouped form's shared memory; per-head form below
-  }
   if (arcb_attn_paged_enabled() && fits && (dh == 128 || dh == 64)) {
     if (dh == 128)
       return paged_any<128>(q, Kc, Vc, pt, pt_stride, pos, n_heads, n_kv, attn_scale, max_T, B, cluster, X, lmax,
@@ -849,13 +547,6 @@ static int g_attn_paged = 1;
 extern "C" void arcb_set_attn_paged(int on) { g_attn_paged = on; }
 int arcb_attn_paged_enabled() { return g_attn_paged; }
 
-// Grouped-query form for GQA heads (1) or one CTA per query head (0, the
-// default); both compute the same values.  The grouped form is faster per
-// kernel from 16 decode lanes up, but the 70B continuous-batching run has not
-// yet shown a gain, so it is opt-in.
-static int g_attn_gqa = 0;
-extern "C" void arcb_set_attn_gqa(int on) { g_attn_gqa = on; }
-int arcb_attn_gqa_enabled() { return g_attn_gqa; }
 
 extern "C" int arcb_attn_mla(const int64_t* q, const int64_t* cache, const int* pt, int pt_stride, const int* pos,
                              int n_heads, int dk, int dv, int64_t attn_scale, int max_T, int B, int cluster,

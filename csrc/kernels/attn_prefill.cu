@@ -23,9 +23,16 @@
 //    kvh * G + i (G = n_heads / n_kv <= QB) of slot blockIdx.x at position
 //    pos[slot], pages pt[slot]: the G heads that share a KV head read each of
 //    its pages once, instead of once per head.
-// QB * 16 threads.  Output: limb planes of the W_o operand (limb_row layout
-// of B slots) and the limb count (atomicMax).  The page ring holds `ring`
-// pages (set per launch from the shared memory the scores leave).
+// QB * 32 threads: one warp per query.  Output: limb planes of the W_o
+// operand (limb_row layout of B slots) and the limb count (atomicMax).  The
+// page ring holds `ring` pages (set per launch from the shared memory the
+// scores leave).
+//
+// Exact int32 fast path: a 64-bit wrapping multiply-add costs about five
+// integer instructions.  When a query row and a whole K page fit in int32,
+// every product fits exactly in int64, so one widening multiply-add per
+// element gives the identical wrapping sum; likewise a weight (at most ONE)
+// times a V value that fits in int32.  Each page is checked when it lands.
 #include "common.cuh"
 #include "lut.cuh"
 
@@ -57,20 +64,20 @@ __device__ __forceinline__ int64_t hmax16(int64_t v) {
 }
 
 template <int QB, int DH, int MODE>
-__global__ void __launch_bounds__(QB * 16) k_attn_block(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
+__global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
                                                         const int64_t* __restrict__ Vc, const int* __restrict__ pt,
                                                         int pt_stride, const int* __restrict__ pos, int nq, int p0,
                                                         int n_heads, int n_kv, int64_t attn_scale, int max_T, int B,
                                                         int RING, int8_t* __restrict__ X, int* __restrict__ lmax,
                                                         int* __restrict__ err) {
-  constexpr int NT = QB * 16;
+  constexpr int NT = QB * 32;
   constexpr int PB = PAGE * DH * 8;  // one page of one KV head
-  constexpr int EPT = DH / 16;       // output elements per thread in the value pass
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ int64_t lut[EXP_LUT_N];
   __shared__ __align__(8) uint64_t full[MAX_RING];
   __shared__ int s_need, s_abort;
-  const int tid = threadIdx.x, qi = tid >> 4, kk = tid & 15;
+  __shared__ int qfit[QB];  // query row fits in int32
+  const int tid = threadIdx.x, qi = tid >> 5, lane = tid & 31, kk = lane & 15, hh = lane >> 4;
   const int G = n_heads / n_kv;
   const int d = n_heads * DH;
   const uint32_t ring = (smem_u32(dsm) + 127u) & ~127u;
@@ -83,6 +90,7 @@ __global__ void __launch_bounds__(QB * 16) k_attn_block(const int64_t* __restric
     s_need = 0;
     s_abort = 0;
   }
+  if (tid < QB) qfit[tid] = 1;
   pdl_wait_dep();
   pdl_allow_next();
   // block geometry: live queries, their slot / head / position, the pages
@@ -128,7 +136,9 @@ __global__ void __launch_bounds__(QB * 16) k_attn_block(const int64_t* __restric
     const int qq = i / DH, e = i - qq * DH;
     const size_t src = MODE == 0 ? (size_t)(blockIdx.x * QB + qq) * d + blockIdx.y * DH + e
                                  : (size_t)blockIdx.x * d + (kvh * G + qq) * DH + e;
-    qs[i] = qq < nreal && !bad ? q[src] : 0;
+    const int64_t v = qq < nreal && !bad ? q[src] : 0;
+    qs[i] = v;
+    if (v != (int64_t)(int32_t)v) qfit[qq] = 0;
   }
   auto wait_use = [&](int u) -> bool {
     if (tid == 0 && !mbar_wait(smem_u32(&full[u % RING]), (uint32_t)(u / RING) & 1u)) {
@@ -138,6 +148,13 @@ __global__ void __launch_bounds__(QB * 16) k_attn_block(const int64_t* __restric
     __syncthreads();
     return s_abort == 0;
   };
+  // every value of the page in ring stage u fits in int32 (a block-wide vote)
+  auto page_fits = [&](int u) -> bool {
+    const int64_t* pg = (const int64_t*)(ringp + (u % RING) * PB);
+    bool f = true;
+    for (int i = tid; i < PAGE * DH; i += NT) f &= pg[i] == (int64_t)(int32_t)pg[i];
+    return __syncthreads_and(f) != 0;
+  };
   auto release = [&]() {
     __syncthreads();
     if (tid == 0 && issued < uses) {
@@ -146,62 +163,155 @@ __global__ void __launch_bounds__(QB * 16) k_attn_block(const int64_t* __restric
     }
   };
   const bool live = qi < nreal && !bad;
-  // ---- pass 1: scores of keys j <= pq (thread: position qi, key kk of each page)
-  int64_t mx = INT64_MIN;
+  // position of query qq of the block (the last key it attends to)
+  auto qpos = [&](int qq) { return MODE == 0 ? p0 + (int)blockIdx.x * QB + qq : pq; };
+  // Register-tiled form (int32 pages): thread = (key kk1, slice sl); it holds
+  // the slice of every query in registers and reads each K element once for
+  // all of them.  S1 = 2 * QB slices per key, EPS elements per slice.
+  constexpr int S1 = NT / PAGE, EPS = DH / S1;
+  static_assert(S1 == 2 * QB, "two slice lanes per query after the reduce-scatter");
+  const int kk1 = tid / S1, sl = tid % S1;
+  __syncthreads();  // qfit complete
+  bool qall = true;
+  for (int qq = 0; qq < QB; ++qq) qall &= qfit[qq] != 0;
+  int qreg[QB][EPS];
+#pragma unroll
+  for (int qq = 0; qq < QB; ++qq)
+#pragma unroll
+    for (int i = 0; i < EPS; ++i) qreg[qq][i] = (int)qs[qq * DH + i * S1 + sl];
+  // ---- pass 1: scores of keys j <= (position of the query)
   bool ok = true;
+  constexpr int HD = DH / 2;
   for (int pi = 0; pi < npg && ok; ++pi) {
     if (!(ok = wait_use(pi))) break;
+    const bool fast = page_fits(pi) && qall;
     const int64_t* kp = (const int64_t*)(ringp + (pi % RING) * PB);
-    const int j = pi * PAGE + kk;
-    if (live && j <= pq) {
-      const int64_t* kr = kp + kk * DH;
-      const int64_t* qr = qs + qi * DH;
-      uint64_t acc = 0;
-#pragma unroll 8
-      for (int e0 = 0; e0 < DH; ++e0) {
-        const int e = (e0 + kk) & (DH - 1);  // rotated so the 16 key rows hit different banks
-        acc += (uint64_t)qr[e] * (uint64_t)kr[e];
+    if (fast) {
+      // slice sl takes elements i * S1 + sl: the lanes of a key read 16 different banks
+      const int* k32 = (const int*)(kp + kk1 * DH + sl);
+      int kv[EPS];
+#pragma unroll
+      for (int i = 0; i < EPS; ++i) kv[i] = k32[2 * i * S1];
+      uint64_t v[QB];
+#pragma unroll
+      for (int qq = 0; qq < QB; ++qq) {
+        int64_t acc = 0;
+#pragma unroll
+        for (int i = 0; i < EPS; ++i) acc += (int64_t)qreg[qq][i] * (int64_t)kv[i];
+        v[qq] = (uint64_t)acc;
       }
-      const int64_t s = attn_score((int64_t)acc, attn_scale);
-      sc[qi * Tp + j] = s;
-      mx = s > mx ? s : mx;
+      // reduce-scatter over the S1 lanes of this key: lane sl ends with the
+      // whole dot of query sl / 2 (wrapping sums, exact)
+#pragma unroll
+      for (int st = 0, m = S1 / 2; m >= 1; ++st, m >>= 1) {
+        const int cnt = QB >> st;
+        if (cnt > 1) {
+          const bool up = (sl & m) != 0;
+#pragma unroll
+          for (int i = 0; i < cnt / 2; ++i) {
+            const uint64_t mine = up ? v[cnt / 2 + i] : v[i];
+            const uint64_t other = up ? v[i] : v[cnt / 2 + i];
+            v[i] = mine + (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)other, m);
+          }
+        } else {
+          v[0] += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v[0], m);
+        }
+      }
+      const int qq = sl >> 1, j = pi * PAGE + kk1;
+      if ((sl & 1) == 0 && qq < nreal && !bad && j <= qpos(qq)) sc[qq * Tp + j] = attn_score((int64_t)v[0], attn_scale);
+    } else {
+      // general form (64-bit products): warp = query qi, lane = key kk of the
+      // page and half hh of the elements, halves summed by a shuffle
+      const int j = pi * PAGE + kk;
+      const int64_t* kr = kp + kk * DH + hh * HD;
+      const int64_t* qr = qs + qi * DH + hh * HD;
+      uint64_t a0 = 0, a1 = 0;
+      if (live && j <= pq) {
+#pragma unroll 4
+        for (int e0 = 0; e0 < HD; e0 += 2) {
+          const int e = (e0 + 2 * kk) & (HD - 1);
+          a0 += (uint64_t)qr[e] * (uint64_t)kr[e];
+          a1 += (uint64_t)qr[e + 1] * (uint64_t)kr[e + 1];
+        }
+      }
+      uint64_t acc = a0 + a1;
+      acc += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)acc, 16);
+      if (live && j <= pq && hh == 0) sc[qi * Tp + j] = attn_score((int64_t)acc, attn_scale);
     }
     release();
   }
-  // ---- pass 2: exact max and sum of exps per position; pass 3: weights
-  mx = hmax16(mx);
+  __syncthreads();
+  // ---- pass 2: exact max and sum of exps per position (warp = query qi)
   const int Tq = pq + 1;
+  int64_t mx = INT64_MIN;
+  if (ok && live)
+    for (int jj = lane; jj < Tq; jj += 32) mx = sc[qi * Tp + jj] > mx ? sc[qi * Tp + jj] : mx;
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const int64_t o2 = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)mx, m);
+    mx = o2 > mx ? o2 : mx;
+  }
   uint64_t su = 0;
   if (ok && live)
-    for (int j = kk; j < Tq; j += 16) {
-      const int64_t ex = integer_exp(wsub(sc[qi * Tp + j], mx), lut);
-      sc[qi * Tp + j] = ex;
+    for (int jj = lane; jj < Tq; jj += 32) {
+      const int64_t ex = integer_exp(wsub(sc[qi * Tp + jj], mx), lut);
+      sc[qi * Tp + jj] = ex;
       su += (uint64_t)ex;
     }
-  const int64_t gsum = (int64_t)hsum16(su);
-  if (ok && live)
-    for (int j = kk; j < Tq; j += 16) {
-      int64_t w;
-      if (Tq == 1) w = ONE;
-      else if (gsum == 0) w = ONE / Tq;
-      else w = wmul(sc[qi * Tp + j], ONE) / gsum;
-      sc[qi * Tp + j] = w;
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) su += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)su, m);
+  const int64_t gsum = (int64_t)su;
+  // ---- pass 3: weights in [0, ONE]; zero past each position's last key
+  if (ok)
+    for (int jj = lane; jj < Tp; jj += 32) {
+      int64_t w = 0;
+      if (live && jj < Tq) {
+        if (Tq == 1) w = ONE;
+        else if (gsum == 0) w = ONE / Tq;
+        else w = wmul(sc[qi * Tp + jj], ONE) / gsum;
+      }
+      sc[qi * Tp + jj] = w;
     }
   __syncthreads();
-  // ---- value pass: thread = position qi, elements kk + 16 m
-  uint64_t o[EPT];
+  // ---- value pass.  Register-tiled form (int32 pages): thread = element
+  // slice es (elements es + 32 i), 8 queries (qb8 .. qb8 + 7), keys kg, kg + 8
+  // of each page; general form: warp = query qi, lane = elements lane + 32 m.
+  constexpr int EPV = DH / 32, QH = QB / 8;
+  const int es = tid & 31, rest = tid >> 5, kg = rest / QH, qb8 = (rest % QH) * 8;
+  uint64_t ot[8][EPV];
 #pragma unroll
-  for (int m = 0; m < EPT; ++m) o[m] = 0;
+  for (int qq = 0; qq < 8; ++qq)
+#pragma unroll
+    for (int i = 0; i < EPV; ++i) ot[qq][i] = 0;
+  uint64_t o[EPV];
+#pragma unroll
+  for (int m = 0; m < EPV; ++m) o[m] = 0;
   for (int pi = 0; pi < npg && ok; ++pi) {
     const int u = npg + pi;
     if (!(ok = wait_use(u))) break;
+    const bool fast = page_fits(u);
     const int64_t* vp = (const int64_t*)(ringp + (u % RING) * PB);
-    if (live) {
+    if (fast) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int k = kg + 8 * h, j = pi * PAGE + k;
+        const int* v32 = (const int*)(vp + k * DH + es);
+        int vv[EPV];
+#pragma unroll
+        for (int i = 0; i < EPV; ++i) vv[i] = v32[64 * i];
+#pragma unroll
+        for (int qq = 0; qq < 8; ++qq) {
+          const int64_t w = sc[(qb8 + qq) * Tp + j];  // 0 past the position's last key
+#pragma unroll
+          for (int i = 0; i < EPV; ++i) ot[qq][i] += (uint64_t)((w * (int64_t)vv[i]) >> FRAC_BITS);
+        }
+      }
+    } else if (live) {
       const int kmax = min(PAGE, Tq - pi * PAGE);
       for (int k = 0; k < kmax; ++k) {
         const int64_t w = sc[qi * Tp + pi * PAGE + k];
 #pragma unroll
-        for (int m = 0; m < EPT; ++m) o[m] += (uint64_t)mulshr(w, vp[k * DH + kk + 16 * m]);
+        for (int m = 0; m < EPV; ++m) o[m] += (uint64_t)mulshr(w, vp[k * DH + lane + 32 * m]);
       }
     }
     release();
@@ -209,20 +319,36 @@ __global__ void __launch_bounds__(QB * 16) k_attn_block(const int64_t* __restric
   // copies in flight (only after an abort) must land before the CTA exits
   if (tid == 0)
     for (int u = max(0, issued - RING); u < issued; ++u) mbar_wait(smem_u32(&full[u % RING]), (uint32_t)(u / RING) & 1u);
-  // ---- limb planes of the W_o operand (zeros for padding slots)
+  // ---- both forms' partial outputs summed in shared memory (the idle ring)
+  __syncthreads();
+  unsigned long long* osm = (unsigned long long*)ringp;  // [QB][DH]
+  for (int i = tid; i < QB * DH; i += NT) osm[i] = 0;
+  __syncthreads();
+#pragma unroll
+  for (int qq = 0; qq < 8; ++qq)
+#pragma unroll
+    for (int i = 0; i < EPV; ++i)
+      if (ot[qq][i]) atomicAdd(osm + (qb8 + qq) * DH + es + 32 * i, (unsigned long long)ot[qq][i]);
+#pragma unroll
+  for (int m = 0; m < EPV; ++m)
+    if (o[m]) atomicAdd(osm + qi * DH + lane + 32 * m, (unsigned long long)o[m]);
+  __syncthreads();
+  // ---- limb planes of the W_o operand (zeros for padding slots and dead queries)
   int need = 0;
-  if (slot < B && (MODE == 0 || qi < G)) {
+  for (int i = tid; i < QB * DH; i += NT) {
+    const int qq = i / DH, e = i - qq * DH;
+    const int sl2 = MODE == 0 ? (int)blockIdx.x * QB + qq : slot;
+    const int h2 = MODE == 0 ? hq : kvh * G + qq;
+    if (sl2 >= B || (MODE == 1 && qq >= G)) continue;
+    int8_t dg[8];
+    int nl = 0;
+    if (qq < nreal && !bad && ok) nl = limb_split8((int64_t)osm[i], dg);
+    else
 #pragma unroll
-    for (int m = 0; m < EPT; ++m) {
-      int8_t dg[8];
-      const int nl = (live && ok) ? limb_split8((int64_t)o[m], dg) : 0;
-      if (!(live && ok))
+      for (int l = 0; l < 8; ++l) dg[l] = 0;
+    need = nl > need ? nl : need;
 #pragma unroll
-        for (int l = 0; l < 8; ++l) dg[l] = 0;
-      need = nl > need ? nl : need;
-#pragma unroll
-      for (int l = 0; l < 8; ++l) X[limb_row(l, slot, B) * d + hq * DH + kk + 16 * m] = dg[l];
-    }
+    for (int l = 0; l < 8; ++l) X[limb_row(l, sl2, B) * d + h2 * DH + e] = dg[l];
   }
   need = __reduce_max_sync(0xffffffffu, need);
   if ((tid & 31) == 0 && need) atomicMax(&s_need, need);
@@ -253,7 +379,7 @@ int launch(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt
   const dim3 grid = MODE == 0 ? dim3((B + QB - 1) / QB, n_heads) : dim3(B, n_kv);
   // a position beyond the score buffer is reported (ARCB_ERR_SEQ_OVERFLOW), never written past it
   const int cap = max_T < Tp ? max_T : Tp;
-  return launch_k(k_attn_block<QB, DH, MODE>, grid, dim3(QB * 16), smem, st, q, Kc, Vc, pt, pt_stride, pos, nq, p0,
+  return launch_k(k_attn_block<QB, DH, MODE>, grid, dim3(QB * 32), smem, st, q, Kc, Vc, pt, pt_stride, pos, nq, p0,
                   n_heads, n_kv, attn_scale, cap, B, ring, X, lmax, err);
 }
 

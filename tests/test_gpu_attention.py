@@ -1,8 +1,7 @@
 """Paged decode attention kernels against a numpy restatement of the
 reference's integer attention (spec.softmax; scores ((q.k >> 16) * scale)
->> 16 with wrapping dots; per-term (w * v) >> 16): the grouped-query form
-(one cluster per KV head, used from 8 slots up), the TMA-fed page-ring form
-per query head and the per-thread-load form, every cluster size, GQA with
+>> 16 with wrapping dots; per-term (w * v) >> 16): the TMA-fed page-ring
+form per query head and the per-thread-load form, every cluster size, GQA with
 1, 2, 4 and 8 query heads per KV head, several slots of different lengths
 over a shuffled page table, and magnitudes that wrap."""
 import numpy as np
@@ -35,7 +34,7 @@ def _reference(q, K, V, pt, pos, n_heads, n_kv, dh, scale):
     return out
 
 
-@pytest.mark.parametrize("form", ["gqa", "paged", "plain"])
+@pytest.mark.parametrize("form", ["paged", "plain"])
 @pytest.mark.parametrize("cluster", [1, 2, 4, 8])
 @pytest.mark.parametrize("dh,n_heads,n_kv,lens,mag", [
     (128, 4, 4, [386], 1 << 18),
@@ -67,14 +66,12 @@ def test_attention_matches_reference(form, cluster, dh, n_heads, n_kv, lens, mag
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     o = torch.zeros(B, n_heads * dh, dtype=torch.int64, device=dev)
     ops.set_attn_paged(form != "plain")
-    ops.set_attn_gqa(form == "gqa")
     try:
         ops.attn(t(q), t(K), t(V), t(pt), t(pos), n_heads, n_kv, dh, scale, B, X, lm, max_T, err, o_out=o,
                  cluster=cluster)
         torch.cuda.synchronize()
     finally:
         ops.set_attn_paged(True)
-        ops.set_attn_gqa(False)
     assert int(err.item()) == 0
     np.testing.assert_array_equal(o.cpu().numpy(), ref)
     planes, need = ops.limb_planes(ref)
