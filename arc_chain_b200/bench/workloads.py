@@ -81,21 +81,29 @@ def batched(model: str, n_requests: int, rank: int, world: int, comm, max_batch:
 def moe_decode(model: str, batch: int, prompt_len: int, gen_len: int, steps: int, warmup: int, rank: int = 0,
                world: int = 1, comm=None) -> dict:
     """MLA + MoE batched greedy decode; expert-parallel over `world` ranks
-    (weights generated on each device, experts g % world == rank)."""
+    (weights generated on each device, experts g % world == rank).  With a
+    token-dispatch communicator each rank owns batch / world of the
+    requests (its own attention, KV cache and dense layers) and the MoE
+    layers exchange tokens; otherwise every rank runs all `batch` tokens."""
     from arc_chain_b200.models import mla_moe_engine as me
 
     cfg = preset(model)
     cfg.max_seq = (prompt_len + gen_len + 2 + 15) // 16 * 16
     m = me.random_device(cfg, torch.device("cuda", torch.cuda.current_device()), 0, rank, world)
-    eng = me.MlaMoeEngine(m, n_pages=batch * ((cfg.max_seq + 15) // 16) + 4, comm=comm if world > 1 else None)
-    bb = eng.buffers(batch, gen_cap=gen_len)
+    dispatch = world > 1 and getattr(comm, "token_dispatch", False)
+    if dispatch and batch % world:
+        raise ValueError(f"batch {batch} does not split over {world} ranks")
+    local = batch // world if dispatch else batch
+    first = rank * local if dispatch else 0
+    eng = me.MlaMoeEngine(m, n_pages=local * ((cfg.max_seq + 15) // 16) + 4, comm=comm if world > 1 else None)
+    bb = eng.buffers(local, gen_cap=gen_len)
     rids = []
-    for i in range(batch):
+    for i in range(first, first + local):
         p = gen.seeded_prompt(prompt_len, cfg.vocab, 1 + i)
         rid = eng.new_request(1 + prompt_len + gen_len)
         eng.prefill(rid, [1] + p)
         rids.append((rid, p))
-    eng._reset_sampling(bb, [r for r, _ in rids], [p[-1] for _, p in rids], [prompt_len + 1] * batch, ())
+    eng._reset_sampling(bb, [r for r, _ in rids], [p[-1] for _, p in rids], [prompt_len + 1] * local, ())
     g = eng._graph_for(bb)
     for _ in range(warmup):
         g.replay()
@@ -115,6 +123,7 @@ def moe_decode(model: str, batch: int, prompt_len: int, gen_len: int, steps: int
             "unit": "tokens/s", "higher_is_better": True, "ms_per_step": round(ms / n, 4), "batch": batch,
             "steps": n, "warmup": warmup, "kernel_errors": err,
             "config": {"model": model, "prompt_len": prompt_len, "gen_len": gen_len, "parallelism": f"ep{world}",
+                       "slots_per_rank": local,
                        "comm": getattr(comm, "__class__", type(None)).__name__ if world > 1 else "none"}}
 
 

@@ -230,6 +230,8 @@ class MlaMoeEngine(Engine):
         c = model.cfg
         self.comm = comm or Comm()
         self.ep = getattr(self.comm, "ep", False)
+        # token dispatch: the trunk runs on this rank's own slots only
+        self.dispatch = getattr(self.comm, "token_dispatch", False)
         if self.ep and (self.comm.size != model.ep_size or self.comm.rank != model.ep_rank):
             raise ValueError("model's expert shard does not match the communicator's rank/size")
         if not self.ep and model.ep_size != 1:
@@ -254,6 +256,33 @@ class MlaMoeEngine(Engine):
             self._bufs[key] = MlaBuffers(self.m, B, self.max_pages, gen_cap)
         return self._bufs[key]
 
+    def _gathered(self, bb: MlaBuffers):
+        """Expert-GEMM operands over the N * B gathered slots of a token-
+        dispatch step: the gathered limb planes (written by every rank's
+        dispatch), the SwiGLU planes, split-K scratch and counters."""
+        gb = getattr(bb, "gath", None)
+        if gb is None:
+            c = self.m.cfg
+            d = c.d_model
+            G = c.n_experts + c.n_shared_experts
+            st = self.comm.state(bb, self.n_moe, d)
+            gb = type("Gathered", (), {})()
+            gb.NB = st.NB
+            dev = bb.h.device
+            bn = ops.fgemm_bn(gb.NB)
+            sub = min(bn, 32)
+            gb.Xm = torch.zeros(ops.limb_rows(gb.NB, bn), max(G * c.moe_d_ff, 16), dtype=I8, device=dev)
+            gb.mXg, gb.mXm = ops.TensorMap(st.Xg, bn, sub), ops.TensorMap(gb.Xm, bn, sub)
+            mmax = max(ly.egu.M for ly in self.m.layers if ly.egu is not None)
+            mmax = max(mmax, max(ly.edown.M for ly in self.m.layers if ly.edown is not None))
+            gb.P = torch.zeros(8 * gb.NB * mmax, dtype=torch.int32, device=dev)
+            gb.tiles = torch.zeros(ops.tile_counters(mmax, gb.NB), dtype=I32, device=dev)
+            gb.cnt = torch.zeros(1, dtype=I32, device=dev)
+            gb.gcnt = st.gcnt
+            gb.route = st.route
+            bb.gath = gb
+        return gb
+
     def _epis(self, bb: MlaBuffers):
         if bb.epis is not None:
             return bb.epis
@@ -270,13 +299,15 @@ class MlaMoeEngine(Engine):
                 e["down"] = ops.epi(ops.RESID, ly.down.s, bb.err, out=bb.h, ldo=d)
             else:
                 e["router"] = ops.epi(ops.STORE, ly.router.s, bb.err, out=bb.rlog, ldo=c.n_experts)
-                e["egu"] = ops.epi(ops.SWIGLU, ly.egu.s, bb.err, X=bb.Xm, ldx=G * c.moe_d_ff,
-                                   lmax_out=bb.cnt[4 * l + 3:4 * l + 4])
-                ed = ops.epi(ops.MOE_COMBINE, ly.edown.s, bb.err, out=bb.h, ldo=d, route=bb.route, route_ld=G)
+                gb = self._gathered(bb) if self.dispatch else None
+                e["egu"] = ops.epi(ops.SWIGLU, ly.egu.s, bb.err, X=gb.Xm if gb else bb.Xm, ldx=G * c.moe_d_ff,
+                                   lmax_out=gb.cnt if gb else bb.cnt[4 * l + 3:4 * l + 4])
+                ed = ops.epi(ops.MOE_COMBINE, ly.edown.s, bb.err, out=bb.h, ldo=d,
+                             route=gb.route if gb else bb.route, route_ld=G)
                 ed.grp_rows, ed.grp_koff = d, c.moe_d_ff
                 if self.ep:
                     # local group g is global expert rank + g * size
-                    ed.route = bb.route.data_ptr() + 8 * m.ep_rank
+                    ed.route = (gb.route if gb else bb.route).data_ptr() + 8 * m.ep_rank
                     ed.route_gs = m.ep_size
                     ed = self.comm.combine_epi(ed, bb, self._moe_index(l), self.n_moe, d)
                 e["edown"] = ed
@@ -285,7 +316,9 @@ class MlaMoeEngine(Engine):
         bb.epis = out
         return out
 
-    def forward(self, bb: MlaBuffers, B: int, with_logits: bool = True) -> None:
+    def forward(self, bb: MlaBuffers, B: int, with_logits: bool = True, span=None) -> None:
+        # span (a prefill chunk's extent) selects the dense model's chunk
+        # attention; MLA attention runs per position here
         m, c = self.m, self.m.cfg
         d, H = c.d_model, c.n_heads
         dn, dr, dv, r = c.qk_nope_dim, c.qk_rope_dim, c.v_head_dim, c.kv_lora_rank
@@ -312,8 +345,14 @@ class MlaMoeEngine(Engine):
             else:
                 ops.linear_gemm(ly.router, bb.mXd, B, c2, bb.P, bb.tiles, e["router"])
                 ops.moe_route(bb.rlog, c.n_experts, c.n_shared_experts, c.moe_top_k, B, bb.route)
-                ops.linear_gemm(ly.egu, bb.mXd, B, c2, bb.P, bb.tiles, e["egu"])
-                ops.linear_gemm(ly.edown, bb.mXm, B, c3, bb.P, bb.tiles, e["edown"])
+                if self.dispatch:
+                    gb = self._gathered(bb)
+                    self.comm.dispatch(bb, bb.Xd, c2, self.n_moe, d, gb.cnt)
+                    ops.linear_gemm(ly.egu, gb.mXg, gb.NB, gb.gcnt, gb.P, gb.tiles, e["egu"])
+                    ops.linear_gemm(ly.edown, gb.mXm, gb.NB, gb.cnt, gb.P, gb.tiles, e["edown"])
+                else:
+                    ops.linear_gemm(ly.egu, bb.mXd, B, c2, bb.P, bb.tiles, e["egu"])
+                    ops.linear_gemm(ly.edown, bb.mXm, B, c3, bb.P, bb.tiles, e["edown"])
                 if self.ep:
                     self.comm.after_combine(bb, self._moe_index(l), self.n_moe, d)
         if with_logits:

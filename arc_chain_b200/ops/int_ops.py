@@ -190,7 +190,7 @@ class Epi(C.Structure):
                 ("max_ctas", C.c_int), ("b_box", C.c_int), ("route_gs", C.c_int), ("peer_h", C.c_void_p),
                 ("peer_sig", C.c_void_p), ("pf_w", C.c_void_p), ("pf_M", C.c_int), ("pf_K", C.c_int),
                 ("pf_tiles", C.c_int), ("sched", C.c_int), ("nrm_gamma", C.c_void_p), ("nrm_ngamma", C.c_int),
-                ("nrm_X", C.c_void_p), ("nrm_lmax", C.c_void_p), ("nrm_cnt", C.c_void_p)]
+                ("nrm_X", C.c_void_p), ("nrm_lmax", C.c_void_p), ("nrm_cnt", C.c_void_p), ("ep_rows", C.c_int)]
 
 
 PARTIAL, STORE, RESID, QKV, SWIGLU, MOE_COMBINE, STORE_PEERS = 0, 1, 2, 3, 4, 5, 6
@@ -472,6 +472,17 @@ def ep_wait_apply(cnt, epoch, per_call: int, h, delta, done, err) -> None:
     _count()
     check(lib().arcb_ep_wait_apply(_p(cnt), _p(epoch), per_call, _p(h), _p(delta), 0 if h is None else h.numel(),
                                    _p(done), _p(err), _s()), "ep_wait_apply")
+
+
+def ep_dispatch(X, B: int, ldx: int, route, G: int, lcnt, rank: int, npeers: int, peer_X, peer_route, peer_counts,
+                peer_sig, cnt, epoch, gcnt, zero_cnt, blocks: int, err) -> None:
+    """Expert-parallel token dispatch: this rank's limb planes and routing
+    weights into every rank's gathered buffers, then a bounded wait for all
+    ranks' (csrc/kernels/ep_ops.cu)."""
+    _count()
+    check(lib().arcb_ep_dispatch(_p(X), B, ldx, _p(route), G, _p(lcnt), rank, npeers, _p(peer_X), _p(peer_route),
+                                 _p(peer_counts), _p(peer_sig), _p(cnt), _p(epoch), _p(gcnt), _p(zero_cnt), blocks,
+                                 _p(err), _s()), "ep_dispatch")
 
 
 def set_prefetch(epi: Epi, next_lin, tiles: int) -> None:

@@ -79,6 +79,10 @@ class Scheduler:
     def __init__(self, engine: Engine, max_batch: int = 32, prefill_chunk: int = 1024,
                  eos: Sequence[int] = (), gen_cap: Optional[int] = None, use_graph: bool = True,
                  metrics_sink: Optional[Callable[[dict], None]] = None, keep_metrics: int = 10000):
+        if getattr(engine, "dispatch", False):
+            # token-dispatch expert parallelism needs every rank in lockstep
+            raise ValueError("the continuous-batching scheduler needs a replicated-token communicator "
+                             "(EpFusedComm / EpNcclComm), not EpDispatchComm")
         self.e = engine
         self.max_batch = max_batch
         self.prefill_chunk = prefill_chunk

@@ -58,6 +58,9 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--gen-len", type=int, default=256)
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
+    ap.add_argument("--ep-layout", default="dispatch", choices=["dispatch", "replicated"],
+                    help="moe workload, N > 1: token dispatch (each rank owns batch / N requests) or every "
+                         "token on every rank")
     ap.add_argument("--fuse-logits", type=int, default=0,
                     help="with --comm fused: the LM head also all-gathers its logits in-kernel")
     ap.add_argument("--fuse-norm", type=int, default=-1,
@@ -125,9 +128,11 @@ def main():
             elif args.workload == "moe":
                 ep_comm = None
                 if world > 1:
-                    from arc_chain_b200.parallel.ep import EpFusedComm, EpNcclComm
+                    from arc_chain_b200.parallel.ep import EpDispatchComm, EpFusedComm, EpNcclComm
 
-                    ep_comm = EpFusedComm() if args.comm == "fused" else EpNcclComm()
+                    # token dispatch by default; "replicated" runs every token on every rank
+                    ep_comm = (EpNcclComm() if args.comm == "nccl" else
+                               EpFusedComm() if args.ep_layout == "replicated" else EpDispatchComm())
                 out = wl.moe_decode("dsv2lite", args.batch or 32, args.prompt_len if args.prompt_len != 128 else 512,
                                     256, args.steps, args.warmup, rank, world, ep_comm)
             else:

@@ -23,7 +23,7 @@
 //    kvh * G + i (G = n_heads / n_kv <= QB) of slot blockIdx.x at position
 //    pos[slot], pages pt[slot]: the G heads that share a KV head read each of
 //    its pages once, instead of once per head.
-// QB * 32 threads: one warp per query.  Output: limb planes of the W_o
+// QB * 32 * WM threads: WM warps per query.  Output: limb planes of the W_o
 // operand (limb_row layout of B slots) and the limb count (atomicMax).  The
 // page ring holds `ring` pages (set per launch from the shared memory the
 // scores leave).
@@ -31,8 +31,13 @@
 // Exact int32 fast path: a 64-bit wrapping multiply-add costs about five
 // integer instructions.  When a query row and a whole K page fit in int32,
 // every product fits exactly in int64, so one widening multiply-add per
-// element gives the identical wrapping sum; likewise a weight (at most ONE)
-// times a V value that fits in int32.  Each page is checked when it lands.
+// element gives the identical wrapping sum.  For a V page that fits in int32
+// the value term runs in 32-bit arithmetic: with v = vh * 2^16 + vl (vh the
+// arithmetic high half, 0 <= vl < 2^16) and 0 <= w <= ONE = 2^16,
+//   (w * v) >> 16 = w * vh + ((w * vl) >> 16)      (w * vl < 2^32, unsigned)
+// and since the weights of one query sum to at most ONE, every partial sum of
+// w * vh lies in [-2^31, 2^31) and of ((w * vl) >> 16) in [0, 2^16]: both
+// int32 accumulators are exact.  Each page is checked when it lands.
 #include "common.cuh"
 #include "lut.cuh"
 
@@ -63,21 +68,24 @@ __device__ __forceinline__ int64_t hmax16(int64_t v) {
   return v;
 }
 
-template <int QB, int DH, int MODE>
-__global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
+template <int QB, int DH, int MODE, int WM>
+__global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
                                                         const int64_t* __restrict__ Vc, const int* __restrict__ pt,
                                                         int pt_stride, const int* __restrict__ pos, int nq, int p0,
                                                         int n_heads, int n_kv, int64_t attn_scale, int max_T, int B,
                                                         int RING, int8_t* __restrict__ X, int* __restrict__ lmax,
                                                         int* __restrict__ err) {
-  constexpr int NT = QB * 32;
+  constexpr int NT = QB * 32 * WM;
   constexpr int PB = PAGE * DH * 8;  // one page of one KV head
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ int64_t lut[EXP_LUT_N];
   __shared__ __align__(8) uint64_t full[MAX_RING];
   __shared__ int s_need, s_abort;
   __shared__ int qfit[QB];  // query row fits in int32
-  const int tid = threadIdx.x, qi = tid >> 5, lane = tid & 31, kk = lane & 15, hh = lane >> 4;
+  __shared__ int64_t red[WM][QB];
+  // general forms: warp (wpart, qi) = part wpart of query qi
+  const int tid = threadIdx.x, qi = (tid >> 5) % QB, wpart = (tid >> 5) / QB, lane = tid & 31, kk = lane & 15,
+            hh = lane >> 4;
   const int G = n_heads / n_kv;
   const int d = n_heads * DH;
   const uint32_t ring = (smem_u32(dsm) + 127u) & ~127u;
@@ -167,9 +175,10 @@ __global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restric
   auto qpos = [&](int qq) { return MODE == 0 ? p0 + (int)blockIdx.x * QB + qq : pq; };
   // Register-tiled form (int32 pages): thread = (key kk1, slice sl); it holds
   // the slice of every query in registers and reads each K element once for
-  // all of them.  S1 = 2 * QB slices per key, EPS elements per slice.
-  constexpr int S1 = NT / PAGE, EPS = DH / S1;
-  static_assert(S1 == 2 * QB, "two slice lanes per query after the reduce-scatter");
+  // all of them.  S1 = 2 * QB * WM slices per key, EPS elements per slice;
+  // after the reduce-scatter LQ lanes hold each query's dot.
+  constexpr int S1 = NT / PAGE, EPS = DH / S1, LQ = S1 / QB;
+  static_assert(S1 % QB == 0 && S1 <= 32 && EPS >= 1, "slice lanes of a key within one warp");
   const int kk1 = tid / S1, sl = tid % S1;
   __syncthreads();  // qfit complete
   bool qall = true;
@@ -201,7 +210,7 @@ __global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restric
         v[qq] = (uint64_t)acc;
       }
       // reduce-scatter over the S1 lanes of this key: lane sl ends with the
-      // whole dot of query sl / 2 (wrapping sums, exact)
+      // whole dot of query sl / LQ (wrapping sums, exact)
 #pragma unroll
       for (int st = 0, m = S1 / 2; m >= 1; ++st, m >>= 1) {
         const int cnt = QB >> st;
@@ -217,8 +226,8 @@ __global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restric
           v[0] += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v[0], m);
         }
       }
-      const int qq = sl >> 1, j = pi * PAGE + kk1;
-      if ((sl & 1) == 0 && qq < nreal && !bad && j <= qpos(qq)) sc[qq * Tp + j] = attn_score((int64_t)v[0], attn_scale);
+      const int qq = sl / LQ, j = pi * PAGE + kk1;
+      if (sl % LQ == 0 && qq < nreal && !bad && j <= qpos(qq)) sc[qq * Tp + j] = attn_score((int64_t)v[0], attn_scale);
     } else {
       // general form (64-bit products): warp = query qi, lane = key kk of the
       // page and half hh of the elements, halves summed by a shuffle
@@ -226,7 +235,7 @@ __global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restric
       const int64_t* kr = kp + kk * DH + hh * HD;
       const int64_t* qr = qs + qi * DH + hh * HD;
       uint64_t a0 = 0, a1 = 0;
-      if (live && j <= pq) {
+      if (live && wpart == 0 && j <= pq) {
 #pragma unroll 4
         for (int e0 = 0; e0 < HD; e0 += 2) {
           const int e = (e0 + 2 * kk) & (HD - 1);
@@ -236,34 +245,51 @@ __global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restric
       }
       uint64_t acc = a0 + a1;
       acc += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)acc, 16);
-      if (live && j <= pq && hh == 0) sc[qi * Tp + j] = attn_score((int64_t)acc, attn_scale);
+      if (live && wpart == 0 && j <= pq && hh == 0) sc[qi * Tp + j] = attn_score((int64_t)acc, attn_scale);
     }
     release();
   }
   __syncthreads();
-  // ---- pass 2: exact max and sum of exps per position (warp = query qi)
+  // ---- pass 2: exact max and sum of exps per position (WM warps per query,
+  // partial results combined through shared memory)
   const int Tq = pq + 1;
+  const int j0 = wpart * 32 + lane;
+  constexpr int JS = 32 * WM;
   int64_t mx = INT64_MIN;
   if (ok && live)
-    for (int jj = lane; jj < Tq; jj += 32) mx = sc[qi * Tp + jj] > mx ? sc[qi * Tp + jj] : mx;
+    for (int jj = j0; jj < Tq; jj += JS) mx = sc[qi * Tp + jj] > mx ? sc[qi * Tp + jj] : mx;
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) {
     const int64_t o2 = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)mx, m);
     mx = o2 > mx ? o2 : mx;
   }
+  if (WM > 1) {
+    if (lane == 0) red[wpart][qi] = mx;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < WM; ++w) mx = red[w][qi] > mx ? red[w][qi] : mx;
+    __syncthreads();
+  }
   uint64_t su = 0;
   if (ok && live)
-    for (int jj = lane; jj < Tq; jj += 32) {
+    for (int jj = j0; jj < Tq; jj += JS) {
       const int64_t ex = integer_exp(wsub(sc[qi * Tp + jj], mx), lut);
       sc[qi * Tp + jj] = ex;
       su += (uint64_t)ex;
     }
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) su += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)su, m);
+  if (WM > 1) {
+    if (lane == 0) red[wpart][qi] = (int64_t)su;
+    __syncthreads();
+    su = 0;
+#pragma unroll
+    for (int w = 0; w < WM; ++w) su += (uint64_t)red[w][qi];
+  }
   const int64_t gsum = (int64_t)su;
   // ---- pass 3: weights in [0, ONE]; zero past each position's last key
   if (ok)
-    for (int jj = lane; jj < Tp; jj += 32) {
+    for (int jj = j0; jj < Tp; jj += JS) {
       int64_t w = 0;
       if (live && jj < Tq) {
         if (Tq == 1) w = ONE;
@@ -274,18 +300,22 @@ __global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restric
     }
   __syncthreads();
   // ---- value pass.  Register-tiled form (int32 pages): thread = element
-  // slice es (elements es + 32 i), 8 queries (qb8 .. qb8 + 7), keys kg, kg + 8
-  // of each page; general form: warp = query qi, lane = elements lane + 32 m.
-  constexpr int EPV = DH / 32, QH = QB / 8;
-  const int es = tid & 31, rest = tid >> 5, kg = rest / QH, qb8 = (rest % QH) * 8;
-  uint64_t ot[8][EPV];
+  // slice es (elements es + 32 i), QG queries (qg0 .. qg0 + QG - 1), KPT keys
+  // of each page; hi/lo int32 accumulators (exact, see the header).  General
+  // form: warp (0, qi) = query qi, lane = elements lane + 32 m.
+  constexpr int EPV = DH / 32, QG = DH == 128 ? 4 : 8, QH = QB / QG, KG = NT / 32 / QH, KPT = PAGE / KG;
+  static_assert(QB % QG == 0 && PAGE % KG == 0, "value-pass tiling");
+  const int es = tid & 31, rest = tid >> 5, kg = rest / QH, qg0 = (rest % QH) * QG;
+  const int* w32 = (const int*)sc;  // weight (qq, j): low word of sc[qq * Tp + j]
+  int acch[QG][EPV];
+  unsigned accl[QG][EPV];
 #pragma unroll
-  for (int qq = 0; qq < 8; ++qq)
+  for (int qq = 0; qq < QG; ++qq)
 #pragma unroll
-    for (int i = 0; i < EPV; ++i) ot[qq][i] = 0;
-  uint64_t o[EPV];
-#pragma unroll
-  for (int m = 0; m < EPV; ++m) o[m] = 0;
+    for (int i = 0; i < EPV; ++i) acch[qq][i] = 0, accl[qq][i] = 0;
+  // general-form partial outputs: the query rows' area, free after pass 1
+  unsigned long long* osl = (unsigned long long*)qs;
+  for (int i = tid; i < QB * DH; i += NT) osl[i] = 0;
   for (int pi = 0; pi < npg && ok; ++pi) {
     const int u = npg + pi;
     if (!(ok = wait_use(u))) break;
@@ -293,26 +323,39 @@ __global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restric
     const int64_t* vp = (const int64_t*)(ringp + (u % RING) * PB);
     if (fast) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int k = kg + 8 * h, j = pi * PAGE + k;
+      for (int h = 0; h < KPT; ++h) {
+        const int k = kg + KG * h, j = pi * PAGE + k;
         const int* v32 = (const int*)(vp + k * DH + es);
-        int vv[EPV];
+        int vh[EPV];
+        unsigned vl[EPV];
 #pragma unroll
-        for (int i = 0; i < EPV; ++i) vv[i] = v32[64 * i];
+        for (int i = 0; i < EPV; ++i) {
+          const int v = v32[64 * i];
+          vh[i] = v >> 16;
+          vl[i] = (unsigned)v & 0xffffu;
+        }
 #pragma unroll
-        for (int qq = 0; qq < 8; ++qq) {
-          const int64_t w = sc[(qb8 + qq) * Tp + j];  // 0 past the position's last key
+        for (int qq = 0; qq < QG; ++qq) {
+          const int w = w32[2 * ((qg0 + qq) * Tp + j)];  // 0 past the position's last key
 #pragma unroll
-          for (int i = 0; i < EPV; ++i) ot[qq][i] += (uint64_t)((w * (int64_t)vv[i]) >> FRAC_BITS);
+          for (int i = 0; i < EPV; ++i) {
+            acch[qq][i] += w * vh[i];
+            accl[qq][i] += ((unsigned)w * vl[i]) >> 16;
+          }
         }
       }
-    } else if (live) {
+    } else if (live && wpart == 0) {
       const int kmax = min(PAGE, Tq - pi * PAGE);
+      uint64_t o[EPV];
+#pragma unroll
+      for (int m = 0; m < EPV; ++m) o[m] = 0;
       for (int k = 0; k < kmax; ++k) {
         const int64_t w = sc[qi * Tp + pi * PAGE + k];
 #pragma unroll
         for (int m = 0; m < EPV; ++m) o[m] += (uint64_t)mulshr(w, vp[k * DH + lane + 32 * m]);
       }
+#pragma unroll
+      for (int m = 0; m < EPV; ++m) osl[qi * DH + lane + 32 * m] += o[m];  // one warp per query row
     }
     release();
   }
@@ -325,13 +368,14 @@ __global__ void __launch_bounds__(QB * 32) k_attn_block(const int64_t* __restric
   for (int i = tid; i < QB * DH; i += NT) osm[i] = 0;
   __syncthreads();
 #pragma unroll
-  for (int qq = 0; qq < 8; ++qq)
+  for (int qq = 0; qq < QG; ++qq)
 #pragma unroll
-    for (int i = 0; i < EPV; ++i)
-      if (ot[qq][i]) atomicAdd(osm + (qb8 + qq) * DH + es + 32 * i, (unsigned long long)ot[qq][i]);
-#pragma unroll
-  for (int m = 0; m < EPV; ++m)
-    if (o[m]) atomicAdd(osm + qi * DH + lane + 32 * m, (unsigned long long)o[m]);
+    for (int i = 0; i < EPV; ++i) {
+      const int64_t t = (int64_t)acch[qq][i] + (int64_t)accl[qq][i];
+      if (t) atomicAdd(osm + (qg0 + qq) * DH + es + 32 * i, (unsigned long long)t);
+    }
+  for (int i = tid; i < QB * DH; i += NT)
+    if (osl[i]) atomicAdd(osm + i, osl[i]);
   __syncthreads();
   // ---- limb planes of the W_o operand (zeros for padding slots and dead queries)
   int need = 0;
@@ -360,7 +404,7 @@ static size_t smem_bytes(int QB, int DH, int Tp, int ring) {
   return 128 + (size_t)ring * PAGE * DH * 8 + (size_t)QB * DH * 8 + (size_t)QB * Tp * 8;
 }
 
-template <int QB, int DH, int MODE>
+template <int QB, int DH, int MODE, int WM>
 int launch(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride, const int* pos, int nq,
            int p0, int n_heads, int n_kv, int64_t attn_scale, int max_T, int B, int Tlim, int8_t* X, int* lmax,
            int* err, cudaStream_t st) {
@@ -371,7 +415,7 @@ int launch(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt
   if (smem > 220 * 1024) return -3;
   static size_t attr = 0;
   if (smem > attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_attn_block<QB, DH, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_attn_block<QB, DH, MODE, WM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return (int)e;
     attr = smem;
@@ -379,7 +423,7 @@ int launch(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt
   const dim3 grid = MODE == 0 ? dim3((B + QB - 1) / QB, n_heads) : dim3(B, n_kv);
   // a position beyond the score buffer is reported (ARCB_ERR_SEQ_OVERFLOW), never written past it
   const int cap = max_T < Tp ? max_T : Tp;
-  return launch_k(k_attn_block<QB, DH, MODE>, grid, dim3(QB * 32), smem, st, q, Kc, Vc, pt, pt_stride, pos, nq, p0,
+  return launch_k(k_attn_block<QB, DH, MODE, WM>, grid, dim3(QB * 32 * WM), smem, st, q, Kc, Vc, pt, pt_stride, pos, nq, p0,
                   n_heads, n_kv, attn_scale, cap, B, ring, X, lmax, err);
 }
 
@@ -406,14 +450,14 @@ int arcb_attn_prefill(const int64_t* q, const int64_t* Kc, const int64_t* Vc, co
   const int T = p0 + nq;
   const bool wide = T <= arcb_attn_prefill_max_T(dh, 16);
   if (dh == 128)
-    return wide ? ap::launch<16, 128, 0>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
+    return wide ? ap::launch<16, 128, 0, 1>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
                                          lmax, err, st)
-                : ap::launch<8, 128, 0>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
+                : ap::launch<8, 128, 0, 1>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
                                         lmax, err, st);
   if (dh == 64)
-    return wide ? ap::launch<16, 64, 0>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
+    return wide ? ap::launch<16, 64, 0, 1>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
                                         lmax, err, st)
-                : ap::launch<8, 64, 0>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
+                : ap::launch<8, 64, 0, 1>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
                                        lmax, err, st);
   return -2;
 }
@@ -428,10 +472,10 @@ int arcb_attn_gqa_block(const int64_t* q, const int64_t* Kc, const int64_t* Vc, 
   cudaStream_t st = (cudaStream_t)stream;
   if (n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > 8) return -2;
   if (dh == 128)
-    return ap::launch<8, 128, 1>(q, Kc, Vc, pt, pt_stride, pos, 0, 0, n_heads, n_kv, attn_scale, max_T, B, t_lim, X,
+    return ap::launch<8, 128, 1, 2>(q, Kc, Vc, pt, pt_stride, pos, 0, 0, n_heads, n_kv, attn_scale, max_T, B, t_lim, X,
                                  lmax, err, st);
   if (dh == 64)
-    return ap::launch<8, 64, 1>(q, Kc, Vc, pt, pt_stride, pos, 0, 0, n_heads, n_kv, attn_scale, max_T, B, t_lim, X,
+    return ap::launch<8, 64, 1, 2>(q, Kc, Vc, pt, pt_stride, pos, 0, 0, n_heads, n_kv, attn_scale, max_T, B, t_lim, X,
                                 lmax, err, st);
   return -2;
 }

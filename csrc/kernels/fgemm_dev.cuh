@@ -117,6 +117,11 @@ struct Epi {
   int8_t* nrm_X;
   int* nrm_lmax;
   int* nrm_cnt;
+  // Token-dispatch expert parallelism: with peer_h set and ep_rows > 0, the
+  // MOE_COMBINE add of gathered slot b goes only to its owner rank
+  // b / ep_rows, at row b % ep_rows of that rank's combine buffer (each rank
+  // owns ep_rows consecutive slots).  0 = add into every rank's buffer.
+  int ep_rows;
 };
 
 // Ring depth for decode-sized tiles (BN <= 32).  A 5-stage ring (two CTAs
@@ -235,7 +240,10 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
       if (w != 0) {
         const unsigned long long add = (unsigned long long)mulshr(w, v);
         const size_t off = (size_t)b * E.ldo + i;
-        if (E.peer_h) {
+        if (E.peer_h && E.ep_rows > 0) {
+          const int p = b / E.ep_rows;
+          atomicAdd((unsigned long long*)(E.peer_h[p] + (size_t)(b - p * E.ep_rows) * E.ldo + i), add);
+        } else if (E.peer_h) {
           for (int p = 0; p < E.npeers; ++p) atomicAdd((unsigned long long*)(E.peer_h[p] + off), add);
         } else {
           atomicAdd((unsigned long long*)(E.out + off), add);

@@ -1,6 +1,8 @@
 """Expert parallelism for the MLA + MoE decoder: the device generator with
-expert shards, and 2-rank runs (NCCL and fused peer-push combine) against
-the oracle."""
+expert shards, and 2-rank runs against the oracle: replicated tokens (NCCL
+and fused peer-push combine) and token dispatch (each rank decodes its own
+prompts; tokens are sent to the experts' ranks and combined on their
+owner)."""
 import json
 import os
 import subprocess
@@ -38,10 +40,10 @@ def test_device_generator_matches_host_shards(ep_size):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("comm", ["nccl", "fused"])
+@pytest.mark.parametrize("comm", ["nccl", "fused", "dispatch"])
 def test_ep2_matches_oracle(comm):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    port = 29600 + (os.getpid() % 200) + (7 if comm == "fused" else 0)
+    port = 29600 + (os.getpid() % 200) + {"nccl": 0, "fused": 7, "dispatch": 13}[comm]
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
            os.path.join(ROOT, "tests", "ep_worker.py"), "--comm", comm]
@@ -49,4 +51,5 @@ def test_ep2_matches_oracle(comm):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("{")][-1]
     res = json.loads(line)
-    assert res["ok_all_ranks"] and res["kernel_errors"] == 0 and res["checks"] == 12
+    assert res["ok_all_ranks"] and res["kernel_errors"] == 0
+    assert res["checks"] == (5 if comm == "dispatch" else 12)
