@@ -113,11 +113,10 @@ __global__ void k_ep_dispatch(const int8_t* __restrict__ X, int B, int ldx, cons
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) peer_counts[p][rank] = *lcnt;
   }
+  __threadfence_system();  // every thread's peer stores, before the CTA's arrival
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
+  if (threadIdx.x == 0)
     for (int p = 0; p < npeers; ++p) atomicAdd_system(peer_sig[p], 1ull);
-  }
   if (blockIdx.x == 0) {
     __shared__ int ok;
     if (threadIdx.x == 0) {
