@@ -154,7 +154,24 @@ def main():
         return
     if a.only == "optimeline":
         # per-op device time of one eager 7B decode step (CUDA events between launches)
-        print(json.dumps(op_timeline(fuse_norm=os.environ.get("ARCB_FUSE_NORM") == "1")), flush=True)
+        from arc_chain_b200.utils.clocks import ClockSampler
+
+        with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+            r = op_timeline(fuse_norm=os.environ.get("ARCB_FUSE_NORM") == "1")
+        r["clocks"] = clk.summary()
+        if r["rank"] == 0:
+            print(json.dumps(r), flush=True)
+        return
+    if a.only == "optimeline_moe":
+        # per-op device time of one eager MLA + MoE decode step (expert-parallel under torch.distributed.run)
+        from arc_chain_b200.utils.clocks import ClockSampler
+
+        with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+            r = op_timeline_moe(a.model or "dsv2lite", a.B if a.B > 1 else 32, a.T,
+                                layout=os.environ.get("ARCB_EP_LAYOUT", "dispatch"))
+        r["clocks"] = clk.summary()
+        if r["rank"] == 0:
+            print(json.dumps(r), flush=True)
         return
     if a.only == "large":
         # 70B-architecture shapes at prefill / batched sizes: time and int8 tensor rate
@@ -302,9 +319,10 @@ def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -
             cnt[lab] += 1
             prev = e
         eng.op_events = None
+    agg = _max_over_ranks(agg, world)
     out = {"world": world, "fuse_norm": eng._norm_fused(), "total_us": round(sum(agg.values()), 1),
            "per_op_us": {k: {"launches": cnt[k] // reps, "total": round(v, 1), "each": round(v / max(1, cnt[k] // reps), 2)}
-                         for k, v in agg.items()}}
+                         for k, v in agg.items()}, "rank": rank}
     if world > 1:
         import gc
 
@@ -315,6 +333,88 @@ def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -
         dist.destroy_process_group()
     return out
 
+
+
+def _max_over_ranks(agg: dict, world: int) -> dict:
+    """Per-label device times, each the maximum over the ranks (every rank
+    records the same labels in the same order)."""
+    if world <= 1:
+        return dict(agg)
+    import torch.distributed as dist
+
+    keys = list(agg)
+    t = torch.tensor([agg[k] for k in keys], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return dict(zip(keys, t.tolist()))
+
+
+def op_timeline_moe(model: str = "dsv2lite", B: int = 32, T: int = 512, reps: int = 3,
+                    layout: str = "dispatch") -> dict:
+    """Per-op device time of one eager MLA + MoE decode step over B slots in
+    total (every slot at position T - 1, distinct pages), expert-parallel over
+    the ranks of torch.distributed.run (token dispatch: B / N slots per rank;
+    replicated: all B on every rank), each op the maximum over ranks."""
+    import collections
+
+    import torch.distributed as dist
+
+    from arc_chain_b200.models import mla_moe_engine as me
+    from arc_chain_b200.models.config import preset
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank, comm = 0, None
+    if world > 1:
+        from arc_chain_b200.parallel import tp
+        from arc_chain_b200.parallel.ep import EpDispatchComm, EpFusedComm
+
+        rank, world = tp.init_distributed()
+        comm = EpDispatchComm() if layout == "dispatch" else EpFusedComm()
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = preset(model)
+    cfg.max_seq = (T + 16 + 15) // 16 * 16
+    local = B // world if (world > 1 and layout == "dispatch") else B
+    m = me.random_device(cfg, dev, 0, rank, world)
+    pps = cfg.max_seq // 16
+    eng = me.MlaMoeEngine(m, n_pages=local * pps + 4, comm=comm)
+    bb = eng.buffers(local, gen_cap=8)
+    bb.tokens.copy_(torch.arange(local, dtype=torch.int32) * 7 + 3 + rank)
+    bb.pos.fill_(T - 1)
+    bb.pt.copy_(torch.arange(local * pps, dtype=torch.int32).view(local, pps)[:, :bb.pt.shape[1]])
+    for _ in range(2):
+        eng.forward(bb, local, True)
+    agg, cnt = collections.defaultdict(float), collections.Counter()
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        eng.op_events = []
+        torch.cuda._sleep(80_000_000)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        eng.forward(bb, local, True)
+        torch.cuda.synchronize()
+        prev = e0
+        for lab, e in eng.op_events:
+            agg[lab] += prev.elapsed_time(e) * 1000 / reps
+            cnt[lab] += 1
+            prev = e
+        eng.op_events = None
+    agg = _max_over_ranks(agg, world)
+    out = {"model": model, "B": B, "slots_per_rank": local, "T": T, "world": world, "layout": layout,
+           "total_us": round(sum(agg.values()), 1), "kernel_errors": eng.check_errors(),
+           "per_op_us": {k: {"launches": cnt[k] // reps, "total": round(v, 1),
+                             "each": round(v / max(1, cnt[k] // reps), 2)} for k, v in agg.items()}, "rank": rank}
+    if world > 1:
+        import gc
+
+        eng._graphs.clear()
+        gc.collect()
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
 
 
 def op_timeline_batched(model: str = "llama70b", B: int = 64, T: int = 800, reps: int = 3) -> dict:

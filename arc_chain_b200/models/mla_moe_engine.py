@@ -246,6 +246,7 @@ class MlaMoeEngine(Engine):
         self._bufs = {}
         self._graphs = {}
         self._rid = 0
+        self.op_events = None  # a list: forward records (label, event) after each op
 
     def _moe_index(self, layer: int) -> int:
         return sum(1 for ly in self.m.layers[:layer] if ly.edown is not None)
@@ -325,37 +326,63 @@ class MlaMoeEngine(Engine):
         G = c.n_experts + c.n_shared_experts
         E = self._epis(bb)
         T = self.max_pages * PAGE
+        ev = self.op_events
+
+        def mark(label):
+            if ev is not None:
+                e_ = torch.cuda.Event(enable_timing=True)
+                e_.record()
+                ev.append((label, e_))
+
         ops.embed(bb.tokens, m.emb, m.emb_s, c.vocab, d, B, bb.h, bb.cnt, bb.ss)
+        mark("embed")
         for l, ly in enumerate(m.layers):
             c0, c1, c2, c3 = (bb.cnt[4 * l + i:4 * l + i + 1] for i in range(4))
             e = E[l]
             ops.rmsnorm_limbs(bb.h, ly.attn_norm, d, B, bb.Xd, c0)
+            mark("norm")
             ops.linear_gemm(ly.q, bb.mXd, B, c0, bb.P, bb.tiles, e["q"])
             ops.linear_gemm(ly.kva, bb.mXd, B, c0, bb.P, bb.tiles, e["kva"])
+            mark("q_kva")
             ops.mla_kv(bb.kva, r, dr, ly.kv_norm, self.kv.K[l], bb.pt, bb.pos, m.rope_cos, m.rope_sin,
                        self.max_seq, B, bb.err)
             ops.mla_q(bb.q, H, dn, dr, r, ly.uk, ly.uk_s, bb.pos, m.rope_cos, m.rope_sin, self.max_seq, B, bb.Q)
+            mark("mla_kv_q")
             ops.attn_mla(bb.Q, self.kv.K[l], bb.pt, bb.pos, H, self.dk, r, m.attn_scale, T, B, bb.oc, bb.err)
+            mark("attn")
             ops.mla_out(bb.oc, H, r, dv, ly.uv, ly.uv_s, B, bb.Xo, c1)
+            mark("mla_out")
             ops.linear_gemm(ly.wo, bb.mXo, B, c1, bb.P, bb.tiles, e["wo"])
+            mark("wo")
             ops.rmsnorm_limbs(bb.h, ly.ffn_norm, d, B, bb.Xd, c2)
+            mark("norm")
             if ly.gu is not None:
                 ops.linear_gemm(ly.gu, bb.mXd, B, c2, bb.P, bb.tiles, e["gu"])
                 ops.linear_gemm(ly.down, bb.mXf, B, c3, bb.P, bb.tiles, e["down"])
+                mark("dense_ffn")
             else:
                 ops.linear_gemm(ly.router, bb.mXd, B, c2, bb.P, bb.tiles, e["router"])
+                mark("router")
                 ops.moe_route(bb.rlog, c.n_experts, c.n_shared_experts, c.moe_top_k, B, bb.route)
+                mark("route")
                 if self.dispatch:
                     gb = self._gathered(bb)
                     self.comm.dispatch(bb, bb.Xd, c2, self.n_moe, d, gb.cnt)
+                    mark("dispatch")
                     ops.linear_gemm(ly.egu, gb.mXg, gb.NB, gb.gcnt, gb.P, gb.tiles, e["egu"])
+                    mark("expert_gate_up")
                     ops.linear_gemm(ly.edown, gb.mXm, gb.NB, gb.cnt, gb.P, gb.tiles, e["edown"])
+                    mark("expert_down_combine")
                 else:
                     ops.linear_gemm(ly.egu, bb.mXd, B, c2, bb.P, bb.tiles, e["egu"])
+                    mark("expert_gate_up")
                     ops.linear_gemm(ly.edown, bb.mXm, B, c3, bb.P, bb.tiles, e["edown"])
+                    mark("expert_down_combine")
                 if self.ep:
                     self.comm.after_combine(bb, self._moe_index(l), self.n_moe, d)
+                    mark("combine_wait")
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
             ops.rmsnorm_limbs(bb.h, m.final_norm, d, B, bb.Xd, cf)
             ops.linear_gemm(m.lm, bb.mXd, B, cf, bb.P, bb.tiles, E[-1]["lm"])
+            mark("lm_head")
