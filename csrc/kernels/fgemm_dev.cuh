@@ -117,6 +117,16 @@ struct Epi {
   int8_t* nrm_X;
   int* nrm_lmax;
   int* nrm_cnt;
+  // Tensor-parallel reduce-scatter + all-gather (rp = 1 and rs_ag = 1), for
+  // large batches on 4+ ranks: the completed tile's sums go only to its
+  // owner rank (m-tile index mod npeers) and bump only the owner's counter;
+  // the owner sums the npeers slots, stores the total into every rank's
+  // final area (slot npeers of peer_R) and bumps every rank's final counter
+  // (cnt at offset rs_cnt_off); every rank then applies the epilogue to all
+  // tiles from its final area.  Each rank sends 2 (N - 1) / N of a tile's
+  // bytes instead of N - 1 times them.
+  int rs_ag;
+  int rs_cnt_off;
   // Token-dispatch expert parallelism: with peer_h set and ep_rows > 0, the
   // MOE_COMBINE add of gathered slot b goes only to its owner rank
   // b / ep_rows, at row b % ep_rows of that rank's combine buffer (each rank
@@ -262,6 +272,10 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
 __device__ __forceinline__ void push_row(const Epi& E, int M, int B, int m, bool valid, int b, uint64_t acc) {
   if (!valid) return;
   const size_t off = ((size_t)E.rank * B + b) * M + m;
+  if (E.rs_ag) {  // reduce-scatter: only the tile's owner
+    __stcg((long long*)(E.peer_R[(m / BM) % E.npeers] + off), (long long)acc);
+    return;
+  }
   for (int p = 0; p < E.npeers; ++p) __stcg((long long*)(E.peer_R[p] + off), (long long)acc);
 }
 
@@ -273,6 +287,30 @@ __device__ __forceinline__ void emit_row(const Epi& E, int M, int B, int m, bool
                                          int& need) {
   if constexpr (PUSH) push_row(E, M, B, m, valid, b, acc);
   else apply_row(E, M, m, valid, b, acc, need);
+}
+
+// Reduce-scatter owner: row m of slots [bb0, bb1) summed over the npeers
+// slots and stored into every rank's final area (slot npeers of peer_R).
+__device__ __forceinline__ void owner_sum_to_all(const Epi& E, int M, int m, bool valid, int B, int bb0, int bb1) {
+  if (!valid) return;
+  const int64_t* R = E.peer_R[E.rank];
+  for (int b = bb0; b < bb1; ++b) {
+    uint64_t acc = 0;
+#pragma unroll 8
+    for (int r = 0; r < E.npeers; ++r) acc += (uint64_t)__ldcg((const long long*)(R + ((size_t)r * B + b) * M + m));
+    const size_t off = ((size_t)E.npeers * B + b) * M + m;
+    for (int p = 0; p < E.npeers; ++p) __stcg((long long*)(E.peer_R[p] + off), (long long)acc);
+  }
+}
+
+// All-gather receiver: row m of slots [bb0, bb1) from this rank's final area.
+__device__ __forceinline__ void finalize_from_F(const Epi& E, int M, int m, bool valid, int B, int& need, int bb0,
+                                                int bb1) {
+  const int64_t* F = E.peer_R[E.rank] + (size_t)E.npeers * B * M;
+  for (int b = bb0; b < bb1; ++b) {
+    const uint64_t acc = valid ? (uint64_t)__ldcg((const long long*)(F + (size_t)b * M + m)) : 0;
+    apply_row(E, M, m, valid, b, acc, need);
+  }
 }
 
 // Tensor-parallel finaliser: row m of slots [bb0, bb1) is the wrapping sum

@@ -393,8 +393,11 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         // the tile's sums are in every rank's receive buffer: signal each rank once
         __threadfence_system();
         epi_bar();
-        if (warp == 2 && lane == 0)
-          for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + tl, 1);
+        if (warp == 2 && lane == 0) {
+          if (E.rs_ag) atomicAdd_system(E.peer_cnt[mt % E.npeers] + tl, 1);
+          else
+            for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + tl, 1);
+        }
       }
       if (E.mode == SWIGLU && E.lmax_out) {
         need = __reduce_max_sync(0xffffffffu, need);
@@ -409,7 +412,56 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       if (warp == 2 && lane == 0)
         for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_sig[p], 1ull);
     }
-    if (E.rp && E.mode != PARTIAL) {
+    if (E.rp && E.mode != PARTIAL && E.rs_ag) {
+      // ---- reduce-scatter owner: every tile of this rank's m-tiles (all of
+      // them first, since they wait only on partial pushes), then the
+      // all-gather receiver for every tile
+      for (int t = blockIdx.x; t < W.Mt * ntu; t += gridDim.x) {
+        const int mt = t / ntu, nt = t - mt * ntu;
+        if (mt % E.npeers != E.rank) continue;
+        const int sb0 = nt * S, nb = min(S, B - sb0);
+        if (warp == 2 && lane == 0) *ok_ptr = wait_counter_geq(E.cnt_local + t, E.npeers) ? 1 : 0;
+        epi_bar();
+        const bool ok = *ok_ptr != 0;
+        epi_bar();
+        if (!ok) {
+          if (warp == 2 && lane == 0) set_error(E.err, ARCB_ERR_COMM_TIMEOUT);
+          continue;
+        }
+        __threadfence_system();
+        const int m = mt * BM + q * 32 + lane;
+        owner_sum_to_all(E, M, m, m < M, B, sb0, sb0 + nb);
+        __threadfence_system();
+        epi_bar();
+        if (warp == 2 && lane == 0) {
+          E.cnt_local[t] = 0;
+          for (int p = 0; p < E.npeers; ++p) atomicAdd_system(E.peer_cnt[p] + E.rs_cnt_off + t, 1);
+        }
+      }
+      for (int t = blockIdx.x; t < W.Mt * ntu; t += gridDim.x) {
+        const int mt = t / ntu, nt = t - mt * ntu;
+        const int sb0 = nt * S, nb = min(S, B - sb0);
+        if (warp == 2 && lane == 0) *ok_ptr = wait_counter_geq(E.cnt_local + E.rs_cnt_off + t, 1) ? 1 : 0;
+        epi_bar();
+        const bool ok = *ok_ptr != 0;
+        epi_bar();
+        if (!ok) {
+          if (warp == 2 && lane == 0) set_error(E.err, ARCB_ERR_COMM_TIMEOUT);
+          continue;
+        }
+        __threadfence_system();
+        const int m = mt * BM + q * 32 + lane;
+        int need = 0;
+        finalize_from_F(E, M, m, m < M, B, need, sb0, sb0 + nb);
+        if (E.nrm_gamma) __threadfence();
+        epi_bar();
+        if (warp == 2 && lane == 0) {
+          E.cnt_local[E.rs_cnt_off + t] = 0;
+          if (E.nrm_gamma) atomicAdd(E.nrm_cnt, 1);
+        }
+      }
+      if (E.prof && warp == 2 && lane == 0) E.prof[blockIdx.x * 8 + 5] = globaltimer_ns();
+    } else if (E.rp && E.mode != PARTIAL) {
       // ---- finaliser: (m-tile, n-tile) t = blockIdx.x (mod grid) of this rank's copy
       const int target = E.npeers;  // one arrival per rank per tile
       for (int t = blockIdx.x; t < W.Mt * ntu; t += gridDim.x) {

@@ -16,7 +16,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--comm", default="fused", choices=["nccl", "fused", "fused-logits", "fused-norm"])
+    ap.add_argument("--comm", default="fused", choices=["nccl", "fused", "fused-logits", "fused-norm", "fused-rsag"])
     a = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -34,7 +34,9 @@ def main():
     if a.comm.startswith("fused"):
         from arc_chain_b200.parallel.fused import FusedComm
 
-        comm = FusedComm(fuse_logits=a.comm in ("fused-logits", "fused-norm"))
+        # fused-rsag: the reduce-scatter + all-gather form at every batch size
+        comm = FusedComm(fuse_logits=a.comm in ("fused-logits", "fused-norm"),
+                         rs_ag="on" if a.comm == "fused-rsag" else "auto")
     cfg = preset("tiny")
     if (cfg.d_ff // world) % 16:  # TP shards of the FFN must stay 16-byte rows
         cfg = dataclasses.replace(cfg, d_ff=768)
