@@ -251,35 +251,51 @@ __global__ void __launch_bounds__(Cfg<BN, Q4, NC>::THREADS, 1)
     int64_t inv[2];
 #pragma unroll
     for (int b = 0; b < 2; ++b) inv[b] = b < B ? rms_inv((int64_t)E.nc_ss[b], K) : 0;
+    // the chunks this CTA consumes, in order, each once
     uint32_t done = 0;
+    int list[NC_CHUNKS], nl = 0;
     const int n = W.count();
     for (int i = 0; i < n; ++i) {
       const int kc = W.kc(W.item(i));
-      if ((done >> kc) & 1u) continue;
-      done |= 1u << kc;
-      uint8_t* tile = panel + kc * BN * BK;
-      for (int u = t; u < B * 32; u += 128) {
-        const int b = u >> 5, k4 = (u & 31) * 4, kx = kc * BK + k4;
-        uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (!((done >> kc) & 1u)) {
+        done |= 1u << kc;
+        list[nl++] = kc;
+      }
+    }
+    // thread t converts element t of every listed chunk (both slots), 8
+    // chunks at a time so their loads are in flight together
+    constexpr int G = 8;
+    for (int g0 = 0; g0 < nl; g0 += G) {
+      int64_t x[G][2], gm[G];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int k = kx + e;
-          const int64_t x = k < K ? E.nc_h[(size_t)b * K + k] : 0;
-          const int64_t y = k < K ? rms_apply(x, inv[b], k < E.nc_ngamma ? E.nc_gamma[k] : ONE) : 0;
+      for (int c = 0; c < G; ++c) {
+        const int k = (g0 + c < nl) ? list[g0 + c] * BK + t : K;
+        gm[c] = k < K ? (k < E.nc_ngamma ? E.nc_gamma[k] : ONE) : 0;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) x[c][b] = (k < K && b < B) ? E.nc_h[(size_t)b * K + k] : 0;
+      }
+#pragma unroll
+      for (int c = 0; c < G; ++c) {
+        if (g0 + c >= nl) break;
+        uint8_t* tile = panel + list[g0 + c] * BN * BK;
+        const int k = list[g0 + c] * BK + t;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          if (b >= B) break;
+          const int64_t y = k < K ? rms_apply(x[c][b], inv[b], gm[c]) : 0;
           int8_t dg[8];
           limb_split8(y, dg);
 #pragma unroll
-          for (int l = 0; l < 8; ++l) w[l] |= (uint32_t)(uint8_t)dg[l] << (8 * e);
-        }
-#pragma unroll
-        for (int l = 0; l < 8; ++l) {
-          const int r = l * B + b;
-          *(uint32_t*)(tile + r * BK + ((((k4 >> 4) ^ (r & 7))) << 4) + (k4 & 15)) = w[l];
+          for (int l = 0; l < 8; ++l) {
+            const int r = l * B + b;
+            tile[r * BK + ((((t >> 4) ^ (r & 7))) << 4) + (t & 15)] = (uint8_t)dg[l];
+          }
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(cbar(kc));
+      if (lane == 0)
+        for (int c = 0; c < G && g0 + c < nl; ++c) mbar_arrive(cbar(list[g0 + c]));
     }
   } else if (Q4 && warp >= 6) {
     // ---------------- Q4 converter warps 6..9: packed tile -> swizzled int8 A
