@@ -27,34 +27,54 @@ import sys
 import torch
 
 
+def _clocked(run) -> None:
+    """Runs run(iters) (a benchmark returning a dict) with the clock sampler
+    on: enough iterations for samples on a plain run, two under a profiler
+    (PT_SECONDS=0); prints the dict with the clock record."""
+    import os
+
+    from arc_chain_b200.utils.clocks import ClockSampler
+
+    import time
+
+    secs = float(os.environ.get("PT_SECONDS", "1.0"))
+    with ClockSampler(0, period_ms=50) as clk:
+        w0 = time.perf_counter()
+        res = run(2 if secs == 0 else 400)
+        while time.perf_counter() - w0 < secs:  # repeat so the sampler sees the load
+            res = run(400)
+    res["clocks"] = clk.summary()
+    print(json.dumps(res), flush=True)
+
+
 def attn():
     from arc_chain_b200.bench.kernels import bench_attn
 
-    print(json.dumps(bench_attn(386, iters=2)))
+    _clocked(lambda n: bench_attn(386, iters=n))
 
 
 def gemm_b1():
     from arc_chain_b200.bench.kernels import bench_fgemm
 
-    print(json.dumps(bench_fgemm(22016, 4096, 1, iters=2)))
+    _clocked(lambda n: bench_fgemm(22016, 4096, 1, iters=n))
 
 
 def gemm_b256():
     from arc_chain_b200.bench.kernels import bench_fgemm
 
-    print(json.dumps(bench_fgemm(57344, 8192, 256, iters=2, limbs=4)))
+    _clocked(lambda n: bench_fgemm(57344, 8192, 256, iters=max(2, n // 8), limbs=4))
 
 
 def commit():
     from arc_chain_b200.bench.crypto import bench_commit
 
-    print(json.dumps(bench_commit(1 << 20, reps=2)))
+    _clocked(lambda n: bench_commit(1 << 20, reps=max(2, n // 20)))
 
 
 def ed25519():
     from arc_chain_b200.bench.crypto import bench_ed25519
 
-    print(json.dumps(bench_ed25519(1 << 16, reps=2)))
+    _clocked(lambda n: bench_ed25519(1 << 16, reps=max(2, n // 40)))
 
 
 def _timed(fn, warm: int, iters: int, extra: dict) -> None:

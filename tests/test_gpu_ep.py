@@ -1,5 +1,5 @@
 """Expert parallelism for the MLA + MoE decoder: the device generator with
-expert shards, and 2-rank runs against the oracle: replicated tokens (NCCL
+expert shards, and 2-, 4- and 8-rank runs (as the box allows) against the oracle: replicated tokens (NCCL
 and fused peer-push combine) and token dispatch (each rank decodes its own
 prompts; tokens are sent to the experts' ranks and combined on their
 owner)."""
@@ -39,13 +39,15 @@ def test_device_generator_matches_host_shards(ep_size):
                 assert torch.equal(getattr(la, n), getattr(lb, n)), n
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("comm", ["nccl", "fused", "dispatch"])
-def test_ep2_matches_oracle(comm):
+def test_ep_matches_oracle(comm, world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    port = 29600 + (os.getpid() % 200) + {"nccl": 0, "fused": 7, "dispatch": 13}[comm]
+    port = 29600 + (os.getpid() % 200) + {"nccl": 0, "fused": 7, "dispatch": 13}[comm] + 20 * world
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={port}",
            os.path.join(ROOT, "tests", "ep_worker.py"), "--comm", comm]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
