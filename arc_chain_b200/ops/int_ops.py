@@ -191,8 +191,7 @@ class Epi(C.Structure):
                 ("peer_sig", C.c_void_p), ("pf_w", C.c_void_p), ("pf_M", C.c_int), ("pf_K", C.c_int),
                 ("pf_tiles", C.c_int), ("sched", C.c_int), ("nrm_gamma", C.c_void_p), ("nrm_ngamma", C.c_int),
                 ("nrm_X", C.c_void_p), ("nrm_lmax", C.c_void_p), ("nrm_cnt", C.c_void_p), ("rs_ag", C.c_int),
-                ("rs_cnt_off", C.c_int), ("nc_h", C.c_void_p), ("nc_ss", C.c_void_p), ("nc_gamma", C.c_void_p),
-                ("nc_ngamma", C.c_int), ("ep_rows", C.c_int)]
+                ("rs_cnt_off", C.c_int), ("ep_rows", C.c_int)]
 
 
 PARTIAL, STORE, RESID, QKV, SWIGLU, MOE_COMBINE, STORE_PEERS = 0, 1, 2, 3, 4, 5, 6

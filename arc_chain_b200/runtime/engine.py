@@ -134,10 +134,6 @@ class Engine:
         # resident and prefetch weights while it runs, which the fused form,
         # holding every SM until its norm phase ends, gives up.
         self.fuse_norm = os.environ.get("ARCB_FUSE_NORM", "0") == "1"
-        # decode of one or two slots (int8 weights, d <= 4096): the GEMM after
-        # each RMSNorm builds its limb operand from the hidden state itself
-        # (norm converter warps), so the separate norm launches go away
-        self.norm_conv = os.environ.get("ARCB_NORM_CONV", "1") != "0"
         # prefill chunks: one chunk-attention launch per layer (each K/V page
         # read once per 16 positions) instead of the per-position decode kernel
         self.prefill_attn = os.environ.get("ARCB_PREFILL_ATTN", "1") != "0"
@@ -173,7 +169,6 @@ class Engine:
         E = self._epis(bb)
         reduce_in_kernel = cm.size == 1 or getattr(cm, "fused", False)
         fused_norm = self._norm_fused()
-        nc = self._norm_conv(B)
         nv = torch.cuda.nvtx if self.nvtx else None
         ev = self.op_events
 
@@ -189,10 +184,10 @@ class Engine:
             e = E[l]
             if nv:
                 nv.range_push(f"layer {l} attention")
-            if (l == 0 or not fused_norm) and not nc:
+            if l == 0 or not fused_norm:
                 ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
                 mark("norm")
-            ops.linear_gemm(Ly.qkv, bb.mXd, B, c0, bb.P, bb.tiles, e["qkv_nc" if nc else "qkv"])
+            ops.linear_gemm(Ly.qkv, bb.mXd, B, c0, bb.P, bb.tiles, e["qkv"])
             mark("qkv")
             T_all = self.max_pages * PAGE
             if span is not None:
@@ -219,10 +214,10 @@ class Engine:
             if nv:
                 nv.range_pop()
                 nv.range_push(f"layer {l} ffn")
-            if not fused_norm and not nc:
+            if not fused_norm:
                 ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
                 mark("norm")
-            ops.linear_gemm(Ly.gu, bb.mXd, B, c2, bb.P, bb.tiles, e["gu_nc" if nc else "gu"])
+            ops.linear_gemm(Ly.gu, bb.mXd, B, c2, bb.P, bb.tiles, e["gu"])
             mark("gate_up")
             if reduce_in_kernel:
                 cm.fgemm_reduce(Ly.down, bb.mXf, B, c3, bb, e["down"], site=1)
@@ -235,17 +230,16 @@ class Engine:
                 nv.range_pop()
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
-            if not fused_norm and not nc:
+            if not fused_norm:
                 ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
-            lm0 = E[-1]["lm_nc" if nc else "lm"]
-            lm_e = cm.lm_epi(lm0, bb, c.vocab, m.vocab_offset) if hasattr(cm, "lm_epi") else lm0
+            lm_e = cm.lm_epi(E[-1]["lm"], bb, c.vocab, m.vocab_offset) if hasattr(cm, "lm_epi") else E[-1]["lm"]
             ops.linear_gemm(m.lm, bb.mXd, B, cf, bb.P, bb.tiles, lm_e)
             cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset, bb=bb)
             mark("lm_head")
 
     def _epis(self, bb: StepBuffers):
         """Epilogue descriptors of every fused GEMM of a forward over `bb`."""
-        if bb.epis is not None and getattr(bb, "epis_norm", None) == (self._norm_fused(), self._norm_conv(bb.B)):
+        if bb.epis is not None and getattr(bb, "epis_norm", None) == self._norm_fused():
             return bb.epis
         m, c = self.m, self.m.cfg
         d, dh = c.d_model, c.d_head
@@ -263,19 +257,6 @@ class Engine:
                 "partial": ops.epi(ops.PARTIAL, Ly.wo.s, bb.err),
             })
         out.append({"lm": ops.epi(ops.STORE, m.lm.s, bb.err, out=bb.logits_local, ldo=m.lm.M)})
-        if self._norm_conv(bb.B):
-            # the same descriptors, with the norm converter's inputs
-            L = c.n_layers
-            for l, Ly in enumerate(m.layers):
-                for key, row, g in (("qkv", 2 * l, Ly.attn_norm), ("gu", 2 * l + 1, Ly.ffn_norm)):
-                    e = ops.Epi.from_buffer_copy(out[l][key])
-                    e.nc_h, e.nc_ss, e.nc_gamma, e.nc_ngamma = (bb.h.data_ptr(), bb.ss[row].data_ptr(),
-                                                                g.data_ptr(), g.numel())
-                    out[l][key + "_nc"] = e
-            e = ops.Epi.from_buffer_copy(out[-1]["lm"])
-            e.nc_h, e.nc_ss, e.nc_gamma, e.nc_ngamma = (bb.h.data_ptr(), bb.ss[2 * L].data_ptr(),
-                                                        m.final_norm.data_ptr(), m.final_norm.numel())
-            out[-1]["lm_nc"] = e
         if self._norm_fused():
             L = c.n_layers
             for l, Ly in enumerate(m.layers):
@@ -294,15 +275,8 @@ class Engine:
         for (e, _), (_, nxt) in zip(chain, chain[1:]):
             ops.set_prefetch(e, nxt, self.prefetch_tiles)
         bb.epis = out
-        bb.epis_norm = (self._norm_fused(), self._norm_conv(bb.B))
+        bb.epis_norm = self._norm_fused()
         return out
-
-    def _norm_conv(self, B: int) -> bool:
-        """The norm converter serves this step (see norm_conv)."""
-        m = self.m
-        lins = [Ly.qkv for Ly in m.layers] + [Ly.gu for Ly in m.layers] + [m.lm]
-        return (bool(self.norm_conv) and B <= 2 and not self._norm_fused() and m.cfg.d_model <= 4096 and
-                all(getattr(x, "q4", None) is None for x in lins))
 
     def _norm_fused(self) -> bool:
         """Norms run inside the residual GEMMs (needs the in-kernel reduce)."""

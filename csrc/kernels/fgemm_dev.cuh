@@ -127,13 +127,6 @@ struct Epi {
   // bytes instead of N - 1 times them.
   int rs_ag;
   int rs_cnt_off;
-  // Norm converter (NC kernels only): hidden state [B, K] int64, its sums
-  // of squares ss [B] and the norm weights; the limb operand is built from
-  // them in shared memory (see Cfg).
-  const int64_t* nc_h;
-  const uint64_t* nc_ss;
-  const int64_t* nc_gamma;
-  int nc_ngamma;
   // Token-dispatch expert parallelism: with peer_h set and ep_rows > 0, the
   // MOE_COMBINE add of gathered slot b goes only to its owner rank
   // b / ep_rows, at row b % ep_rows of that rank's combine buffer (each rank
@@ -148,30 +141,18 @@ struct Epi {
 #define ARCB_FG_SMALL_STAGES 11
 #endif
 
-// NC (norm converter): the limb operand is not loaded by TMA.  Converter
-// warps build it in a shared-memory panel, once per K chunk the CTA uses,
-// straight from the hidden state: y = rms_apply(h, rms_inv(ss), gamma), then
-// the 8-digit split (all 8 planes, so the limb count is 8).  This removes the
-// separate RMSNorm -> limb-planes launch before the GEMM.  Panel: NC_CHUNKS
-// K chunks of BN x 128 bytes (K <= NC_CHUNKS * 128), 128-byte swizzled like
-// a TMA tile; 8 * B <= BN = 16 (decode of one or two slots).
-constexpr int NC_CHUNKS = 32;
-
-template <int BN, bool Q4 = false, bool NC = false>
+template <int BN, bool Q4 = false>
 struct Cfg {
-  static_assert(!(Q4 && NC), "the norm converter serves int8 weights");
   static constexpr int A_BYTES = BM * BK;
-  static constexpr int B_BYTES = NC ? 0 : BN * BK;         // per-stage limb tile (TMA)
-  static constexpr int PANEL = NC ? NC_CHUNKS * BN * BK : 0;  // NC: limb panel, one tile per K chunk
+  static constexpr int B_BYTES = BN * BK;
   static constexpr int Q_BYTES = Q4 ? Q4_TILE : 0;        // staging of the packed Q4 tile
   static constexpr int STAGE_BYTES = (Q4 ? Q4_TILE : A_BYTES) + B_BYTES;  // bytes TMA brings per stage
   static constexpr int STAGES = Q4 ? (BN <= 32 ? 7 : (BN <= 64 ? 6 : (BN <= 128 ? 5 : 3)))
-                                   : NC ? 8
-                                        : (BN <= 32 ? ARCB_FG_SMALL_STAGES : (BN <= 64 ? 8 : (BN <= 128 ? 6 : 4)));
+                                   : (BN <= 32 ? ARCB_FG_SMALL_STAGES : (BN <= 64 ? 8 : (BN <= 128 ? 6 : 4)));
   static constexpr int ACC_COLS = BN < 32 ? 32 : BN;       // one TMEM accumulator
   static constexpr int TMEM_COLS = 2 * ACC_COLS;          // double buffered
-  static constexpr int THREADS = (Q4 || NC) ? 320 : NTHREADS;  // + 4 converter warps
-  static constexpr int SMEM = 1024 + STAGES * (A_BYTES + B_BYTES + Q_BYTES) + PANEL + (NC ? 1024 : 512);
+  static constexpr int THREADS = Q4 ? 320 : NTHREADS;     // + 4 converter warps for Q4
+  static constexpr int SMEM = 1024 + STAGES * (A_BYTES + B_BYTES + Q_BYTES) + 512;
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

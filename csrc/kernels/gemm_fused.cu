@@ -32,20 +32,19 @@ using namespace q16;
 namespace fg {
 
 // MB: the launch has several 32-slot blocks (B > 32, 256-row tiles only).
-template <int BN, bool Q4, bool MB, bool NC = false>
-__global__ void __launch_bounds__(Cfg<BN, Q4, NC>::THREADS, 1)
+template <int BN, bool Q4, bool MB>
+__global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
     k_gemm_fused(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
                  int B, int n_tiles_max, int prefetch_ok, const int* __restrict__ lmax, int* __restrict__ P,
                  int* __restrict__ tile_cnt, const __grid_constant__ Epi E, const uint8_t* __restrict__ q4w) {
-  using C = Cfg<BN, Q4, NC>;
+  using C = Cfg<BN, Q4>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t a_base = base;
   const uint32_t b_base = base + C::STAGES * C::A_BYTES;
   const uint32_t q_base = b_base + C::STAGES * C::B_BYTES;  // Q4 staging (Q_BYTES per stage)
-  const uint32_t p_base = q_base + C::STAGES * C::Q_BYTES;  // NC: limb panel (PANEL bytes)
-  const uint32_t bar = p_base + C::PANEL;
+  const uint32_t bar = q_base + C::STAGES * C::Q_BYTES;
   auto full = [&](int s) { return bar + 8u * s; };
   auto empty = [&](int s) { return bar + 8u * (C::STAGES + s); };
   auto seg_full = [&](int t) { return bar + 8u * (2 * C::STAGES + t); };
@@ -55,7 +54,6 @@ __global__ void __launch_bounds__(Cfg<BN, Q4, NC>::THREADS, 1)
   volatile uint32_t* tslot_ptr = (volatile uint32_t*)(smem_raw + (tslot - raw));
   volatile int* flag_ptr = (volatile int*)(smem_raw + (tslot + 8 - raw));
   volatile int* ok_ptr = (volatile int*)(smem_raw + (tslot + 12 - raw));
-  auto cbar = [&](int kc) { return tslot + 16u + 8u * kc; };  // NC: panel chunk kc converted
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   Work W{(M + BM - 1) / BM, (K + BK - 1) / BK, 0, 0};
@@ -71,8 +69,6 @@ __global__ void __launch_bounds__(Cfg<BN, Q4, NC>::THREADS, 1)
     }
     if (Q4)
       for (int s = 0; s < C::STAGES; ++s) mbar_init(conv(s), 4);
-    if (NC)
-      for (int kc = 0; kc < NC_CHUNKS; ++kc) mbar_init(cbar(kc), 4);
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -97,9 +93,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4, NC>::THREADS, 1)
   // b_row: first operand row of the item's n-tile; tile: weight tile index
   // (m-tile * chunks + chunk) in the tiled weight layout.
   auto load_b = [&](int s, int b_row, int kx, int rows) {
-    if constexpr (NC) {
-      return;  // the converter warps build the operand
-    } else if constexpr (BN >= 64) {
+    if constexpr (BN >= 64) {
       for (int r0 = 0; r0 < rows; r0 += bbox)
         tma_load_2d(b_base + s * C::B_BYTES + r0 * BK, &tmB, full(s), kx, b_row + r0);
     } else {
@@ -138,7 +132,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4, NC>::THREADS, 1)
   }
   pdl_wait();
   if (E.prof && threadIdx.x == 0) E.prof[blockIdx.x * 8 + 1] = globaltimer_ns();
-  const int L = NC ? 8 : max(1, *lmax);  // NC: all 8 planes are in the panel
+  const int L = max(1, *lmax);
   const int nrows = L * S;  // live rows of every n-tile: L limbs of S slots
   W.range(ntu, MULTI && E.sched == 0);
 
@@ -150,7 +144,7 @@ __global__ void __launch_bounds__(Cfg<BN, Q4, NC>::THREADS, 1)
       // -> (tile, chunk) mapping is evaluated once per segment (tile) and
       // the chunk, stage and parity then advance by increments.
       const int live = BN >= 64 ? min(BN, (min(BN, nrows) + bbox - 1) / bbox * bbox) : BN;
-      const uint32_t tx_bytes = (Q4 ? Q4_TILE : C::A_BYTES) + (NC ? 0 : live * BK);
+      const uint32_t tx_bytes = (Q4 ? Q4_TILE : C::A_BYTES) + live * BK;
       int issued = 0, i = 0, s = 0;
       uint32_t ph = 0;
       bool ok = true;
@@ -214,19 +208,17 @@ __global__ void __launch_bounds__(Cfg<BN, Q4, NC>::THREADS, 1)
         const uint32_t dst = tmem + (uint32_t)(tb * C::ACC_COLS);
         for (int j = it; j < se; ++j, ++i) {
           const int s = i % C::STAGES;
-          if (!mbar_wait(Q4 ? conv(s) : full(s), (uint32_t)(i / C::STAGES) & 1u) ||
-              (NC && !mbar_wait(cbar(W.kc(j)), 0u))) {
+          if (!mbar_wait(Q4 ? conv(s) : full(s), (uint32_t)(i / C::STAGES) & 1u)) {
             set_error(E.err, ARCB_ERR_TIMEOUT_FULL);
             ok = false;
             break;
           }
           tc_fence_after();
           if (E.prof && i == 0) E.prof[blockIdx.x * 8 + 2] = globaltimer_ns();
-          const uint32_t bt = NC ? p_base + (uint32_t)(W.kc(j) * BN * BK) : b_base + s * C::B_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             const uint64_t ad = sw128_kmajor_desc(a_base + s * C::A_BYTES + kk * 32);
-            const uint64_t bd = sw128_kmajor_desc(bt + kk * 32);
+            const uint64_t bd = sw128_kmajor_desc(b_base + s * C::B_BYTES + kk * 32);
             mma_i8(dst, ad, bd, idesc, (j > it || kk > 0) ? 1u : 0u);
           }
           mma_commit(empty(s));
@@ -235,67 +227,6 @@ __global__ void __launch_bounds__(Cfg<BN, Q4, NC>::THREADS, 1)
         if (E.prof) E.prof[blockIdx.x * 8 + 3] = globaltimer_ns();
         it = W.next(se);
       }
-    }
-  } else if (NC && warp >= 6) {
-    // ---------------- norm converter warps 6..9: hidden state -> limb panel
-    // Rows l * B + b (limb l of slot b) of chunk kc's tile hold the digits of
-    // y = rms_apply(h[b, kc * 128 + k], rms_inv(ss[b], K), gamma); rows from
-    // 8 * B up stay zero.  Chunks are converted in the order this CTA's MMAs
-    // consume them, each once, and announced by their own barrier.
-    const int t = threadIdx.x - 192;
-    uint8_t* panel = smem_raw + (p_base - raw);
-    for (int i = t; i < NC_CHUNKS * BN * BK / 16; i += 128) {
-      const int r = (i * 16 / BK) % BN;
-      if (r >= 8 * B) *(uint4*)(panel + i * 16) = make_uint4(0, 0, 0, 0);
-    }
-    int64_t inv[2];
-#pragma unroll
-    for (int b = 0; b < 2; ++b) inv[b] = b < B ? rms_inv((int64_t)E.nc_ss[b], K) : 0;
-    // the chunks this CTA consumes, in order, each once
-    uint32_t done = 0;
-    int list[NC_CHUNKS], nl = 0;
-    const int n = W.count();
-    for (int i = 0; i < n; ++i) {
-      const int kc = W.kc(W.item(i));
-      if (!((done >> kc) & 1u)) {
-        done |= 1u << kc;
-        list[nl++] = kc;
-      }
-    }
-    // thread t converts element t of every listed chunk (both slots), 8
-    // chunks at a time so their loads are in flight together
-    constexpr int G = 8;
-    for (int g0 = 0; g0 < nl; g0 += G) {
-      int64_t x[G][2], gm[G];
-#pragma unroll
-      for (int c = 0; c < G; ++c) {
-        const int k = (g0 + c < nl) ? list[g0 + c] * BK + t : K;
-        gm[c] = k < K ? (k < E.nc_ngamma ? E.nc_gamma[k] : ONE) : 0;
-#pragma unroll
-        for (int b = 0; b < 2; ++b) x[c][b] = (k < K && b < B) ? E.nc_h[(size_t)b * K + k] : 0;
-      }
-#pragma unroll
-      for (int c = 0; c < G; ++c) {
-        if (g0 + c >= nl) break;
-        uint8_t* tile = panel + list[g0 + c] * BN * BK;
-        const int k = list[g0 + c] * BK + t;
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          if (b >= B) break;
-          const int64_t y = k < K ? rms_apply(x[c][b], inv[b], gm[c]) : 0;
-          int8_t dg[8];
-          limb_split8(y, dg);
-#pragma unroll
-          for (int l = 0; l < 8; ++l) {
-            const int r = l * B + b;
-            tile[r * BK + ((((t >> 4) ^ (r & 7))) << 4) + (t & 15)] = (uint8_t)dg[l];
-          }
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0)
-        for (int c = 0; c < G && g0 + c < nl; ++c) mbar_arrive(cbar(list[g0 + c]));
     }
   } else if (Q4 && warp >= 6) {
     // ---------------- Q4 converter warps 6..9: packed tile -> swizzled int8 A
@@ -622,14 +553,13 @@ static int num_sms() {
   return n;
 }
 
-template <int BN, bool Q4, bool MB = false, bool NC = false>
+template <int BN, bool Q4, bool MB = false>
 int launch(const CUtensorMap* a, const CUtensorMap* b, int M, int K, int B, const int* lmax, int* P, int* cnt,
            const Epi& E, cudaStream_t st, int pdl, const uint8_t* q4w) {
-  using C = Cfg<BN, Q4, NC>;
+  using C = Cfg<BN, Q4>;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(k_gemm_fused<BN, Q4, MB, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_fused<BN, Q4, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return (int)e;
     attr = true;
   }
@@ -644,8 +574,8 @@ int launch(const CUtensorMap* a, const CUtensorMap* b, int M, int K, int B, cons
   at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_fused<BN, Q4, MB, NC>, *a, *b, M, K, B, n_tiles_max, 1, lmax, P,
-                                     cnt, E, q4w);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_fused<BN, Q4, MB>, *a, *b, M, K, B, n_tiles_max, 1, lmax, P, cnt,
+                                     E, q4w);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
@@ -677,12 +607,6 @@ int arcb_fgemm(const void* tmA, const void* tmB, int M, int K, int B, int bn, co
   pdl = pdl && arcb_pdl_enabled();
   E.B = B;
   cudaStream_t st = (cudaStream_t)stream;
-  if (E.nc_h) {  // norm converter: the limb operand is built from the hidden state in the kernel
-    // one 16-row tile holds the 8 planes of up to 2 slots; the panel of a
-    // wider tile would not leave room for the weight ring
-    if (8 * B > 16 || bn != 16 || K > fg::NC_CHUNKS * fg::BK || !E.nc_ss) return -2;
-    return fg::launch<16, false, false, true>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
-  }
   switch (bn) {
     case 16: return fg::launch<16, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
     case 32: return fg::launch<32, false>(a, b, M, K, B, lmax, P, tile_cnt, E, st, pdl, nullptr);
