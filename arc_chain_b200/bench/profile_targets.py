@@ -226,7 +226,54 @@ def attn_block():
     assert int(err.item()) == 0
 
 
-TARGETS = {"attn_block": attn_block, "attn": attn, "gemm_b1": gemm_b1, "gemm_b256": gemm_b256, "commit": commit, "ed25519": ed25519,
+def moe_gemm():
+    """Expert GEMMs of one MoE layer, DeepSeek-V2-Lite shapes with 33 local
+    experts (expert parallelism over 2 GPUs), 32 gathered slots, 4 limbs:
+    gate/up (SwiGLU epilogue writing the down GEMM's limb planes) and down
+    (grouped: each expert reads its own 1408 columns; routing-weighted
+    combine into the hidden state).  ARCB_PT_MOE=down times the down GEMM."""
+    import os
+
+    from arc_chain_b200.ops import int_ops as ops
+
+    dev = torch.device("cuda")
+    G, F, d, B = 33, 1408, 2048, 32
+    which = os.environ.get("ARCB_PT_MOE", "gate_up")
+    bn = ops.fgemm_bn(B)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    if which == "gate_up":
+        M, K = G * 2 * F, d
+    else:
+        M, K = G * d, G * F
+    W = ops.tile_weight(torch.randint(-127, 128, (M, K if which == "gate_up" else F), dtype=torch.int8, device=dev))
+    wm = ops.TensorMap(W, 128)
+    S = torch.randint(1, 100, (M,), dtype=torch.int64, device=dev)
+    X = torch.randint(-127, 128, (ops.limb_rows(B, bn), K), dtype=torch.int8, device=dev)
+    xm = ops.TensorMap(X, bn, min(bn, 32))
+    lmax = torch.tensor([4], dtype=torch.int32, device=dev)
+    P = torch.zeros(8 * B * M, dtype=torch.int32, device=dev)
+    tiles = torch.zeros(ops.tile_counters(M, B), dtype=torch.int32, device=dev)
+    if which == "gate_up":
+        Xm = torch.zeros(ops.limb_rows(B, bn), G * F, dtype=torch.int8, device=dev)
+        lo = torch.zeros(1, dtype=torch.int32, device=dev)
+        e = ops.epi(ops.SWIGLU, S, err, X=Xm, ldx=G * F, lmax_out=lo)
+        nbytes = M * K
+    else:
+        h = torch.zeros(B, d, dtype=torch.int64, device=dev)
+        # 8 of the 66 experts per slot carry weight (6 routed + 2 shared)
+        route = torch.zeros(B, 66, dtype=torch.int64, device=dev)
+        route[:, torch.randperm(66)[:8]] = 8192
+        e = ops.epi(ops.MOE_COMBINE, S, err, out=h, ldo=d, route=route, route_ld=66)
+        e.grp_rows, e.grp_koff = d, F
+        nbytes = M * F
+    e.max_ctas = min(ops.num_sms(), ops.split_ctas(M, B, bn))
+    _timed(lambda: ops.fgemm(wm, xm, M, K if which == "gate_up" else F, B, lmax, P, tiles, e), 3, 10,
+           {"kernel": f"k_gemm_fused<256,0,0> expert {which}", "M": M, "K": K, "B": B, "limbs": 4,
+            "bytes": nbytes})
+    assert int(err.item()) == 0
+
+
+TARGETS = {"moe_gemm": moe_gemm, "attn_block": attn_block, "attn": attn, "gemm_b1": gemm_b1, "gemm_b256": gemm_b256, "commit": commit, "ed25519": ed25519,
            "mla_attn": mla_attn, "moe_route": moe_route, "q4_gemm": q4_gemm, "sample": sample,
            "norm_limbs": norm_limbs}
 

@@ -81,11 +81,11 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
   __shared__ int64_t lut[EXP_LUT_N];
   __shared__ __align__(8) uint64_t full[MAX_RING];
   __shared__ int s_need, s_abort;
+  __shared__ int cons[MAX_RING], last_use[MAX_RING];  // warps done with a stage; its latest use
   __shared__ int qfit[QB];  // query row fits in int32
   __shared__ int64_t red[WM][QB];
-  // general forms: warp (wpart, qi) = part wpart of query qi
-  const int tid = threadIdx.x, qi = (tid >> 5) % QB, wpart = (tid >> 5) / QB, lane = tid & 31, kk = lane & 15,
-            hh = lane >> 4;
+  // softmax passes: warp (wpart, qi) = part wpart of query qi
+  const int tid = threadIdx.x, qi = (tid >> 5) % QB, wpart = (tid >> 5) / QB, lane = tid & 31;
   const int G = n_heads / n_kv;
   const int d = n_heads * DH;
   const uint32_t ring = (smem_u32(dsm) + 127u) & ~127u;
@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
     s_abort = 0;
   }
   if (tid < QB) qfit[tid] = 1;
+  if (tid < MAX_RING) cons[tid] = 0, last_use[tid] = -1;
   pdl_wait_dep();
   pdl_allow_next();
   // block geometry: live queries, their slot / head / position, the pages
@@ -127,18 +128,18 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
   const int npg = (nreal > 0 && !bad) ? (Tmax + PAGE - 1) / PAGE : 0;
   const int Tp = npg * PAGE;
   const int uses = 2 * npg;
-  int issued = 0;
-  auto issue = [&](int u) {  // thread 0
+  auto issue = [&](int u) {  // one thread
     const bool isv = u >= npg;
     const int page = ptb[isv ? u - npg : u];
     const int64_t* src = (isv ? Vc : Kc) + ((size_t)page * n_kv + kvh) * PAGE * DH;
     const uint32_t bar = smem_u32(&full[u % RING]);
+    last_use[u % RING] = u;
     mbar_arrive_expect_tx(bar, PB);
     bulk_g2s(ring + (u % RING) * PB, src, PB, bar);
   };
   __syncthreads();
   if (tid == 0)
-    for (; issued < min(RING, uses); ++issued) issue(issued);
+    for (int u = 0; u < min(RING, uses); ++u) issue(u);
   for (int i = tid; i < EXP_LUT_N; i += NT) lut[i] = g_exp_lut.v[i];
   for (int i = tid; i < QB * DH; i += NT) {
     const int qq = i / DH, e = i - qq * DH;
@@ -148,28 +149,39 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
     qs[i] = v;
     if (v != (int64_t)(int32_t)v) qfit[qq] = 0;
   }
-  auto wait_use = [&](int u) -> bool {
-    if (tid == 0 && !mbar_wait(smem_u32(&full[u % RING]), (uint32_t)(u / RING) & 1u)) {
+  // Pages are consumed warp by warp, with no block-wide barrier per page:
+  // each warp waits for the stage itself (lane 0, bounded), and the last warp
+  // to finish with a stage refills it with the use RING ahead.  A timeout
+  // sets the abort flag, which every warp checks before its next page.
+  constexpr int NW = NT / 32;
+  auto wait_page = [&](int u) -> bool {
+    if (*(volatile int*)&s_abort) return false;
+    int got = 1;
+    if (lane == 0) got = mbar_wait(smem_u32(&full[u % RING]), (uint32_t)(u / RING) & 1u) ? 1 : 0;
+    got = __shfl_sync(0xffffffffu, got, 0);
+    __syncwarp();
+    if (!got && lane == 0) {
       s_abort = 1;
       set_error(err, ARCB_ERR_TIMEOUT_FULL);
     }
-    __syncthreads();
-    return s_abort == 0;
+    return got != 0;
   };
-  // every value of the page in ring stage u fits in int32 (a block-wide vote)
-  auto page_fits = [&](int u) -> bool {
-    const int64_t* pg = (const int64_t*)(ringp + (u % RING) * PB);
-    bool f = true;
-    for (int i = tid; i < PAGE * DH; i += NT) f &= pg[i] == (int64_t)(int32_t)pg[i];
-    return __syncthreads_and(f) != 0;
-  };
-  auto release = [&]() {
-    __syncthreads();
-    if (tid == 0 && issued < uses) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(issued++);
+  auto page_done = [&](int u) {
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();  // this warp's reads of the stage come first
+      const int st = u % RING;
+      if (atomicAdd(&cons[st], 1) == NW - 1) {
+        cons[st] = 0;
+        if (u + RING < uses && !*(volatile int*)&s_abort) {
+          __threadfence_block();
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue(u + RING);
+        }
+      }
     }
   };
+  auto fits32 = [](int64_t v) { return v == (int64_t)(int32_t)v; };
   const bool live = qi < nreal && !bad;
   // position of query qq of the block (the last key it attends to)
   auto qpos = [&](int qq) { return MODE == 0 ? p0 + (int)blockIdx.x * QB + qq : pq; };
@@ -188,20 +200,24 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
   for (int qq = 0; qq < QB; ++qq)
 #pragma unroll
     for (int i = 0; i < EPS; ++i) qreg[qq][i] = (int)qs[qq * DH + i * S1 + sl];
-  // ---- pass 1: scores of keys j <= (position of the query)
-  bool ok = true;
-  constexpr int HD = DH / 2;
-  for (int pi = 0; pi < npg && ok; ++pi) {
-    if (!(ok = wait_use(pi))) break;
-    const bool fast = page_fits(pi) && qall;
-    const int64_t* kp = (const int64_t*)(ringp + (pi % RING) * PB);
-    if (fast) {
-      // slice sl takes elements i * S1 + sl: the lanes of a key read 16 different banks
-      const int* k32 = (const int*)(kp + kk1 * DH + sl);
-      int kv[EPS];
+  // ---- pass 1: scores of keys j <= (position of the query).  Each warp
+  // takes its key(s) of the page: 32-bit products when its elements and the
+  // query rows fit in int32 (decided per warp), 64-bit products otherwise;
+  // the same reduce-scatter either way.
+  for (int pi = 0; pi < npg; ++pi) {
+    if (!wait_page(pi)) break;
+    const int64_t* kr = (const int64_t*)(ringp + (pi % RING) * PB) + kk1 * DH + sl;
+    int kv[EPS];
+    bool fit = qall;
 #pragma unroll
-      for (int i = 0; i < EPS; ++i) kv[i] = k32[2 * i * S1];
-      uint64_t v[QB];
+    for (int i = 0; i < EPS; ++i) {
+      const int64_t x = kr[i * S1];
+      kv[i] = (int)x;
+      fit &= fits32(x);
+    }
+    fit = __all_sync(0xffffffffu, fit);
+    uint64_t v[QB];
+    if (fit) {
 #pragma unroll
       for (int qq = 0; qq < QB; ++qq) {
         int64_t acc = 0;
@@ -209,47 +225,37 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
         for (int i = 0; i < EPS; ++i) acc += (int64_t)qreg[qq][i] * (int64_t)kv[i];
         v[qq] = (uint64_t)acc;
       }
-      // reduce-scatter over the S1 lanes of this key: lane sl ends with the
-      // whole dot of query sl / LQ (wrapping sums, exact)
+    } else {  // 64-bit products, operands re-read from shared memory
 #pragma unroll
-      for (int st = 0, m = S1 / 2; m >= 1; ++st, m >>= 1) {
-        const int cnt = QB >> st;
-        if (cnt > 1) {
-          const bool up = (sl & m) != 0;
-#pragma unroll
-          for (int i = 0; i < cnt / 2; ++i) {
-            const uint64_t mine = up ? v[cnt / 2 + i] : v[i];
-            const uint64_t other = up ? v[i] : v[cnt / 2 + i];
-            v[i] = mine + (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)other, m);
-          }
-        } else {
-          v[0] += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v[0], m);
-        }
+      for (int qq = 0; qq < QB; ++qq) {
+        uint64_t acc = 0;
+        for (int i = 0; i < EPS; ++i) acc += (uint64_t)qs[qq * DH + i * S1 + sl] * (uint64_t)kr[i * S1];
+        v[qq] = acc;
       }
-      const int qq = sl / LQ, j = pi * PAGE + kk1;
-      if (sl % LQ == 0 && qq < nreal && !bad && j <= qpos(qq)) sc[qq * Tp + j] = attn_score((int64_t)v[0], attn_scale);
-    } else {
-      // general form (64-bit products): warp = query qi, lane = key kk of the
-      // page and half hh of the elements, halves summed by a shuffle
-      const int j = pi * PAGE + kk;
-      const int64_t* kr = kp + kk * DH + hh * HD;
-      const int64_t* qr = qs + qi * DH + hh * HD;
-      uint64_t a0 = 0, a1 = 0;
-      if (live && wpart == 0 && j <= pq) {
-#pragma unroll 4
-        for (int e0 = 0; e0 < HD; e0 += 2) {
-          const int e = (e0 + 2 * kk) & (HD - 1);
-          a0 += (uint64_t)qr[e] * (uint64_t)kr[e];
-          a1 += (uint64_t)qr[e + 1] * (uint64_t)kr[e + 1];
-        }
-      }
-      uint64_t acc = a0 + a1;
-      acc += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)acc, 16);
-      if (live && wpart == 0 && j <= pq && hh == 0) sc[qi * Tp + j] = attn_score((int64_t)acc, attn_scale);
     }
-    release();
+    // reduce-scatter over the S1 lanes of this key: lane sl ends with the
+    // whole dot of query sl / LQ (wrapping sums, exact)
+#pragma unroll
+    for (int st = 0, m = S1 / 2; m >= 1; ++st, m >>= 1) {
+      const int cnt = QB >> st;
+      if (cnt > 1) {
+        const bool up = (sl & m) != 0;
+#pragma unroll
+        for (int i = 0; i < cnt / 2; ++i) {
+          const uint64_t mine = up ? v[cnt / 2 + i] : v[i];
+          const uint64_t other = up ? v[i] : v[cnt / 2 + i];
+          v[i] = mine + (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)other, m);
+        }
+      } else {
+        v[0] += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v[0], m);
+      }
+    }
+    const int qq = sl / LQ, j = pi * PAGE + kk1;
+    if (sl % LQ == 0 && qq < nreal && !bad && j <= qpos(qq)) sc[qq * Tp + j] = attn_score((int64_t)v[0], attn_scale);
+    page_done(pi);
   }
   __syncthreads();
+  bool ok = s_abort == 0;
   // ---- pass 2: exact max and sum of exps per position (WM warps per query,
   // partial results combined through shared memory)
   const int Tq = pq + 1;
@@ -298,11 +304,15 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
       }
       sc[qi * Tp + jj] = w;
     }
+  // 64-bit partial outputs of pages that do not fit int32: the query rows'
+  // area, free after pass 1
+  unsigned long long* osl = (unsigned long long*)qs;
+  for (int i = tid; i < QB * DH; i += NT) osl[i] = 0;
   __syncthreads();
-  // ---- value pass.  Register-tiled form (int32 pages): thread = element
-  // slice es (elements es + 32 i), QG queries (qg0 .. qg0 + QG - 1), KPT keys
-  // of each page; hi/lo int32 accumulators (exact, see the header).  General
-  // form: warp (0, qi) = query qi, lane = elements lane + 32 m.
+  // ---- value pass: thread = element slice es (elements es + 32 i), QG
+  // queries (qg0 .. qg0 + QG - 1), KPT keys of each page.  Warps whose
+  // values fit in int32 use the hi/lo int32 accumulators (exact, see the
+  // header); otherwise 64-bit terms added into osl.
   constexpr int EPV = DH / 32, QG = DH == 128 ? 4 : 8, QH = QB / QG, KG = NT / 32 / QH, KPT = PAGE / KG;
   static_assert(QB % QG == 0 && PAGE % KG == 0, "value-pass tiling");
   const int es = tid & 31, rest = tid >> 5, kg = rest / QH, qg0 = (rest % QH) * QG;
@@ -313,24 +323,30 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
   for (int qq = 0; qq < QG; ++qq)
 #pragma unroll
     for (int i = 0; i < EPV; ++i) acch[qq][i] = 0, accl[qq][i] = 0;
-  // general-form partial outputs: the query rows' area, free after pass 1
-  unsigned long long* osl = (unsigned long long*)qs;
-  for (int i = tid; i < QB * DH; i += NT) osl[i] = 0;
   for (int pi = 0; pi < npg && ok; ++pi) {
     const int u = npg + pi;
-    if (!(ok = wait_use(u))) break;
-    const bool fast = page_fits(u);
+    if (!wait_page(u)) break;
     const int64_t* vp = (const int64_t*)(ringp + (u % RING) * PB);
-    if (fast) {
+    int vv[KPT][EPV];
+    bool fit = true;
 #pragma unroll
-      for (int h = 0; h < KPT; ++h) {
-        const int k = kg + KG * h, j = pi * PAGE + k;
-        const int* v32 = (const int*)(vp + k * DH + es);
+    for (int h = 0; h < KPT; ++h)
+#pragma unroll
+      for (int i = 0; i < EPV; ++i) {
+        const int64_t x = vp[(kg + KG * h) * DH + es + 32 * i];
+        vv[h][i] = (int)x;
+        fit &= fits32(x);
+      }
+    fit = __all_sync(0xffffffffu, fit);
+#pragma unroll
+    for (int h = 0; h < KPT; ++h) {
+      const int j = pi * PAGE + kg + KG * h;
+      if (fit) {
         int vh[EPV];
         unsigned vl[EPV];
 #pragma unroll
         for (int i = 0; i < EPV; ++i) {
-          const int v = v32[64 * i];
+          const int v = vv[h][i];
           vh[i] = v >> 16;
           vl[i] = (unsigned)v & 0xffffu;
         }
@@ -343,25 +359,25 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
             accl[qq][i] += ((unsigned)w * vl[i]) >> 16;
           }
         }
+      } else {
+        for (int qq = 0; qq < QG; ++qq) {
+          const int64_t w = sc[(qg0 + qq) * Tp + j];
+          if (w == 0) continue;
+#pragma unroll
+          for (int i = 0; i < EPV; ++i)
+            atomicAdd(osl + (qg0 + qq) * DH + es + 32 * i,
+                      (unsigned long long)mulshr(w, vp[(kg + KG * h) * DH + es + 32 * i]));
+        }
       }
-    } else if (live && wpart == 0) {
-      const int kmax = min(PAGE, Tq - pi * PAGE);
-      uint64_t o[EPV];
-#pragma unroll
-      for (int m = 0; m < EPV; ++m) o[m] = 0;
-      for (int k = 0; k < kmax; ++k) {
-        const int64_t w = sc[qi * Tp + pi * PAGE + k];
-#pragma unroll
-        for (int m = 0; m < EPV; ++m) o[m] += (uint64_t)mulshr(w, vp[k * DH + lane + 32 * m]);
-      }
-#pragma unroll
-      for (int m = 0; m < EPV; ++m) osl[qi * DH + lane + 32 * m] += o[m];  // one warp per query row
     }
-    release();
+    page_done(u);
   }
+  __syncthreads();
+  ok = ok && s_abort == 0;
   // copies in flight (only after an abort) must land before the CTA exits
   if (tid == 0)
-    for (int u = max(0, issued - RING); u < issued; ++u) mbar_wait(smem_u32(&full[u % RING]), (uint32_t)(u / RING) & 1u);
+    for (int st = 0; st < RING; ++st)
+      if (last_use[st] >= 0) mbar_wait(smem_u32(&full[st]), (uint32_t)(last_use[st] / RING) & 1u);
   // ---- both forms' partial outputs summed in shared memory (the idle ring)
   __syncthreads();
   unsigned long long* osm = (unsigned long long*)ringp;  // [QB][DH]
@@ -449,11 +465,11 @@ int arcb_attn_prefill(const int64_t* q, const int64_t* Kc, const int64_t* Vc, co
   if (n_kv <= 0 || n_heads % n_kv) return -2;
   const int T = p0 + nq;
   const bool wide = T <= arcb_attn_prefill_max_T(dh, 16);
+  // head dim 128: 8 positions per CTA, two warps per position (16 positions
+  // would need more than the 128 registers a 512-thread CTA can have)
   if (dh == 128)
-    return wide ? ap::launch<16, 128, 0, 1>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
-                                         lmax, err, st)
-                : ap::launch<8, 128, 0, 1>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
-                                        lmax, err, st);
+    return ap::launch<8, 128, 0, 2>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X, lmax,
+                                    err, st);
   if (dh == 64)
     return wide ? ap::launch<16, 64, 0, 1>(q, Kc, Vc, pt, 0, nullptr, nq, p0, n_heads, n_kv, attn_scale, max_T, B, T, X,
                                         lmax, err, st)
