@@ -40,6 +40,7 @@ _SIGS = {
     "arcb_blake3_batch_commit": (i32, [vp, i64, vp, i64, vp, vp, i64, vp, vp]),
     "arcb_merkle_root": (i32, [vp, i64, vp, vp, vp, vp]),
     "arcb_ep_wait_apply": (i32, [vp, vp, C.c_uint64, vp, vp, i64, vp, vp, vp]),
+    "arcb_check_udiv": (i32, [i64, i64, i32, vp, vp]),
     "arcb_ep_dispatch": (i32, [vp, i32, i32, vp, i32, vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, i32, vp, vp]),
     "arcb_attn_prefill": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, i64, i32, i32, vp, vp, vp, vp]),
     "arcb_attn_prefill_max_T": (i32, [i32, i32]),

@@ -486,6 +486,14 @@ def ep_dispatch(X, B: int, ldx: int, route, G: int, lcnt, rank: int, npeers: int
                                  _p(err), _s()), "ep_dispatch")
 
 
+def check_udiv(den0: int, den1: int, n_rand: int) -> int:
+    """Mismatches of the kernels' small-quotient division against the
+    compiler's 64-bit division (csrc/kernels/decode_ops.cu: k_check_udiv)."""
+    bad = torch.zeros(1, dtype=torch.int64, device="cuda")
+    check(lib().arcb_check_udiv(den0, den1, n_rand, _p(bad), _s()), "check_udiv")
+    return int(bad.item())
+
+
 def set_prefetch(epi: Epi, next_lin, tiles: int) -> None:
     """Points a fused GEMM's epilogue descriptor at the next GEMM's int8
     weights (cross-GEMM L2 prefetch of its first `tiles` tiles per CTA)."""

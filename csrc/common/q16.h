@@ -37,6 +37,24 @@ Q16_HD int64_t mulshr(int64_t a, int64_t b) { return wmul(a, b) >> FRAC_BITS; }
 // an explicit panic path, which cannot be reached with a positive divisor.
 Q16_HD int64_t tdiv(int64_t a, int64_t b) { return a / b; }
 
+// floor(num / den) for 0 <= num < 2^34 and den >= 1 whose quotient is below
+// 2^20 (the sigmoid and softmax weight divisions: quotients <= ONE).  On the
+// device: an estimate from single-precision operands and the correctly
+// rounded reciprocal (relative error below 2^-21, so within 1 of the true
+// quotient at these sizes), then the exact remainder decides a final +-1
+// (the last step of schoolbook long division).  The host divides directly.
+Q16_HD int64_t udiv_small(int64_t num, int64_t den) {
+#if defined(__CUDA_ARCH__)
+  uint64_t q = (uint64_t)((float)num * __frcp_rn((float)den));
+  const int64_t r = (int64_t)((uint64_t)num - q * (uint64_t)den);
+  if (r < 0) --q;
+  else if (r >= den) ++q;
+  return (int64_t)q;
+#else
+  return num / den;
+#endif
+}
+
 // exp LUT: T[256] = ONE, T[i] = (T[i+1] * 63521) >> 16 (integer_lut.rs:24-51).
 // The table is built by the recurrence so it has no float dependency.
 inline void build_exp_lut(int64_t* t) {
@@ -86,12 +104,12 @@ Q16_HD int64_t silu(int64_t x, const int64_t* lut) {
     int64_t e = integer_exp(wsub(0, x), lut);
     int64_t den = ONE + e;
     if (den < 1) den = 1;
-    sig = (ONE * ONE) / den;
+    sig = udiv_small(ONE * ONE, den);  // e in [0, ONE]: den in [ONE, 2 ONE]
   } else {
     int64_t e = integer_exp(x, lut);
     int64_t den = ONE + e;
     if (den < 1) den = 1;
-    sig = (e * ONE) / den;
+    sig = udiv_small(e * ONE, den);
   }
   return mulshr(x, sig);
 }

@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(NT) k_attn_cluster(const int64_t* __restrict__
     int64_t w;
     if (T == 1) w = ONE;
     else if (gsum == 0) w = ONE / T;
-    else w = wmul(sc[jj], ONE) / gsum;
+    else w = udiv_small(wmul(sc[jj], ONE), gsum);  // e <= gsum: quotient <= ONE
     sc[jj] = w;
   }
   __syncthreads();
@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(NT) k_attn_paged(const int64_t* __restrict__ q
     int64_t w;
     if (T == 1) w = ONE;
     else if (gsum == 0) w = ONE / T;
-    else w = wmul(sc[jj], ONE) / gsum;
+    else w = udiv_small(wmul(sc[jj], ONE), gsum);  // e <= gsum: quotient <= ONE
     sc[jj] = w;
   }
   __syncthreads();

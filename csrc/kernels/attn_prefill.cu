@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(QB * 32 * WM) k_attn_block(const int64_t* __re
       if (live && jj < Tq) {
         if (Tq == 1) w = ONE;
         else if (gsum == 0) w = ONE / Tq;
-        else w = wmul(sc[qi * Tp + jj], ONE) / gsum;
+        else w = udiv_small(wmul(sc[qi * Tp + jj], ONE), gsum);  // e <= gsum: quotient <= ONE
       }
       sc[qi * Tp + jj] = w;
     }

@@ -394,7 +394,7 @@ __global__ void k_attn_pv(const int64_t* __restrict__ Vc, const int* __restrict_
     int64_t w;
     if (T == 1) w = ONE;
     else if (s == 0) w = ONE / T;
-    else w = wmul(integer_exp(wsub(Sbh[j], mx), lut), ONE) / s;
+    else w = udiv_small(wmul(integer_exp(wsub(Sbh[j], mx), lut), ONE), s);
     wsh[j - j0] = w;
   }
   __syncthreads();
@@ -543,6 +543,32 @@ __global__ void k_rng_i8(uint64_t key, int8_t* __restrict__ out, int64_t n) {
 }  // namespace
 
 // ==================================================================== C ABI
+// Checks udiv_small (q16.h) against the compiler's 64-bit division on the
+// divisions the kernels make.  Sigmoid: every den in [den0, den1) (inside
+// [ONE, 2 ONE]) against num = ONE * ONE and every num = e * ONE, e in
+// [0, ONE].  Softmax weights: n_rand pseudo-random (e <= ONE, sum >= e up to
+// 2^40) pairs per thread.  Mismatches are counted into *bad.
+__global__ void k_check_udiv(int64_t den0, int64_t den1, int n_rand, unsigned long long* bad) {
+  unsigned long long nbad = 0;
+  const int64_t den = den0 + blockIdx.x;
+  if (den < den1) {
+    for (int64_t e = threadIdx.x; e <= ONE + 1; e += blockDim.x) {
+      const int64_t num = e <= ONE ? e * ONE : ONE * ONE;
+      nbad += udiv_small(num, den) != num / den;
+    }
+  }
+  uint64_t x = 0x9E3779B97F4A7C15ull * (blockIdx.x * blockDim.x + threadIdx.x + 1);
+  for (int i = 0; i < n_rand; ++i) {
+    x ^= x << 13, x ^= x >> 7, x ^= x << 17;  // xorshift64
+    const int64_t e = (int64_t)(x % (uint64_t)(ONE + 1));
+    x ^= x << 13, x ^= x >> 7, x ^= x << 17;
+    const int64_t sum = e + (int64_t)(x >> (24 + (x & 15)));  // spans many magnitudes
+    if (sum == 0) continue;
+    nbad += udiv_small(e * ONE, sum) != (e * ONE) / sum;
+  }
+  if (nbad) atomicAdd(bad, nbad);
+}
+
 extern "C" {
 
 static int g_pdl = 1;
@@ -616,6 +642,12 @@ int arcb_rng_i8(uint64_t seed, uint64_t stream, int8_t* out, int64_t n, void* st
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (blocks < 1) blocks = 1;
   return launch_k(k_rng_i8, dim3(blocks), dim3(256), 0, S_(st), key, out, n);
+}
+
+// Self-check of the kernels' exact small-quotient division (see k_check_udiv).
+int arcb_check_udiv(int64_t den0, int64_t den1, int n_rand, unsigned long long* bad, void* st) {
+  const int blocks = (int)(den1 - den0) > 0 ? (int)(den1 - den0) : 1;
+  return launch_k(k_check_udiv, dim3(blocks), dim3(256), 0, S_(st), den0, den1, n_rand, bad);
 }
 
 }  // extern "C"

@@ -266,6 +266,29 @@ __device__ __forceinline__ void apply_row(const Epi& E, int M, int m, bool valid
   }
 }
 
+// SWIGLU epilogue for two consecutive slots b, b + 1 at once (acc0, acc1:
+// row m's recombined sums of those slots).  Rows come in (gate, up) pairs;
+// the gate lane computes slot b's output and the up lane slot b + 1's, one
+// shuffle giving each the partner value it lacks.  Called by all 32 lanes.
+__device__ __forceinline__ void swiglu_pair(const Epi& E, int M, int m, bool valid, int b, uint64_t acc0,
+                                            uint64_t acc1, int& need) {
+  const int64_t s = valid ? E.scales[m] : 0;
+  const int64_t v0 = mulshr((int64_t)acc0, s), v1 = mulshr((int64_t)acc1, s);
+  const bool gate = (m & 1) == 0;
+  // gate lane sends its slot-(b+1) gate, up lane its slot-b up value
+  const int64_t other = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)(gate ? v1 : v0), 1);
+  const int bs = gate ? b : b + 1;
+  if (valid && bs < E.B) {
+    const int64_t y = gate ? swiglu(v0, other, g_exp_lut.v) : swiglu(other, v1, g_exp_lut.v);
+    int8_t dg[8];
+    const int n = limb_split8(y, dg);
+    need = n > need ? n : need;
+    const int j = m >> 1;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) E.X[limb_row(l, bs, E.B) * E.ldx + j] = dg[l];
+  }
+}
+
 // Tensor-parallel reduce mode: stores this rank's recombined sum of row m,
 // slot b into slot `rank` of every rank's receive buffer (plain stores to
 // peer memory; the caller fences and signals once the tile is complete).

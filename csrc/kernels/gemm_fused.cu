@@ -305,13 +305,29 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
           for (int l = 0; l < 8; ++l)
             if (l < L) tmem_ld8(taddr + (uint32_t)(l * S + s0), r[l]);
           tmem_ld_wait();
+          if (E.mode == SWIGLU) {
+            // slot pairs: the gate lane (even row) finishes slot j and the up
+            // lane (odd row) slot j + 1, so no lane of the pair idles
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint64_t acc = 0;
+            for (int j = 0; j < 8; j += 2) {
+              uint64_t a0 = 0, a1 = 0;
 #pragma unroll
-            for (int l = 0; l < 8; ++l)
-              if (l < L) acc += (uint64_t)(int64_t)(int)r[l][j] << (8 * l);
-            apply_row(E, M, m, valid, sb0 + s0 + j, acc, need);
+              for (int l = 0; l < 8; ++l)
+                if (l < L) {
+                  a0 += (uint64_t)(int64_t)(int)r[l][j] << (8 * l);
+                  a1 += (uint64_t)(int64_t)(int)r[l][j + 1] << (8 * l);
+                }
+              swiglu_pair(E, M, m, valid, sb0 + s0 + j, a0, a1, need);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint64_t acc = 0;
+#pragma unroll
+              for (int l = 0; l < 8; ++l)
+                if (l < L) acc += (uint64_t)(int64_t)(int)r[l][j] << (8 * l);
+              apply_row(E, M, m, valid, sb0 + s0 + j, acc, need);
+            }
           }
         }
       } else if (direct) {

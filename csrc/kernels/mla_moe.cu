@@ -245,7 +245,7 @@ __global__ void k_moe_route(const int64_t* __restrict__ logits, int ldl, int E, 
     }
     const int64_t sum = (int64_t)warp_sum_u64(su);
 #pragma unroll
-    for (int j = 0; j < PER; ++j) p[j] = sum == 0 ? ONE / E : wmul(p[j], ONE) / sum;
+    for (int j = 0; j < PER; ++j) p[j] = sum == 0 ? ONE / E : udiv_small(wmul(p[j], ONE), sum);
   }
   for (int e = lane; e < E + S; e += 32) out[e] = e < E ? 0 : ONE;
   __syncwarp();

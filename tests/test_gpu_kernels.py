@@ -318,3 +318,12 @@ def test_sample_penalty_and_argmax_match_reference():
                    gen_, tok)
         torch.cuda.synchronize()
         assert tok.cpu().tolist() == want, cnt
+
+
+def test_small_quotient_division_is_exact():
+    """The kernels' sigmoid and softmax-weight divisions (an estimate from the
+    single-precision reciprocal plus one remainder correction) equal the
+    64-bit division on every sigmoid divisor and a random softmax sweep."""
+    ops = _ops()
+    one = 1 << 16
+    assert ops.check_udiv(one, 2 * one + 1, 64) == 0
