@@ -150,7 +150,13 @@ def main():
                 r["name"] = name
                 print(json.dumps(r), flush=True)
     if a.only == "optimeline_batched":
-        print(json.dumps(op_timeline_batched(a.model or "llama70b", a.B if a.B > 1 else 64, a.T)), flush=True)
+        from arc_chain_b200.utils.clocks import ClockSampler
+
+        with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+            r = op_timeline_batched(a.model or "llama70b", a.B if a.B > 1 else 64, a.T)
+        r["clocks"] = clk.summary()
+        if r["rank"] == 0:
+            print(json.dumps(r), flush=True)
         return
     if a.only == "optimeline":
         # per-op device time of one eager 7B decode step (CUDA events between launches)
@@ -419,19 +425,33 @@ def op_timeline_moe(model: str = "dsv2lite", B: int = 32, T: int = 512, reps: in
 
 def op_timeline_batched(model: str = "llama70b", B: int = 64, T: int = 800, reps: int = 3) -> dict:
     """Per-op device time of one eager decode step over B slots, every slot at
-    position T - 1 (distinct pages), on one GPU: where a batched step's time goes."""
+    position T - 1 (distinct pages): where a batched step's time goes.  Under
+    torch.distributed.run: tensor-parallel over the ranks (fused in-kernel
+    reduce), each op the maximum over ranks."""
     import collections
+
+    import torch.distributed as dist
 
     from arc_chain_b200.models import dense
     from arc_chain_b200.models.config import preset
-    from arc_chain_b200.runtime.engine import Engine
+    from arc_chain_b200.runtime.engine import Comm, Engine
 
-    torch.cuda.set_device(0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank, comm = 0, Comm()
+    if world > 1:
+        from arc_chain_b200.parallel import tp
+        from arc_chain_b200.parallel.fused import FusedComm
+
+        rank, world = tp.init_distributed()
+        comm = FusedComm()
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
     cfg = preset(model)
     cfg.max_seq = (T + 16 + 15) // 16 * 16
-    m = dense.random_device(cfg, torch.device("cuda", 0), seed=0)
+    m = dense.random_device(cfg, dev, seed=0, tp_rank=rank, tp_size=world)
     pps = cfg.max_seq // 16
-    eng = Engine(m, max_seq=cfg.max_seq, n_pages=B * pps + 4)
+    eng = Engine(m, max_seq=cfg.max_seq, n_pages=B * pps + 4, comm=comm)
     bb = eng.buffers(B, gen_cap=8)
     bb.tokens.copy_(torch.arange(B, dtype=torch.int32) * 7 + 3)
     bb.pos.fill_(T - 1)
@@ -441,6 +461,8 @@ def op_timeline_batched(model: str = "llama70b", B: int = 64, T: int = 800, reps
     agg, cnt = collections.defaultdict(float), collections.Counter()
     for _ in range(reps):
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         eng.op_events = []
         torch.cuda._sleep(80_000_000)
         e0 = torch.cuda.Event(enable_timing=True)
@@ -453,9 +475,20 @@ def op_timeline_batched(model: str = "llama70b", B: int = 64, T: int = 800, reps
             cnt[lab] += 1
             prev = e
         eng.op_events = None
-    return {"model": model, "B": B, "T": T, "total_us": round(sum(agg.values()), 1), "kernel_errors": eng.check_errors(),
-            "per_op_us": {k: {"launches": cnt[k] // reps, "total": round(v, 1), "each": round(v / max(1, cnt[k] // reps), 2)}
-                          for k, v in agg.items()}}
+    agg = _max_over_ranks(agg, world)
+    out = {"model": model, "B": B, "T": T, "world": world, "total_us": round(sum(agg.values()), 1),
+           "kernel_errors": eng.check_errors(), "rank": rank,
+           "per_op_us": {k: {"launches": cnt[k] // reps, "total": round(v, 1), "each": round(v / max(1, cnt[k] // reps), 2)}
+                         for k, v in agg.items()}}
+    if world > 1:
+        import gc
+
+        eng._graphs.clear()
+        gc.collect()
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
 
 
 if __name__ == "__main__":
