@@ -312,43 +312,91 @@ __device__ __forceinline__ void emit_row(const Epi& E, int M, int B, int m, bool
   else apply_row(E, M, m, valid, b, acc, need);
 }
 
-// Reduce-scatter owner: row m of slots [bb0, bb1) summed over the npeers
-// slots and stored into every rank's final area (slot npeers of peer_R).
-__device__ __forceinline__ void owner_sum_to_all(const Epi& E, int M, int m, bool valid, int B, int bb0, int bb1) {
-  if (!valid) return;
-  const int64_t* R = E.peer_R[E.rank];
-  for (int b = bb0; b < bb1; ++b) {
-    uint64_t acc = 0;
-#pragma unroll 8
-    for (int r = 0; r < E.npeers; ++r) acc += (uint64_t)__ldcg((const long long*)(R + ((size_t)r * B + b) * M + m));
-    const size_t off = ((size_t)E.npeers * B + b) * M + m;
-    for (int p = 0; p < E.npeers; ++p) __stcg((long long*)(E.peer_R[p] + off), (long long)acc);
+// Applies the epilogue to row m of FG consecutive slots b0.. whose sums
+// are already in registers.  RESID loads the FG hidden-state values first,
+// so their latencies overlap instead of adding up slot by slot; the other
+// modes go through apply_row.  Called by all lanes of a warp together.
+template <int FG>
+__device__ __forceinline__ void apply_rows(const Epi& E, int M, int m, bool valid, int b0, int nb,
+                                           const uint64_t (&acc)[FG], int& need) {
+  if (E.mode == RESID) {
+    const int64_t s = valid ? E.scales[m] : 0;
+    int64_t h[FG];
+#pragma unroll
+    for (int j = 0; j < FG; ++j) h[j] = (valid && j < nb) ? __ldcg(E.out + (size_t)(b0 + j) * E.ldo + m) : 0;
+#pragma unroll
+    for (int j = 0; j < FG; ++j) {
+      if (j >= nb) break;
+      uint64_t sq = 0;
+      if (valid) {
+        const int64_t r = wadd(h[j], mulshr((int64_t)acc[j], s));
+        E.out[(size_t)(b0 + j) * E.ldo + m] = r;
+        sq = sq16(r);
+      }
+      if (E.ss_out) {
+        sq = warp_sum_u64(sq);
+        if ((threadIdx.x & 31) == 0) atomicAdd(E.ss_out + b0 + j, (unsigned long long)sq);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < FG; ++j)
+      if (j < nb) apply_row(E, M, m, valid, b0 + j, acc[j], need);
   }
 }
 
-// All-gather receiver: row m of slots [bb0, bb1) from this rank's final area.
+// Reduce-scatter owner: row m of slots [bb0, bb1) summed over the npeers
+// slots and stored into every rank's final area (slot npeers of peer_R);
+// four slots' loads in flight at a time.
+__device__ __forceinline__ void owner_sum_to_all(const Epi& E, int M, int m, bool valid, int B, int bb0, int bb1) {
+  if (!valid) return;
+  const int64_t* R = E.peer_R[E.rank];
+  constexpr int FG = 4;
+  for (int b0 = bb0; b0 < bb1; b0 += FG) {
+    uint64_t acc[FG] = {0, 0, 0, 0};
+    for (int r = 0; r < E.npeers; ++r)
+#pragma unroll
+      for (int j = 0; j < FG; ++j)
+        if (b0 + j < bb1) acc[j] += (uint64_t)__ldcg((const long long*)(R + ((size_t)r * B + b0 + j) * M + m));
+    for (int p = 0; p < E.npeers; ++p)
+#pragma unroll
+      for (int j = 0; j < FG; ++j)
+        if (b0 + j < bb1)
+          __stcg((long long*)(E.peer_R[p] + ((size_t)E.npeers * B + b0 + j) * M + m), (long long)acc[j]);
+  }
+}
+
+// All-gather receiver: row m of slots [bb0, bb1) from this rank's final
+// area, eight slots at a time.
 __device__ __forceinline__ void finalize_from_F(const Epi& E, int M, int m, bool valid, int B, int& need, int bb0,
                                                 int bb1) {
   const int64_t* F = E.peer_R[E.rank] + (size_t)E.npeers * B * M;
-  for (int b = bb0; b < bb1; ++b) {
-    const uint64_t acc = valid ? (uint64_t)__ldcg((const long long*)(F + (size_t)b * M + m)) : 0;
-    apply_row(E, M, m, valid, b, acc, need);
+  constexpr int FG = 8;
+  for (int b0 = bb0; b0 < bb1; b0 += FG) {
+    uint64_t acc[FG];
+#pragma unroll
+    for (int j = 0; j < FG; ++j)
+      acc[j] = (valid && b0 + j < bb1) ? (uint64_t)__ldcg((const long long*)(F + (size_t)(b0 + j) * M + m)) : 0;
+    apply_rows<FG>(E, M, m, valid, b0, bb1 - b0, acc, need);
   }
 }
 
 // Tensor-parallel finaliser: row m of slots [bb0, bb1) is the wrapping sum
 // of the npeers ranks' slots of this rank's receive buffer (exact, so the
-// order does not matter and every rank computes the same value).
+// order does not matter and every rank computes the same value); four
+// slots' loads in flight at a time.
 __device__ __forceinline__ void finalize_from_R(const Epi& E, int M, int m, bool valid, int B, int& need, int bb0,
                                                 int bb1) {
   const int64_t* R = E.peer_R[E.rank];
-  for (int b = bb0; b < bb1; ++b) {
-    uint64_t acc = 0;
-    if (valid) {
-#pragma unroll 8
-      for (int r = 0; r < E.npeers; ++r) acc += (uint64_t)__ldcg((const long long*)(R + ((size_t)r * B + b) * M + m));
-    }
-    apply_row(E, M, m, valid, b, acc, need);
+  constexpr int FG = 4;
+  for (int b0 = bb0; b0 < bb1; b0 += FG) {
+    uint64_t acc[FG] = {0, 0, 0, 0};
+    if (valid)
+      for (int r = 0; r < E.npeers; ++r)
+#pragma unroll
+        for (int j = 0; j < FG; ++j)
+          if (b0 + j < bb1) acc[j] += (uint64_t)__ldcg((const long long*)(R + ((size_t)r * B + b0 + j) * M + m));
+    apply_rows<FG>(E, M, m, valid, b0, bb1 - b0, acc, need);
   }
 }
 
@@ -363,7 +411,7 @@ __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int
                                                 int& need, int bb0 = 0, int bb1 = -1) {
   // slots [bb0, bb1) of the partial buffer (row l * B + b); the whole batch by default
   if (bb1 < 0) bb1 = B;
-  if constexpr (BN >= 64 && !PUSH) {
+  if constexpr (BN >= 64) {
     constexpr int FS = 4;  // slots per round: 4 x L loads in flight, no spills
     for (int b0 = bb0; b0 < bb1; b0 += FS) {
       int v[8][FS];
@@ -383,7 +431,7 @@ __device__ __forceinline__ void finalize_from_P(const Epi& E, int* P, int M, int
         uint64_t acc = 0;
 #pragma unroll
         for (int l = 0; l < 8; ++l) acc += (uint64_t)(int64_t)v[l][j] << (8 * l);
-        apply_row(E, M, m, valid, b0 + j, acc, need);
+        emit_row<PUSH>(E, M, B, m, valid, b0 + j, acc, need);
       }
     }
   } else {

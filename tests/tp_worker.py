@@ -38,6 +38,8 @@ def main():
         comm = FusedComm(fuse_logits=a.comm in ("fused-logits", "fused-norm"),
                          rs_ag="on" if a.comm == "fused-rsag" else "auto")
     cfg = preset("tiny")
+    if cfg.n_heads % world:  # whole heads per rank: 8 heads of 64 for 8 ranks
+        cfg = dataclasses.replace(cfg, d_model=512, n_heads=8, n_kv_heads=8, d_ff=1536)
     if (cfg.d_ff // world) % 16:  # TP shards of the FFN must stay 16-byte rows
         cfg = dataclasses.replace(cfg, d_ff=768)
     host = gen.random_model(cfg, 0)
