@@ -79,13 +79,19 @@ Q16_HD int64_t integer_exp(int64_t x, const int64_t* lut) {
 Q16_HD int64_t integer_isqrt(int64_t x) {
   if (x <= 0) return ONE * 100;
   uint64_t ux = (uint64_t)x;
+#if defined(__CUDA_ARCH__)
+  const int lz = __clzll((long long)ux);  // leading zeros (x > 0)
+#else
   int lz = 0;
   for (int b = 63; b >= 0; --b) {
     if ((ux >> b) & 1) break;
     ++lz;
   }
+#endif
   int64_t bits = 63 - lz;
-  int64_t y = ONE * 256 / (int64_t(1) << ((bits + 1) / 2));
+  // ONE * 256 / 2^k with k <= 32: a positive dividend over a power of two,
+  // so the truncating division is the right shift
+  int64_t y = (ONE * 256) >> ((bits + 1) / 2);
   if (y <= 0) y = 1;
   for (int it = 0; it < 3; ++it) {
     int64_t y2 = wmul(y, y) >> FRAC_BITS;

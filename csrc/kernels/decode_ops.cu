@@ -160,7 +160,11 @@ __global__ void k_norm_limbs(const int64_t* __restrict__ h, const uint64_t* __re
   __shared__ int shi[32];
   const int b = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t inv = rms_inv((int64_t)ss[b], d);
+  // one inverse RMS per warp (an integer square root and a 64-bit division),
+  // broadcast to its lanes
+  int64_t inv = 0;
+  if ((threadIdx.x & 31) == 0) inv = rms_inv((int64_t)ss[b], d);
+  inv = (int64_t)__shfl_sync(0xffffffffu, (long long)inv, 0);
   int need = 0;
   if (j < d) {
     const size_t off = (size_t)b * d + j;
@@ -185,7 +189,9 @@ __global__ void k_rmsnorm_limbs(const int64_t* __restrict__ h, const int64_t* __
   uint64_t ss = 0;
   for (int j = threadIdx.x; j < d; j += blockDim.x) ss += sq16(x[j]);
   ss = block_sum_u64(ss, sh);
-  const int64_t inv = rms_inv((int64_t)ss, d);
+  int64_t inv = 0;
+  if ((threadIdx.x & 31) == 0) inv = rms_inv((int64_t)ss, d);
+  inv = (int64_t)__shfl_sync(0xffffffffu, (long long)inv, 0);
   int need = 0;
   for (int j = threadIdx.x; j < d; j += blockDim.x) {
     const int64_t y = rms_apply(x[j], inv, j < ngamma ? gamma[j] : ONE);
