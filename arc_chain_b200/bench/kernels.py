@@ -163,7 +163,7 @@ def main():
         from arc_chain_b200.utils.clocks import ClockSampler
 
         with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
-            r = op_timeline(fuse_norm=os.environ.get("ARCB_FUSE_NORM") == "1")
+            r = op_timeline()
         r["clocks"] = clk.summary()
         if r["rank"] == 0:
             print(json.dumps(r), flush=True)
@@ -271,7 +271,7 @@ def timeline_fgemm(M, K, B=1, reps=5):
 
 
 
-def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -> dict:
+def op_timeline(prompt_len: int = 128, reps: int = 5) -> dict:
     """Mean device time of each op of one eager decode step of the 7B
     architecture (events recorded between launches; the whole step is queued
     behind a sleep so launch overhead is not timed), one rank per GPU when
@@ -300,7 +300,6 @@ def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -
     m = dense.random_device(cfg, torch.device("cuda", torch.cuda.current_device()), seed=0, tp_rank=rank,
                             tp_size=world)
     eng = Engine(m, max_seq=400, comm=comm, n_pages=64)
-    eng.fuse_norm = fuse_norm
     p = gen.seeded_prompt(prompt_len, cfg.vocab, 1)
     rid = eng.new_request(prompt_len + 100)
     eng.prefill(rid, [1] + p)
@@ -326,7 +325,7 @@ def op_timeline(prompt_len: int = 128, reps: int = 5, fuse_norm: bool = False) -
             prev = e
         eng.op_events = None
     agg = _max_over_ranks(agg, world)
-    out = {"world": world, "fuse_norm": eng._norm_fused(), "total_us": round(sum(agg.values()), 1),
+    out = {"world": world, "total_us": round(sum(agg.values()), 1),
            "per_op_us": {k: {"launches": cnt[k] // reps, "total": round(v, 1), "each": round(v / max(1, cnt[k] // reps), 2)}
                          for k, v in agg.items()}, "rank": rank}
     if world > 1:

@@ -188,10 +188,8 @@ class Epi(C.Structure):
                 ("peer_cnt", C.c_void_p), ("cnt_local", C.c_void_p), ("prof", C.c_void_p),
                 ("grp_rows", C.c_int), ("grp_koff", C.c_int), ("route", C.c_void_p), ("route_ld", C.c_int),
                 ("max_ctas", C.c_int), ("b_box", C.c_int), ("route_gs", C.c_int), ("peer_h", C.c_void_p),
-                ("peer_sig", C.c_void_p), ("pf_w", C.c_void_p), ("pf_M", C.c_int), ("pf_K", C.c_int),
-                ("pf_tiles", C.c_int), ("sched", C.c_int), ("nrm_gamma", C.c_void_p), ("nrm_ngamma", C.c_int),
-                ("nrm_X", C.c_void_p), ("nrm_lmax", C.c_void_p), ("nrm_cnt", C.c_void_p), ("rs_ag", C.c_int),
-                ("rs_cnt_off", C.c_int), ("ep_rows", C.c_int)]
+                ("peer_sig", C.c_void_p), ("sched", C.c_int), ("rs_ag", C.c_int), ("rs_cnt_off", C.c_int),
+                ("ep_rows", C.c_int)]
 
 
 PARTIAL, STORE, RESID, QKV, SWIGLU, MOE_COMBINE, STORE_PEERS = 0, 1, 2, 3, 4, 5, 6
@@ -492,13 +490,3 @@ def check_udiv(den0: int, den1: int, n_rand: int) -> int:
     bad = torch.zeros(1, dtype=torch.int64, device="cuda")
     check(lib().arcb_check_udiv(den0, den1, n_rand, _p(bad), _s()), "check_udiv")
     return int(bad.item())
-
-
-def set_prefetch(epi: Epi, next_lin, tiles: int) -> None:
-    """Points a fused GEMM's epilogue descriptor at the next GEMM's int8
-    weights (cross-GEMM L2 prefetch of its first `tiles` tiles per CTA)."""
-    if next_lin is None or getattr(next_lin, "w", None) is None or tiles <= 0:
-        epi.pf_w, epi.pf_tiles = None, 0
-        return
-    epi.pf_w = next_lin.w.data_ptr()
-    epi.pf_M, epi.pf_K, epi.pf_tiles = next_lin.M, next_lin.K, int(tiles)

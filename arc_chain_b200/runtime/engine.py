@@ -91,7 +91,6 @@ class StepBuffers:
         # per-norm sum of squares: [2 * n_layers + 1, B] (u64 bits in int64)
         self.ss = torch.zeros(2 * c.n_layers + 1, B, dtype=I64, device=dev)
         self.err = torch.zeros(1, dtype=I32, device=dev)
-        self.nrm_cnt = torch.zeros(2, dtype=I32, device=dev)  # fused-norm tile / CTA counters
         self.logits_local = torch.zeros(B, model.vocab_local, dtype=I64, device=dev)
         self.logits = self.logits_local if model.tp_size == 1 else torch.zeros(B, c.vocab, dtype=I64, device=dev)
         # sampling state (one sampled slot per row)
@@ -121,19 +120,10 @@ class Engine:
         self._bufs: Dict[Tuple[int, int], StepBuffers] = {}
         self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self._rid = 0
-        # weight tiles per CTA each fused GEMM prefetches into L2 for the next one
-        self.prefetch_tiles = 0
         # NVTX ranges per layer and phase (ARCB_NVTX=1), for timeline profilers
         self.nvtx = bool(os.environ.get("ARCB_NVTX"))
         # optional op timeline of eager forwards: list of (label, CUDA event) appended after each op
         self.op_events = None
-        # RMSNorms fused into the preceding residual GEMM (W_o -> FFN norm,
-        # W_down -> next attention norm / final norm); set before the first
-        # forward.  Exact, but measured slower on the 7B decode (3.01 vs 2.85
-        # ms/token): a separate norm kernel lets the next GEMM's CTAs become
-        # resident and prefetch weights while it runs, which the fused form,
-        # holding every SM until its norm phase ends, gives up.
-        self.fuse_norm = os.environ.get("ARCB_FUSE_NORM", "0") == "1"
         # prefill chunks: one chunk-attention launch per layer (each K/V page
         # read once per 16 positions) instead of the per-position decode kernel
         self.prefill_attn = os.environ.get("ARCB_PREFILL_ATTN", "1") != "0"
@@ -168,7 +158,6 @@ class Engine:
         ss = bb.ss
         E = self._epis(bb)
         reduce_in_kernel = cm.size == 1 or getattr(cm, "fused", False)
-        fused_norm = self._norm_fused()
         nv = torch.cuda.nvtx if self.nvtx else None
         ev = self.op_events
 
@@ -184,9 +173,8 @@ class Engine:
             e = E[l]
             if nv:
                 nv.range_push(f"layer {l} attention")
-            if l == 0 or not fused_norm:
-                ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
-                mark("norm")
+            ops.norm_limbs(bb.h, ss[2 * l], Ly.attn_norm, d, B, bb.Xd, c0)
+            mark("norm")
             ops.linear_gemm(Ly.qkv, bb.mXd, B, c0, bb.P, bb.tiles, e["qkv"])
             mark("qkv")
             T_all = self.max_pages * PAGE
@@ -214,9 +202,8 @@ class Engine:
             if nv:
                 nv.range_pop()
                 nv.range_push(f"layer {l} ffn")
-            if not fused_norm:
-                ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
-                mark("norm")
+            ops.norm_limbs(bb.h, ss[2 * l + 1], Ly.ffn_norm, d, B, bb.Xd, c2)
+            mark("norm")
             ops.linear_gemm(Ly.gu, bb.mXd, B, c2, bb.P, bb.tiles, e["gu"])
             mark("gate_up")
             if reduce_in_kernel:
@@ -230,8 +217,7 @@ class Engine:
                 nv.range_pop()
         if with_logits:
             cf = bb.cnt[4 * c.n_layers:4 * c.n_layers + 1]
-            if not fused_norm:
-                ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
+            ops.norm_limbs(bb.h, ss[2 * c.n_layers], m.final_norm, d, B, bb.Xd, cf)
             lm_e = cm.lm_epi(E[-1]["lm"], bb, c.vocab, m.vocab_offset) if hasattr(cm, "lm_epi") else E[-1]["lm"]
             ops.linear_gemm(m.lm, bb.mXd, B, cf, bb.P, bb.tiles, lm_e)
             cm.gather_logits(bb.logits_local, bb.logits, B, m.vocab_offset, bb=bb)
@@ -239,7 +225,7 @@ class Engine:
 
     def _epis(self, bb: StepBuffers):
         """Epilogue descriptors of every fused GEMM of a forward over `bb`."""
-        if bb.epis is not None and getattr(bb, "epis_norm", None) == self._norm_fused():
+        if bb.epis is not None:
             return bb.epis
         m, c = self.m, self.m.cfg
         d, dh = c.d_model, c.d_head
@@ -257,31 +243,8 @@ class Engine:
                 "partial": ops.epi(ops.PARTIAL, Ly.wo.s, bb.err),
             })
         out.append({"lm": ops.epi(ops.STORE, m.lm.s, bb.err, out=bb.logits_local, ldo=m.lm.M)})
-        if self._norm_fused():
-            L = c.n_layers
-            for l, Ly in enumerate(m.layers):
-                nxt_gamma = m.layers[l + 1].attn_norm if l + 1 < L else m.final_norm
-                nxt_cnt = bb.cnt[4 * (l + 1):4 * (l + 1) + 1]  # = the final norm's counter after the last layer
-                for e, g, lm in ((out[l]["wo"], Ly.ffn_norm, bb.cnt[4 * l + 2:4 * l + 3]),
-                                 (out[l]["down"], nxt_gamma, nxt_cnt)):
-                    e.nrm_gamma, e.nrm_ngamma = g.data_ptr(), g.numel()
-                    e.nrm_X, e.nrm_lmax, e.nrm_cnt = bb.Xd.data_ptr(), lm.data_ptr(), bb.nrm_cnt.data_ptr()
-        # each GEMM prefetches the first weight tiles of the next one in the step
-        chain = []
-        for l, Ly in enumerate(m.layers):
-            chain += [(out[l]["qkv"], Ly.qkv), (out[l]["wo"], Ly.wo), (out[l]["gu"], Ly.gu),
-                      (out[l]["down"], Ly.down)]
-        chain.append((out[-1]["lm"], m.lm))
-        for (e, _), (_, nxt) in zip(chain, chain[1:]):
-            ops.set_prefetch(e, nxt, self.prefetch_tiles)
         bb.epis = out
-        bb.epis_norm = self._norm_fused()
         return out
-
-    def _norm_fused(self) -> bool:
-        """Norms run inside the residual GEMMs (needs the in-kernel reduce)."""
-        cm = self.comm
-        return bool(self.fuse_norm) and (cm.size == 1 or getattr(cm, "fused", False))
 
     def decode_step(self, bb: StepBuffers) -> None:
         """forward + sample for every slot; slots advance in place."""

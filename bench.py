@@ -63,8 +63,6 @@ def main():
                          "token on every rank")
     ap.add_argument("--fuse-logits", type=int, default=0,
                     help="with --comm fused: the LM head also all-gathers its logits in-kernel")
-    ap.add_argument("--fuse-norm", type=int, default=-1,
-                    help="1: RMSNorms run inside the residual GEMMs; 0: separate kernels; -1: engine default")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", default="decode", choices=["decode", "batched", "moe", "specdec"],
                     help="decode: the headline 7B single-stream ms/token; batched: 70B-architecture continuous "
@@ -72,7 +70,6 @@ def main():
     ap.add_argument("--requests", type=int, default=128)
     ap.add_argument("--draft", default="draft1b", help="specdec draft: a preset name, or 'self' (the target's weights)")
     ap.add_argument("--batch", type=int, default=0)
-    ap.add_argument("--prefetch", type=int, default=0, help="weight tiles per CTA each GEMM prefetches for the next")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -161,9 +158,6 @@ def main():
     model = dense.random_device(cfg, dev, seed=0, tp_rank=rank, tp_size=world)
     log("weights ready")
     eng = Engine(model, max_seq=max_seq, comm=comm, n_pages=2 * ((max_seq + 15) // 16))
-    eng.prefetch_tiles = args.prefetch
-    if args.fuse_norm >= 0:
-        eng.fuse_norm = bool(args.fuse_norm)
     prompt = gen.seeded_prompt(args.prompt_len, cfg.vocab, 1)
 
     W, K, G = args.warmup, args.steps, args.gen_len
@@ -254,8 +248,6 @@ def main():
                        "global_batch": 1, "seq_len": args.prompt_len, "gen_len": G,
                        "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
                        "l2": "weights per GPU >> 126 MB L2 (streamed from HBM every step)",
-                       "prefetch_tiles": args.prefetch,
-                       "fuse_norm": bool(eng._norm_fused()),
                        "fuse_logits": bool(getattr(comm, "fuse_logits", False)),
                        "tokens_per_s": round(1000.0 / ms_tok, 2)},
             "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches_per_step * K),

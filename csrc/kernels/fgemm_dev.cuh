@@ -95,28 +95,9 @@ struct Epi {
   int route_gs;
   int64_t* const* peer_h;
   unsigned long long* const* peer_sig;
-  // Cross-GEMM prefetch: once this CTA's producer has issued its last load,
-  // it asks L2 for the first pf_tiles weight tiles that the same CTA index
-  // will stream in the next GEMM (tiled int8 weights pf_w of [pf_M, pf_K],
-  // one N tile, the same grid), so HBM stays busy through this GEMM's tail
-  // and the next GEMM's first stages hit L2.  null = off.
-  const uint8_t* pf_w;
-  int pf_M, pf_K, pf_tiles;
   // Work schedule of launches with several n-tiles: 0 = round-robin whole
   // tiles / n-tile groups (struct Work), 1 = plain stream-K.
   int sched;
-  // Fused RMSNorm of the updated residual (RESID mode; nrm_gamma = null:
-  // off).  Every finalised tile adds 1 to nrm_cnt[0]; once it reaches the
-  // tile count, each CTA normalises its share of out ([B, ldo], the hidden
-  // state) with the completed sums of squares ss_out, writes the next
-  // GEMM's limb planes nrm_X ([8 planes, ldo] in the limb_row layout) and
-  // raises nrm_lmax to their limb count.  nrm_cnt[1] counts CTAs done; the
-  // last resets both.  The wait is bounded (ARCB_ERR_TIMEOUT_DONE).
-  const int64_t* nrm_gamma;
-  int nrm_ngamma;
-  int8_t* nrm_X;
-  int* nrm_lmax;
-  int* nrm_cnt;
   // Tensor-parallel reduce-scatter + all-gather (rp = 1 and rs_ag = 1), for
   // large batches on 4+ ranks: the completed tile's sums go only to its
   // owner rank (m-tile index mod npeers) and bump only the owner's counter;

@@ -179,17 +179,6 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
       if (!ok)
         for (int i = max(0, issued - C::STAGES); i < issued; ++i)
           mbar_wait(full(i % C::STAGES), (uint32_t)(i / C::STAGES) & 1u);
-      if (ok && E.pf_w && E.pf_tiles > 0) {
-        const int mt2 = (E.pf_M + BM - 1) / BM, nch2 = (E.pf_K + BK - 1) / BK;
-        const long long tot2 = (long long)mt2 * nch2;
-        const int a0 = (int)(tot2 * blockIdx.x / gridDim.x), a1 = (int)(tot2 * (blockIdx.x + 1) / gridDim.x);
-        const int np = min(a1 - a0, E.pf_tiles);
-        for (int j = 0; j < np; ++j) {
-          const int it = a0 + j;
-          const uint8_t* src = E.pf_w + ((size_t)((it / nch2) % mt2) * nch2 + (it % nch2)) * (BM * BK);
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(BM * BK) : "memory");
-        }
-      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -399,12 +388,6 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         pushed = last;
         epi_bar();
       }
-      if (E.nrm_gamma && !E.rp && pushed) {
-        // this tile's rows and sums of squares are final: count it for the fused norm
-        __threadfence();
-        epi_bar();
-        if (warp == 2 && lane == 0) atomicAdd(E.nrm_cnt, 1);
-      }
       if (E.rp && pushed) {
         // the tile's sums are in every rank's receive buffer: signal each rank once
         __threadfence_system();
@@ -469,12 +452,8 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         const int m = mt * BM + q * 32 + lane;
         int need = 0;
         finalize_from_F(E, M, m, m < M, B, need, sb0, sb0 + nb);
-        if (E.nrm_gamma) __threadfence();
         epi_bar();
-        if (warp == 2 && lane == 0) {
-          E.cnt_local[E.rs_cnt_off + t] = 0;
-          if (E.nrm_gamma) atomicAdd(E.nrm_cnt, 1);
-        }
+        if (warp == 2 && lane == 0) E.cnt_local[E.rs_cnt_off + t] = 0;
       }
       if (E.prof && warp == 2 && lane == 0) E.prof[blockIdx.x * 8 + 5] = globaltimer_ns();
     } else if (E.rp && E.mode != PARTIAL) {
@@ -496,57 +475,10 @@ __global__ void __launch_bounds__(Cfg<BN, Q4>::THREADS, 1)
         const bool valid = m < M;
         int need = 0;
         finalize_from_R(E, M, m, valid, B, need, sb0, sb0 + nb);
-        if (E.nrm_gamma) __threadfence();
         epi_bar();
-        if (warp == 2 && lane == 0) {
-          E.cnt_local[t] = 0;
-          if (E.nrm_gamma) atomicAdd(E.nrm_cnt, 1);
-        }
+        if (warp == 2 && lane == 0) E.cnt_local[t] = 0;
       }
       if (E.prof && warp == 2 && lane == 0) E.prof[blockIdx.x * 8 + 5] = globaltimer_ns();
-    }
-    if (E.nrm_gamma && E.mode == RESID) {
-      // ---- fused RMSNorm of out once every tile is final (all CTAs are
-      // resident: the grid is at most one CTA per SM and each CTA's shared
-      // memory excludes a second)
-      if (warp == 2 && lane == 0) *ok_ptr = wait_counter_geq(E.nrm_cnt, W.Mt * ntu) ? 1 : 0;
-      epi_bar();
-      const bool ok = *ok_ptr != 0;
-      epi_bar();
-      if (!ok) {
-        if (warp == 2 && lane == 0) set_error(E.err, ARCB_ERR_TIMEOUT_DONE);
-      } else {
-        __threadfence();
-        const int t = threadIdx.x - 64;  // epilogue thread 0..127
-        const int d = E.ldo;
-        // 1 / rms per slot, in the (now idle) stage ring
-        int64_t* sinv = (int64_t*)(smem_raw + (a_base - raw));
-        for (int b = t; b < B; b += 128) sinv[b] = rms_inv((int64_t)__ldcg(E.ss_out + b), d);
-        epi_bar();
-        int need = 0;
-        const long long tot = (long long)B * d;
-        for (long long idx = (long long)blockIdx.x * 128 + t; idx < tot; idx += (long long)gridDim.x * 128) {
-          const int b = (int)(idx / d), j = (int)(idx - (long long)b * d);
-          const int64_t y = rms_apply(__ldcg(E.out + (size_t)b * E.ldo + j), sinv[b],
-                                      j < E.nrm_ngamma ? E.nrm_gamma[j] : ONE);
-          int8_t dg[8];
-          const int nl = limb_split8(y, dg);
-          need = nl > need ? nl : need;
-#pragma unroll
-          for (int l = 0; l < 8; ++l) E.nrm_X[limb_row(l, b, B) * d + j] = dg[l];
-        }
-        need = __reduce_max_sync(0xffffffffu, need);
-        if (lane == 0 && need > 0) atomicMax(E.nrm_lmax, need);
-      }
-      epi_bar();
-      if (warp == 2 && lane == 0) {
-        __threadfence();
-        if (atomicAdd(E.nrm_cnt + 1, 1) == (int)gridDim.x - 1) {
-          E.nrm_cnt[0] = 0;
-          E.nrm_cnt[1] = 0;
-          __threadfence();
-        }
-      }
     }
   }
   if (E.prof && threadIdx.x == 0) E.prof[blockIdx.x * 8 + 6] = globaltimer_ns();

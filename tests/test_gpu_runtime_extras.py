@@ -68,28 +68,3 @@ def test_build_engine_from_config():
     host = gen.random_model(preset("tiny"), 0)
     p = gen.seeded_prompt(8, host.cfg.vocab, 1)
     assert eng.generate(p, 6) == arcref.Model(host).generate(p, 6)
-
-
-@pytest.mark.parametrize("name", ["tiny", "micro_gqa"])
-def test_fused_norm_matches_oracle(name):
-    """RMSNorms folded into the residual GEMMs: same tokens as the oracle,
-    single stream (eager and graph) and continuous batching past 32 lanes."""
-    from arc_chain_b200.models import dense
-    from arc_chain_b200.runtime.engine import Engine
-    from arc_chain_b200.runtime.scheduler import Scheduler
-
-    host = gen.random_model(preset(name), 0)
-    oracle = arcref.Model(host)
-    eng = Engine(dense.from_host(host, "cuda"))
-    eng.fuse_norm = True
-    p = gen.seeded_prompt(20, host.cfg.vocab, 1)
-    want = oracle.generate(p, 10)
-    for g in (False, True):
-        assert eng.generate(p, 10, use_graph=g) == want
-    sch = Scheduler(eng, max_batch=40, prefill_chunk=32, gen_cap=10)
-    specs = [(gen.seeded_prompt(3 + (7 * i) % 23, host.cfg.vocab, 200 + i), 3 + i % 7) for i in range(40)]
-    rids = [sch.submit(q, n) for q, n in specs]
-    sch.run()
-    for rid, (q, n) in zip(rids, specs):
-        assert sch.requests[rid].tokens == oracle.generate(q, n)[0]
-    assert eng.check_errors() == 0

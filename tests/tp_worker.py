@@ -16,7 +16,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--comm", default="fused", choices=["nccl", "fused", "fused-logits", "fused-norm", "fused-rsag"])
+    ap.add_argument("--comm", default="fused", choices=["nccl", "fused", "fused-logits", "fused-rsag"])
     a = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -35,7 +35,7 @@ def main():
         from arc_chain_b200.parallel.fused import FusedComm
 
         # fused-rsag: the reduce-scatter + all-gather form at every batch size
-        comm = FusedComm(fuse_logits=a.comm in ("fused-logits", "fused-norm"),
+        comm = FusedComm(fuse_logits=a.comm == "fused-logits",
                          rs_ag="on" if a.comm == "fused-rsag" else "auto")
     cfg = preset("tiny")
     if cfg.n_heads % world:  # whole heads per rank: 8 heads of 64 for 8 ranks
@@ -45,7 +45,6 @@ def main():
     host = gen.random_model(cfg, 0)
     oracle = arcref.Model(host)
     eng = Engine(dense.from_host(host, "cuda", rank, world), comm=comm, n_pages=512, max_seq=256)
-    eng.fuse_norm = a.comm == "fused-norm"
     res = {"comm": a.comm, "world": world, "ok": True, "checks": 0}
     prompt = gen.seeded_prompt(32, cfg.vocab, 1)
     ref, rh = oracle.generate(prompt, 24)
