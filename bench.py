@@ -61,8 +61,8 @@ def main():
     ap.add_argument("--ep-layout", default="dispatch", choices=["dispatch", "replicated"],
                     help="moe workload, N > 1: token dispatch (each rank owns batch / N requests) or every "
                          "token on every rank")
-    ap.add_argument("--fuse-logits", type=int, default=0,
-                    help="with --comm fused: the LM head also all-gathers its logits in-kernel")
+    ap.add_argument("--fuse-logits", type=int, default=1,
+                    help="with --comm fused: 1 (default) the LM head all-gathers its logits in-kernel; 0 over NCCL")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", default="decode", choices=["decode", "batched", "moe", "specdec"],
                     help="decode: the headline 7B single-stream ms/token; batched: 70B-architecture continuous "

@@ -16,7 +16,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--comm", default="fused", choices=["nccl", "fused", "fused-logits", "fused-rsag"])
+    ap.add_argument("--comm", default="fused", choices=["nccl", "fused", "fused-nccl-logits", "fused-rsag"])
     a = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -35,7 +35,8 @@ def main():
         from arc_chain_b200.parallel.fused import FusedComm
 
         # fused-rsag: the reduce-scatter + all-gather form at every batch size
-        comm = FusedComm(fuse_logits=a.comm == "fused-logits",
+        # fused-nccl-logits: the fused reduce with the logits gathered over NCCL
+        comm = FusedComm(fuse_logits=a.comm != "fused-nccl-logits",
                          rs_ag="on" if a.comm == "fused-rsag" else "auto")
     cfg = preset("tiny")
     if cfg.n_heads % world:  # whole heads per rank: 8 heads of 64 for 8 ranks
