@@ -29,15 +29,17 @@
 // scores leave).
 //
 // Exact int32 fast path: a 64-bit wrapping multiply-add costs about five
-// integer instructions.  When a query row and a whole K page fit in int32,
-// every product fits exactly in int64, so one widening multiply-add per
-// element gives the identical wrapping sum.  For a V page that fits in int32
+// integer instructions.  When the query rows and the K elements a warp reads
+// fit in int32, every product fits exactly in int64, so one widening
+// multiply-add per element gives the identical wrapping sum.  For V values
+// that fit in int32
 // the value term runs in 32-bit arithmetic: with v = vh * 2^16 + vl (vh the
 // arithmetic high half, 0 <= vl < 2^16) and 0 <= w <= ONE = 2^16,
 //   (w * v) >> 16 = w * vh + ((w * vl) >> 16)      (w * vl < 2^32, unsigned)
 // and since the weights of one query sum to at most ONE, every partial sum of
 // w * vh lies in [-2^31, 2^31) and of ((w * vl) >> 16) in [0, 2^16]: both
-// int32 accumulators are exact.  Each page is checked when it lands.
+// int32 accumulators are exact.  Each warp checks the elements it reads and
+// takes the 64-bit form for them otherwise.
 #include "common.cuh"
 #include "lut.cuh"
 
@@ -52,20 +54,6 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
-}
-
-__device__ __forceinline__ uint64_t hsum16(uint64_t v) {  // over the 16 lanes of a half-warp
-#pragma unroll
-  for (int m = 8; m >= 1; m >>= 1) v += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
-  return v;
-}
-__device__ __forceinline__ int64_t hmax16(int64_t v) {
-#pragma unroll
-  for (int m = 8; m >= 1; m >>= 1) {
-    const int64_t o = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, m);
-    v = o > v ? o : v;
-  }
-  return v;
 }
 
 template <int QB, int DH, int MODE, int WM>
