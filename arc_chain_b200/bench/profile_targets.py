@@ -115,10 +115,16 @@ def _timed(fn, warm: int, iters: int, extra: dict) -> None:
 
 
 def mla_attn():
+    """MLA latent attention (DeepSeek-V2-Lite, 16 heads, T = 512); B and the
+    cluster size from ARCB_PT_B / ARCB_PT_CS (default 32 slots, heuristic)."""
+    import os
+
     from arc_chain_b200.ops import int_ops as ops
 
     dev = torch.device("cuda")
-    H, r, dr, T, B = 16, 512, 64, 512, 32
+    H, r, dr, T = 16, 512, 64, 512
+    B = int(os.environ.get("ARCB_PT_B", "32"))
+    cs = int(os.environ.get("ARCB_PT_CS", "0")) or None
     dk = r + dr
     pages = (T + 15) // 16
     cache = torch.randint(-(1 << 18), 1 << 18, (B * pages, 1, 16, dk), dtype=torch.int64, device=dev)
@@ -127,9 +133,9 @@ def mla_attn():
     pt = torch.arange(B * pages, dtype=torch.int32, device=dev).view(B, pages)
     pos = torch.full((B,), T - 1, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    _timed(lambda: ops.attn_mla(Q, cache, pt, pos, H, dk, r, 5793, T, B, oc, err), 3, 10,
+    _timed(lambda: ops.attn_mla(Q, cache, pt, pos, H, dk, r, 5793, T, B, oc, err, cluster=cs), 3, 10,
            {"kernel": "attn_mla (k_attn_cluster)", "heads": H, "dk": dk, "dv": r, "T": T, "B": B,
-            "bytes": B * T * dk * 8})
+            "cluster": cs or ops.attn_cluster_size(B, H), "bytes": B * T * dk * 8})
     assert int(err.item()) == 0
 
 
