@@ -31,3 +31,32 @@ def test_scheduler_refuses_token_dispatch():
 
     with pytest.raises(ValueError, match="replicated-token"):
         Scheduler(Eng())
+
+
+@pytest.mark.parametrize("N,B", [(2, 1), (2, 16), (4, 8), (8, 4), (8, 16)])
+def test_token_dispatch_layout(N, B):
+    """The expert-parallel dispatch places row limb_row(l, b, B) of rank r's
+    limb planes at row limb_row(l, r * B + b, N * B) of every gathered
+    buffer (csrc/kernels/ep_ops.cu: k_ep_dispatch).  Assembled that way, the
+    gathered buffer is exactly the limb operand of all N * B slots, and the
+    combine's owner of gathered slot g (g // B, row g % B) is the rank that
+    sent it."""
+    import numpy as np
+
+    from arc_chain_b200.ops import int_ops as ops
+
+    rng = np.random.default_rng(N * 100 + B)
+    K = 64
+    xs = [rng.integers(-(1 << 40), 1 << 40, size=(B, K), dtype=np.int64) for _ in range(N)]
+    NB = N * B
+    want, _ = ops.limb_planes(np.concatenate(xs), ops.limb_rows(NB))
+    got = np.zeros_like(want)
+    for r, x in enumerate(xs):
+        local, _ = ops.limb_planes(x, ops.limb_rows(B))
+        for l in range(8):
+            for b in range(B):
+                got[ops.limb_row(l, r * B + b, NB)] = local[ops.limb_row(l, b, B)]
+    np.testing.assert_array_equal(got, want)
+    for g in range(NB):
+        owner, row = g // B, g % B
+        assert owner * B + row == g and np.array_equal(xs[owner][row], np.concatenate(xs)[g])
