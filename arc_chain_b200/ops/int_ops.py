@@ -417,11 +417,10 @@ def split_ctas(M: int, B: int, bn: int) -> int:
     return max(1, mt * n_tiles(B) * splits)
 
 
-def linear_gemm(lin, xmap: TensorMap, B: int, lmax, P, tile_cnt, epi: Epi, max_ctas: int = 0) -> None:
-    """Dispatch a Linear (int8 tiles or Q4 tiles) to its fused GEMM.
-    max_ctas > 0 overrides the persistent-CTA heuristic."""
+def linear_gemm(lin, xmap: TensorMap, B: int, lmax, P, tile_cnt, epi: Epi) -> None:
+    """Dispatch a Linear (int8 tiles or Q4 tiles) to its fused GEMM."""
     if not epi.peer_sig:  # expert-parallel arrival counts assume the full grid
-        epi.max_ctas = min(num_sms(), max_ctas or split_ctas(lin.M, B, xmap.box_rows))
+        epi.max_ctas = min(num_sms(), split_ctas(lin.M, B, xmap.box_rows))
     if getattr(lin, "q4", None) is not None:
         fgemm_q4(lin.q4, xmap, lin.M, lin.K, B, lmax, P, tile_cnt, epi)
     else:

@@ -102,10 +102,6 @@ class FusedComm(NcclComm):
         # (each rank sends 2 (N - 1) / N of the output instead of N - 1 times
         # it, for one more NVLink hop); "on" / "off" force it
         self.rs_ag = os.environ.get("ARCB_RS_AG", rs_ag)
-        # persistent CTAs of the reduce GEMMs (0: the shared heuristic); one
-        # CTA per 128-row tile makes every tile direct (no split-K partials
-        # before the push)
-        self.rp_ctas = int(os.environ.get("ARCB_RP_CTAS", "0"))
         self.group_name = (group or dist.group.WORLD).group_name
         self._sites = {}
         self._epis = {}
@@ -176,7 +172,4 @@ class FusedComm(NcclComm):
             self._epis[key] = (e, epi)  # keep the source alive: its id is the key
         else:
             e = e[0]
-        ctas = self.rp_ctas if self.rp_ctas > 0 else 0
-        if self.rp_ctas < 0:  # -1: one CTA per 128-row tile
-            ctas = (lin.M + ops.BM - 1) // ops.BM * ops.n_tiles(B)
-        ops.linear_gemm(lin, xmap, B, lmax, s.P, bb.tiles, e, max_ctas=ctas)
+        ops.linear_gemm(lin, xmap, B, lmax, s.P, bb.tiles, e)
