@@ -23,10 +23,6 @@ _SIGS = {
     "arcb_norm_limbs": (i32, [vp, vp, vp, i32, i32, i32, vp, vp, vp, vp]),
     "arcb_rmsnorm_limbs": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, vp]),
     "arcb_finalize": (i32, [vp, i32, i32, vp, vp, vp, i32, i32, vp, vp]),
-    "arcb_finalize_qkv": (i32, [vp, i32, vp, vp, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp, vp, i32, vp, vp]),
-    "arcb_finalize_swiglu": (i32, [vp, i32, i32, vp, vp, vp, vp, vp, vp]),
-    "arcb_attn_decode": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, i32, i64, i32, i32, i32, vp, vp, vp, vp, vp, vp,
-                               vp, vp, vp]),
     "arcb_sample": (i32, [vp, i32, i32, vp, i32, vp, vp, vp, i32, vp, vp, vp, vp, i32, vp]),
     "arcb_rng_i8": (i32, [u64, u64, vp, i64, vp]),
     "arcb_attn_cluster": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, i32, i64, i32, i32, i32, vp, vp, vp, vp, vp]),

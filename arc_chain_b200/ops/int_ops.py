@@ -55,14 +55,6 @@ def gemm_bn(B: int) -> int:
     return lib().arcb_gemm_bn(B)
 
 
-def _stages(bn: int) -> int:
-    return 4 if bn >= 256 else (6 if bn >= 128 else 8)
-
-
-def gemm_smem(bn: int) -> int:
-    return 1024 + _stages(bn) * (BM * BK + bn * BK) + (2 * _stages(bn) + 2) * 8 + 16
-
-
 _SMS = [None]
 
 
@@ -70,23 +62,6 @@ def num_sms() -> int:
     if _SMS[0] is None:
         _SMS[0] = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     return _SMS[0]
-
-
-def choose_ksplit(M: int, K: int, bn: int, n_tiles: int = 1) -> int:
-    """Split-K factor minimising (waves x chunks per CTA) over the SMs."""
-    mt = (M + BM - 1) // BM * n_tiles
-    nch = (K + BK - 1) // BK
-    occ = max(1, (232448 - 1024) // (gemm_smem(bn) + 1024))
-    slots = num_sms() * occ
-    best, best_t = 1, None
-    for ks in range(1, nch + 1):
-        cps = (nch + ks - 1) // ks
-        ks_eff = (nch + cps - 1) // cps
-        waves = (mt * ks_eff + slots - 1) // slots
-        t = waves * (cps + 1.5)  # +1.5 chunks of fixed per-CTA cost
-        if best_t is None or t < best_t - 1e-9:
-            best, best_t = ks_eff, t
-    return best
 
 
 def gemm_i8(wmap: TensorMap, xmap: TensorMap, M: int, K: int, B: int, ksplit: int, lmax: torch.Tensor,
@@ -119,46 +94,6 @@ def rmsnorm_limbs(h, gamma, d, B, X, lmax, y_out=None):
 def finalize(P, M, B, lmax, scales, out, ldo, mode, ss_out=None):
     _count()
     check(lib().arcb_finalize(_p(P), M, B, _p(lmax), _p(scales), _p(out), ldo, mode, _p(ss_out), _s()), "finalize")
-
-
-def finalize_qkv(P, B, lmax, scales, n_heads, n_kv, dh, q_out, Kc, Vc, pt, pos, rcos, rsin, max_seq, err):
-    _count()
-    check(lib().arcb_finalize_qkv(_p(P), B, _p(lmax), _p(scales), n_heads, n_kv, dh, _p(q_out), _p(Kc), _p(Vc),
-                                  _p(pt), pt.shape[1], _p(pos), _p(rcos), _p(rsin), max_seq, _p(err), _s()),
-          "finalize_qkv")
-
-
-def finalize_swiglu(P, dff, B, lmax, scales, X, lmax_out, y_out=None):
-    _count()
-    check(lib().arcb_finalize_swiglu(_p(P), dff, B, _p(lmax), _p(scales), _p(X), _p(lmax_out), _p(y_out), _s()),
-          "finalize_swiglu")
-
-
-class AttnScratch:
-    """Scratch of the split-KV attention for B slots x n_heads heads."""
-
-    def __init__(self, B, n_heads, dh, max_T, device):
-        self.S = torch.zeros(B * n_heads * max_T, dtype=torch.int64, device=device)
-        self.Mx = torch.full((B * n_heads,), -(1 << 63), dtype=torch.int64, device=device)
-        self.O = torch.zeros(B * n_heads * dh, dtype=torch.int64, device=device)
-        self.cnt = torch.zeros(B * n_heads, dtype=torch.int32, device=device)
-        self.chunk = attn_chunk(B, n_heads, max_T)
-
-
-def attn_chunk(B, n_heads, max_T) -> int:
-    c = -(-max_T * n_heads * B // (4 * 148))
-    c = (c + 15) // 16 * 16
-    return max(16, min(512, c))
-
-
-def attn_decode(q, Kc, Vc, pt, pos, n_heads, n_kv, dh, attn_scale, B, X, lmax, max_T, scratch, err, o_out=None):
-    """Two launches (scores+max, exp-sum+PV+limbs)."""
-    LAUNCHES[0] += 2
-    sc = scratch
-    check(lib().arcb_attn_decode(_p(q), _p(Kc), _p(Vc), _p(pt), pt.shape[1], _p(pos), n_heads, n_kv, dh,
-                                 int(attn_scale), B, sc.chunk, max_T, _p(sc.S), _p(sc.Mx), _p(sc.O), _p(sc.cnt),
-                                 _p(X), _p(lmax), _p(o_out), _p(err), _s()),
-          "attn_decode")
 
 
 def sample(logits, V, n, hist, count, gen, tokens_next, pos_inc=None, done=None, eos=None, lrow=None):
@@ -334,17 +269,6 @@ def q4_group_quantize(w: torch.Tensor):
     m = ((am + 6) // 7).clamp(1, 15)
     q = torch.div(g, m.unsqueeze(-1), rounding_mode="trunc").clamp(-8, 7).view(M, ng * 32)[:, :K]
     return q.to(torch.int8), m.to(torch.uint8)
-
-
-def q4_row_quantize(w: torch.Tensor, s: torch.Tensor):
-    """The reference's per-row Q4 (Q4WeightsX86::from_i8,
-    cached_integer_model.rs:670-701): qpu = max(1, ceil(absmax_row / 7)),
-    q = clamp(trunc(w / qpu), -8, 7), row scale s * qpu; group multipliers 1."""
-    am = w.to(torch.int32).abs().amax(-1).clamp(min=1)
-    qpu = ((am + 6) // 7).clamp(min=1)
-    q = torch.div(w.to(torch.int32), qpu.unsqueeze(-1), rounding_mode="trunc").clamp(-8, 7).to(torch.int8)
-    mult = torch.ones(w.shape[0], (w.shape[1] + 31) // 32, dtype=torch.uint8, device=w.device)
-    return q, mult, s * qpu.to(torch.int64)
 
 
 def fgemm_q4(packed: torch.Tensor, xmap: TensorMap, M: int, K: int, B: int, lmax, P, tile_cnt, epi: Epi,

@@ -31,20 +31,9 @@ using namespace q16;
 
 namespace {
 
-constexpr int PAGE = 16;
-
 __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) v += (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
-  return v;
-}
-
-__device__ __forceinline__ int64_t warp_max_i64(int64_t v) {
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) {
-    int64_t o = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, m);
-    v = o > v ? o : v;
-  }
   return v;
 }
 
@@ -82,22 +71,6 @@ __device__ __forceinline__ uint64_t block_sum_u64(uint64_t v, uint64_t* sh) {
   return r;
 }
 
-__device__ __forceinline__ int64_t block_max_i64(int64_t v, int64_t* sh) {
-  v = warp_max_i64(v);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) sh[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    int64_t x = l < (int)(blockDim.x >> 5) ? sh[l] : INT64_MIN;
-    x = warp_max_i64(x);
-    if (l == 0) sh[0] = x;
-  }
-  __syncthreads();
-  int64_t r = sh[0];
-  __syncthreads();
-  return r;
-}
 
 // Limb digits of v (slot b, column j of a [rows, ld] limb operand of B slots).
 __device__ __forceinline__ void store_limbs(int8_t* X, int B, int ld, int b, int j, int64_t v, int& need) {
@@ -224,219 +197,6 @@ __global__ void k_finalize(int* __restrict__ P, int M, int B, const int* __restr
   if (ss_out) {
     acc = block_sum_u64(acc, sh);
     if (threadIdx.x == 0) atomicAdd((unsigned long long*)(ss_out + b), (unsigned long long)acc);
-  }
-}
-
-// QKV finalize + RoPE on q and k heads + paged KV append (1418-1444).
-// Rows of the fused weight: [0, d) q, [d, d + dkv) k, [d + dkv, d + 2dkv) v.
-__global__ void k_finalize_qkv(int* __restrict__ P, int B, const int* __restrict__ lmax,
-                               const int64_t* __restrict__ scales, int n_heads, int n_kv, int dh,
-                               int64_t* __restrict__ q_out, int64_t* __restrict__ Kc,
-                               int64_t* __restrict__ Vc, const int* __restrict__ pt, int pt_stride,
-                               const int* __restrict__ pos, const int64_t* __restrict__ rcos,
-                               const int64_t* __restrict__ rsin, int max_seq, int* __restrict__ err) {
-  pdl_wait_dep();
-  pdl_allow_next();
-  const int b = blockIdx.y;
-  const int half = dh / 2;
-  const int d = n_heads * dh, dkv = n_kv * dh;
-  const int M = d + 2 * dkv;
-  const int nq = d / 2, nk = dkv / 2;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= nq + nk + dkv) return;
-  const int L = *lmax;
-  const int p = pos[b];
-  if (p < 0 || p >= max_seq) {
-    set_error(err, ARCB_ERR_SEQ_OVERFLOW);
-    return;
-  }
-  const int page = pt[(size_t)b * pt_stride + p / PAGE];
-  const int slot = p % PAGE;
-  if (i < nq + nk) {
-    const bool is_q = i < nq;
-    const int ii = is_q ? i : i - nq;
-    const int head = ii / half, e = ii % half;
-    const int r0 = (is_q ? 0 : d) + head * dh + e, r1 = r0 + half;
-    int64_t x0 = fin_elem(P, M, B, L, b, r0, scales[r0]);
-    int64_t x1 = fin_elem(P, M, B, L, b, r1, scales[r1]);
-    rope_pair(x0, x1, rcos[(size_t)p * half + e], rsin[(size_t)p * half + e]);
-    if (is_q) {
-      q_out[(size_t)b * d + head * dh + e] = x0;
-      q_out[(size_t)b * d + head * dh + e + half] = x1;
-    } else {
-      int64_t* kr = Kc + (((size_t)page * n_kv + head) * PAGE + slot) * dh;
-      kr[e] = x0;
-      kr[e + half] = x1;
-    }
-  } else {
-    const int j = i - nq - nk;
-    const int r = d + dkv + j;
-    const int64_t v = fin_elem(P, M, B, L, b, r, scales[r]);
-    const int head = j / dh, e = j % dh;
-    Vc[(((size_t)page * n_kv + head) * PAGE + slot) * dh + e] = v;
-  }
-}
-
-// gate/up finalize + SwiGLU + limb split for W_down (1496-1498).
-// Rows: [0, dff) gate, [dff, 2dff) up.
-__global__ void k_finalize_swiglu(int* __restrict__ P, int dff, int B, const int* __restrict__ lmax,
-                                  const int64_t* __restrict__ scales, int8_t* __restrict__ X,
-                                  int* __restrict__ lmax_out, int64_t* __restrict__ y_out) {
-  pdl_wait_dep();
-  pdl_allow_next();
-  __shared__ int shi[32];
-  const int b = blockIdx.y;
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  const int M = 2 * dff;
-  int need = 0;
-  if (j < dff) {
-    const int L = *lmax;
-    const int64_t g = fin_elem(P, M, B, L, b, j, scales[j]);
-    const int64_t u = fin_elem(P, M, B, L, b, dff + j, scales[dff + j]);
-    const int64_t y = swiglu(g, u, g_exp_lut.v);
-    if (y_out) y_out[(size_t)b * dff + j] = y;
-    store_limbs(X, B, dff, b, j, y, need);
-  }
-  need = block_max_int(need, shi);
-  if (threadIdx.x == 0) atomicMax(lmax_out, need);
-}
-
-// ------------------------------------------------------------------ attention
-// Exact split-KV decode attention (1448-1476).  softmax_i64 needs the exact
-// global max and the exact global sum, and rounding happens per term, so
-// there is no online rescaling: the keys of one (slot, head) are split over
-// CTAs in three exact integer phases:
-//   A (k_attn_scores): scores s_j = ((q.k_j >> 16) * scale) >> 16 with
-//      wrapping i64 dots -> scratch S, and an atomicMax into Mx;
-//   B (k_attn_pv): every CTA recomputes e_j = exp(s_j - max) over all j and
-//      their sum (integer, order free), then for its own keys
-//      w_j = e_j * ONE / sum and sum_j (w_j * v_j) >> 16 -> u64 atomicAdd into
-//      O; the last CTA of the (slot, head) turns O into limb planes for W_o
-//      and resets O, Mx and its counter.
-// grid = (n_heads, B, n_split); split s covers keys [s*chunk, (s+1)*chunk).
-__global__ void k_attn_scores(const int64_t* __restrict__ q, const int64_t* __restrict__ Kc,
-                              const int* __restrict__ pt, int pt_stride, const int* __restrict__ pos,
-                              int n_heads, int n_kv, int dh, int64_t attn_scale, int chunk, int max_T,
-                              int64_t* __restrict__ S, long long* __restrict__ Mx, int* __restrict__ err) {
-  pdl_wait_dep();
-  pdl_allow_next();
-  __shared__ int64_t qs[256];
-  __shared__ int64_t shm[32];
-  const int hq = blockIdx.x, b = blockIdx.y;
-  const int T = pos[b] + 1;
-  const int j0 = blockIdx.z * chunk;
-  if (T > max_T || T < 1) {
-    if (threadIdx.x == 0 && blockIdx.z == 0) set_error(err, ARCB_ERR_SEQ_OVERFLOW);
-    return;
-  }
-  if (j0 >= T) return;
-  const int j1 = min(T, j0 + chunk);
-  const int kvh = hq * n_kv / n_heads;
-  const int d = n_heads * dh;
-  for (int e = threadIdx.x; e < dh; e += blockDim.x) qs[e] = q[(size_t)b * d + hq * dh + e];
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const int* ptb = pt + (size_t)b * pt_stride;
-  int64_t* Sbh = S + ((size_t)b * n_heads + hq) * max_T;
-  int64_t mx = INT64_MIN;
-  // two keys per warp iteration for memory-level parallelism
-  for (int j = j0 + warp; j < j1; j += 2 * nw) {
-    const int ja = j, jb = j + nw;
-    const int64_t* ka = Kc + (((size_t)ptb[ja / PAGE] * n_kv + kvh) * PAGE + (ja % PAGE)) * dh;
-    const int64_t* kb = jb < j1 ? Kc + (((size_t)ptb[jb / PAGE] * n_kv + kvh) * PAGE + (jb % PAGE)) * dh : ka;
-    uint64_t aa = 0, ab = 0;
-#pragma unroll 4
-    for (int e = lane; e < dh; e += 32) {
-      const uint64_t qe = (uint64_t)qs[e];
-      aa += qe * (uint64_t)__ldg(ka + e);
-      ab += qe * (uint64_t)__ldg(kb + e);
-    }
-    aa = warp_sum_u64(aa);
-    ab = warp_sum_u64(ab);
-    const int64_t sa = attn_score((int64_t)aa, attn_scale);
-    const int64_t sb = attn_score((int64_t)ab, attn_scale);
-    if (lane == 0) {
-      Sbh[ja] = sa;
-      if (jb < j1) Sbh[jb] = sb;
-    }
-    mx = sa > mx ? sa : mx;
-    if (jb < j1) mx = sb > mx ? sb : mx;
-  }
-  mx = block_max_i64(mx, shm);
-  if (threadIdx.x == 0) atomicMax(Mx + (size_t)b * n_heads + hq, (long long)mx);
-}
-
-__global__ void k_attn_pv(const int64_t* __restrict__ Vc, const int* __restrict__ pt, int pt_stride,
-                          const int* __restrict__ pos, int n_heads, int n_kv, int dh, int chunk, int max_T,
-                          const int64_t* __restrict__ S, long long* __restrict__ Mx,
-                          unsigned long long* __restrict__ O, int* __restrict__ cnt, int B,
-                          int8_t* __restrict__ X, int* __restrict__ lmax, int64_t* __restrict__ o_out) {
-  pdl_wait_dep();
-  pdl_allow_next();
-  __shared__ int64_t lut[EXP_LUT_N];
-  __shared__ int64_t wsh[512];
-  __shared__ uint64_t shu[32];
-  __shared__ int shi[32];
-  __shared__ int last_s;
-  const int hq = blockIdx.x, b = blockIdx.y;
-  const int T = pos[b] + 1;
-  const int j0 = blockIdx.z * chunk;
-  if (T > max_T || T < 1 || j0 >= T) return;
-  const int j1 = min(T, j0 + chunk);
-  const int n_split_used = (T + chunk - 1) / chunk;
-  const int kvh = hq * n_kv / n_heads;
-  const int d = n_heads * dh;
-  const size_t bh = (size_t)b * n_heads + hq;
-  const int64_t* Sbh = S + bh * max_T;
-  for (int i = threadIdx.x; i < EXP_LUT_N; i += blockDim.x) lut[i] = g_exp_lut.v[i];
-  __syncthreads();
-  const int64_t mx = (int64_t)Mx[bh];
-  // global sum of exps (every CTA computes the same exact integer)
-  uint64_t sum = 0;
-  for (int j = threadIdx.x; j < T; j += blockDim.x) sum += (uint64_t)integer_exp(wsub(Sbh[j], mx), lut);
-  const int64_t s = (int64_t)block_sum_u64(sum, shu);
-  // weights of this CTA's keys
-  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
-    int64_t w;
-    if (T == 1) w = ONE;
-    else if (s == 0) w = ONE / T;
-    else w = udiv_small(wmul(integer_exp(wsub(Sbh[j], mx), lut), ONE), s);
-    wsh[j - j0] = w;
-  }
-  __syncthreads();
-  const int* ptb = pt + (size_t)b * pt_stride;
-  for (int e = threadIdx.x; e < dh; e += blockDim.x) {
-    uint64_t o = 0;
-#pragma unroll 8
-    for (int j = j0; j < j1; ++j) {
-      const int64_t v = __ldg(Vc + (((size_t)ptb[j / PAGE] * n_kv + kvh) * PAGE + (j % PAGE)) * dh + e);
-      o += (uint64_t)mulshr(wsh[j - j0], v);
-    }
-    if (n_split_used == 1) {
-      O[bh * dh + e] = o;  // sole contributor
-    } else {
-      atomicAdd(O + bh * dh + e, (unsigned long long)o);
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last_s = (n_split_used == 1) || (atomicAdd(cnt + bh, 1) == n_split_used - 1);
-  __syncthreads();
-  if (!last_s) return;
-  __threadfence();
-  int need = 0;
-  for (int e = threadIdx.x; e < dh; e += blockDim.x) {
-    const int64_t o = (int64_t)__ldcg(O + bh * dh + e);
-    O[bh * dh + e] = 0;
-    const size_t off = (size_t)b * d + hq * dh + e;
-    if (o_out) o_out[off] = o;
-    if (X) store_limbs(X, B, d, b, hq * dh + e, o, need);
-  }
-  need = block_max_int(need, shi);
-  if (threadIdx.x == 0) {
-    cnt[bh] = 0;
-    Mx[bh] = LLONG_MIN;
-    if (lmax) atomicMax(lmax, need);
   }
 }
 
@@ -603,37 +363,6 @@ int arcb_finalize(int* P, int M, int B, const int* lmax, const int64_t* scales, 
                   uint64_t* ss_out, void* st) {
   dim3 g((M + 255) / 256, B);
   return launch_k(k_finalize, dim3(g), dim3(256), 0, S_(st), P, M, B, lmax, scales, out, ldo, mode, ss_out);
-}
-
-int arcb_finalize_qkv(int* P, int B, const int* lmax, const int64_t* scales, int n_heads, int n_kv, int dh,
-                      int64_t* q_out, int64_t* Kc, int64_t* Vc, const int* pt, int pt_stride, const int* pos,
-                      const int64_t* rcos, const int64_t* rsin, int max_seq, int* err, void* st) {
-  const int d = n_heads * dh, dkv = n_kv * dh;
-  const int n = d / 2 + dkv / 2 + dkv;
-  dim3 g((n + 127) / 128, B);
-  return launch_k(k_finalize_qkv, dim3(g), dim3(128), 0, S_(st), P, B, lmax, scales, n_heads, n_kv, dh, q_out, Kc, Vc, pt, pt_stride, pos,
-                                         rcos, rsin, max_seq, err);
-}
-
-int arcb_finalize_swiglu(int* P, int dff, int B, const int* lmax, const int64_t* scales, int8_t* X,
-                         int* lmax_out, int64_t* y_out, void* st) {
-  dim3 g((dff + 255) / 256, B);
-  return launch_k(k_finalize_swiglu, dim3(g), dim3(256), 0, S_(st), P, dff, B, lmax, scales, X, lmax_out, y_out);
-}
-
-// Attention scratch: S [B, n_heads, max_T] i64, Mx [B, n_heads] (init
-// LLONG_MIN), O [B, n_heads, dh] u64 (init 0), cnt [B, n_heads] (init 0).
-int arcb_attn_decode(const int64_t* q, const int64_t* Kc, const int64_t* Vc, const int* pt, int pt_stride,
-                     const int* pos, int n_heads, int n_kv, int dh, int64_t attn_scale, int B, int chunk, int max_T,
-                     int64_t* S, long long* Mx, unsigned long long* O, int* cnt, int8_t* X, int* lmax,
-                     int64_t* o_out, int* err, void* st) {
-  if (dh > 256 || chunk > 512 || chunk < 1) return -1;
-  const int nsplit = (max_T + chunk - 1) / chunk;
-  dim3 g(n_heads, B, nsplit);
-  int rc = launch_k(k_attn_scores, g, dim3(128), 0, S_(st), q, Kc, pt, pt_stride, pos, n_heads, n_kv, dh, attn_scale, chunk, max_T, S,
-                                        Mx, err);
-  return launch_k(k_attn_pv, dim3(g), dim3(128), 0, S_(st), Vc, pt, pt_stride, pos, n_heads, n_kv, dh, chunk, max_T, S, Mx, O, cnt, B, X,
-                                    lmax, o_out);
 }
 
 int arcb_sample(int64_t* logits, int ldl, int V, const int* lrow, int S, int* hist, int* count, int* gen,
